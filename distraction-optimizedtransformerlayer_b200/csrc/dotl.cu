@@ -1,0 +1,423 @@
+// libdotl: host side of the C ABI declared in include/dotl.h.
+//
+// One translation unit: the kernel headers are included here so the device
+// error word has a single definition and nvcc sees every launcher with its
+// kernel. Argument checks mirror the reference's TORCH_CHECKs
+// (attention_dispatch.cuh:351-369, linear_gelu.cuh:606-625,
+// add_layernorm.cuh:500-552): a rejected call returns a code and a message
+// and enqueues nothing. Nothing here allocates device memory.
+
+#include "../../include/dotl.h"
+#include "attention.cuh"
+#include "gemm.cuh"
+#include "layernorm.cuh"
+
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int check_launch(const char* who) {
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(DOTL_ECUDA, "%s: kernel launch failed: %s", who, cudaGetErrorString(e));
+    return DOTL_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int current_device(int* dev) {
+    const cudaError_t e = cudaGetDevice(dev);
+    if (e != cudaSuccess) return fail(DOTL_ECUDA, "cudaGetDevice failed: %s", cudaGetErrorString(e));
+    return DOTL_OK;
+}
+
+constexpr int kMaxDevices = 64;
+
+int sm_count(int dev) {
+    static int counts[kMaxDevices] = {0};
+    if (dev < 0 || dev >= kMaxDevices) return 148;
+    if (counts[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        counts[dev] = n;
+    }
+    return counts[dev];
+}
+
+// Raises a kernel's dynamic shared memory limit, once per device.
+template <typename Kernel>
+int ensure_smem(Kernel kernel, uint32_t bytes, int dev, bool* done_flags) {
+    if (dev >= 0 && dev < kMaxDevices && done_flags[dev]) return DOTL_OK;
+    const cudaError_t e =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+    if (e != cudaSuccess)
+        return fail(DOTL_ECUDA, "cudaFuncSetAttribute(%u bytes of shared memory) failed: %s", bytes,
+                    cudaGetErrorString(e));
+    if (dev >= 0 && dev < kMaxDevices) done_flags[dev] = true;
+    return DOTL_OK;
+}
+
+// ------------------------------------------------------------ tensor maps --
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// fp16 tensor map of rank 2 or 4 with a 128-row box (box_rows) and
+// box_cols fp16 columns, swizzled to the box row width.
+int encode_f16_map(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims,
+                   const cuuint64_t* strides_bytes, uint32_t box_cols, uint32_t box_rows, const char* who) {
+    EncodeTiledFn fn = encode_fn();
+    if (fn == nullptr) return fail(DOTL_ECUDA, "%s: cuTensorMapEncodeTiled is unavailable from the driver", who);
+    cuuint32_t box[4] = {box_cols, box_rows, 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUtensorMapSwizzle swz = box_cols * 2 == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                   : box_cols * 2 == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                        : CU_TENSOR_MAP_SWIZZLE_32B;
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, static_cast<cuuint32_t>(rank),
+                          const_cast<void*>(base), dims, strides_bytes, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(DOTL_ECUDA, "%s: cuTensorMapEncodeTiled failed (CUresult %d)", who, (int)r);
+    return DOTL_OK;
+}
+
+// ------------------------------------------------------------------ GEMM --
+
+template <int BN, int STAGES, bool OUT_F16>
+int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const dotl::GemmParams& p, int dev,
+                cudaStream_t stream) {
+    using L = dotl::GemmSmem<BN, STAGES>;
+    auto kernel = dotl::gemm_tc_kernel<BN, STAGES, OUT_F16>;
+    static bool done[kMaxDevices] = {false};
+    if (int rc = ensure_smem(kernel, L::kAlloc, dev, done)) return rc;
+    const int tiles = p.num_m_tiles * p.num_n_tiles;
+    const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
+    kernel<<<grid, dotl::kGemmThreads, L::kAlloc, stream>>>(ta, tw, p);
+    return check_launch("dotl_linear");
+}
+
+// ------------------------------------------------------------- attention --
+
+template <int HD, int STAGES>
+int launch_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const dotl::AttnParams& p,
+                int dev, cudaStream_t stream) {
+    using L = dotl::AttnSmem<HD, STAGES>;
+    auto kernel = dotl::attn_tc_kernel<HD, STAGES>;
+    static bool done[kMaxDevices] = {false};
+    if (int rc = ensure_smem(kernel, L::kAlloc, dev, done)) return rc;
+    const int items = p.num_streams * p.num_q_tiles;
+    const int grid = items < sm_count(dev) ? items : sm_count(dev);
+    kernel<<<grid, dotl::kAttnThreads, L::kAlloc, stream>>>(tq, tk, tv, p);
+    return check_launch("dotl_attention");
+}
+
+}  // namespace
+
+extern "C" {
+
+int dotl_abi_version(void) { return DOTL_ABI_VERSION; }
+
+const char* dotl_last_error(void) { return g_last_error.c_str(); }
+
+int dotl_num_sms(int* out) {
+    if (out == nullptr) return fail(DOTL_EINVAL, "dotl_num_sms: out is NULL");
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    *out = sm_count(dev);
+    return DOTL_OK;
+}
+
+int dotl_device_error(int clear, unsigned int* word) {
+    unsigned int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, dotl::g_dotl_dev_error, sizeof(v));
+    if (e != cudaSuccess) return fail(DOTL_ECUDA, "dotl_device_error: %s", cudaGetErrorString(e));
+    if (clear) {
+        const unsigned int zero = 0;
+        e = cudaMemcpyToSymbol(dotl::g_dotl_dev_error, &zero, sizeof(zero));
+        if (e != cudaSuccess) return fail(DOTL_ECUDA, "dotl_device_error: %s", cudaGetErrorString(e));
+    }
+    if (word != nullptr) *word = v;
+    return DOTL_OK;
+}
+
+int dotl_identity_f32(const float* in, float* out, int64_t n, void* stream) {
+    if (n < 0) return fail(DOTL_EINVAL, "smoke_test_identity: negative size");
+    if (n == 0) return DOTL_OK;
+    if (in == nullptr || out == nullptr) return fail(DOTL_EINVAL, "smoke_test_identity: NULL pointer");
+    const int threads = 256;
+    const int64_t blocks = (n + threads - 1) / threads;
+    dotl::identity_f32_kernel<<<static_cast<unsigned>(blocks), threads, 0, static_cast<cudaStream_t>(stream)>>>(
+        in, out, n);
+    return check_launch("smoke_test_identity");
+}
+
+int dotl_cast_f32_f16(const float* in, void* out, int64_t n, void* stream) {
+    if (n < 0) return fail(DOTL_EINVAL, "dotl_cast_f32_f16: negative size");
+    if (n == 0) return DOTL_OK;
+    if (in == nullptr || out == nullptr) return fail(DOTL_EINVAL, "dotl_cast_f32_f16: NULL pointer");
+    if (!aligned16(in) || !aligned16(out))
+        return fail(DOTL_EINVAL, "dotl_cast_f32_f16: pointers must be 16-byte aligned");
+    const int threads = 256;
+    const int64_t blocks = ((n + 3) / 4 + threads - 1) / threads;
+    dotl::cast_f32_f16_kernel<<<static_cast<unsigned>(blocks), threads, 0, static_cast<cudaStream_t>(stream)>>>(
+        in, static_cast<__half*>(out), n);
+    return check_launch("dotl_cast_f32_f16");
+}
+
+int dotl_cast_f16_f32(const void* in, float* out, int64_t n, void* stream) {
+    if (n < 0) return fail(DOTL_EINVAL, "dotl_cast_f16_f32: negative size");
+    if (n == 0) return DOTL_OK;
+    if (in == nullptr || out == nullptr) return fail(DOTL_EINVAL, "dotl_cast_f16_f32: NULL pointer");
+    const int threads = 256;
+    const int64_t blocks = (n + threads - 1) / threads;
+    dotl::cast_f16_f32_kernel<<<static_cast<unsigned>(blocks), threads, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const __half*>(in), out, n);
+    return check_launch("dotl_cast_f16_f32");
+}
+
+int dotl_layernorm(const float* x, const float* sub, const float* weight, const float* bias, float* x_new,
+                   void* normed, int normed_dtype, const uint8_t* row_valid, int64_t rows, int64_t D, float eps,
+                   void* stream) {
+    const char* who = sub ? "fused_add_layernorm" : "fused_layernorm";
+    if (rows < 0 || D <= 0) return fail(DOTL_EINVAL, "%s: bad shape rows=%lld D=%lld", who, (long long)rows, (long long)D);
+    if (D > 2048) return fail(DOTL_EUNSUPPORTED, "%s: last dimension %lld is over the 2048 this kernel holds in registers", who, (long long)D);
+    if (normed_dtype != DOTL_F32 && normed_dtype != DOTL_F16)
+        return fail(DOTL_EINVAL, "%s: normed dtype must be DOTL_F32 or DOTL_F16", who);
+    if (rows == 0) return DOTL_OK;
+    if (x == nullptr || weight == nullptr || bias == nullptr || normed == nullptr)
+        return fail(DOTL_EINVAL, "%s: NULL pointer", who);
+    if (sub != nullptr && x_new == nullptr) return fail(DOTL_EINVAL, "%s: sub given without x_new", who);
+    const bool vec = (D % 128 == 0) && aligned16(x) && aligned16(weight) && aligned16(bias) && aligned16(normed) &&
+                     (sub == nullptr || (aligned16(sub) && aligned16(x_new)));
+    const int64_t blocks = (rows + dotl::kLnWarpsPerBlock - 1) / dotl::kLnWarpsPerBlock;
+    const dim3 grid(static_cast<unsigned>(blocks));
+    const dim3 block(dotl::kLnWarpsPerBlock * 32);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int Di = static_cast<int>(D);
+
+#define DOTL_LN(EPL, VEC)                                                                                      \
+    do {                                                                                                       \
+        if (normed_dtype == DOTL_F16)                                                                          \
+            dotl::ln_rows_kernel<EPL, VEC, __half><<<grid, block, 0, s>>>(                                     \
+                x, sub, weight, bias, x_new, static_cast<__half*>(normed), row_valid, rows, Di, eps);          \
+        else                                                                                                   \
+            dotl::ln_rows_kernel<EPL, VEC, float><<<grid, block, 0, s>>>(                                      \
+                x, sub, weight, bias, x_new, static_cast<float*>(normed), row_valid, rows, Di, eps);           \
+    } while (0)
+
+    if (vec) {
+        if (D <= 128) DOTL_LN(4, true);
+        else if (D <= 256) DOTL_LN(8, true);
+        else if (D <= 512) DOTL_LN(16, true);
+        else if (D <= 1024) DOTL_LN(32, true);
+        else DOTL_LN(64, true);
+    } else {
+        if (D <= 32) DOTL_LN(1, false);
+        else if (D <= 64) DOTL_LN(2, false);
+        else if (D <= 128) DOTL_LN(4, false);
+        else if (D <= 256) DOTL_LN(8, false);
+        else if (D <= 512) DOTL_LN(16, false);
+        else if (D <= 1024) DOTL_LN(32, false);
+        else DOTL_LN(64, false);
+    }
+#undef DOTL_LN
+    return check_launch(who);
+}
+
+int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,
+                const float* bias, int act, const float* resid, int64_t ldr, const uint8_t* row_valid, int resid_mode,
+                void* out, int out_dtype, int64_t ldo, int tile_n, void* stream) {
+    const char* who = act ? "linear_gelu" : "linear_bias";
+    if (M < 0 || N <= 0 || K <= 0) return fail(DOTL_EINVAL, "%s: bad shape M=%lld N=%lld K=%lld", who, (long long)M, (long long)N, (long long)K);
+    if (M > (int64_t)0x7fffffff - 256 || N > 0x7fffffff || K > 0x7fffffff)
+        return fail(DOTL_EUNSUPPORTED, "%s: dimensions must fit in 31 bits", who);
+    if (act != 0 && act != 1) return fail(DOTL_EINVAL, "%s: act must be 0 (none) or 1 (GELU)", who);
+    if (resid_mode < DOTL_RESID_NONE || resid_mode > DOTL_RESID_ADD_MASKALL)
+        return fail(DOTL_EINVAL, "%s: unknown residual mode %d", who, resid_mode);
+    if (out_dtype != DOTL_F32 && out_dtype != DOTL_F16) return fail(DOTL_EINVAL, "%s: out dtype must be DOTL_F32 or DOTL_F16", who);
+    if (M == 0) return DOTL_OK;
+    if (a == nullptr || w == nullptr || bias == nullptr || out == nullptr) return fail(DOTL_EINVAL, "%s: NULL pointer", who);
+    if (K % 8 != 0 || lda % 8 != 0 || ldw % 8 != 0 || lda < K || ldw < K)
+        return fail(DOTL_EUNSUPPORTED, "%s: K, lda and ldw must be multiples of 8 (16-byte fp16 rows for TMA), got K=%lld lda=%lld ldw=%lld", who, (long long)K, (long long)lda, (long long)ldw);
+    if (!aligned16(a) || !aligned16(w)) return fail(DOTL_EUNSUPPORTED, "%s: a and w must be 16-byte aligned", who);
+    if (N % 8 != 0) return fail(DOTL_EUNSUPPORTED, "%s: N=%lld must be a multiple of 8", who, (long long)N);
+    if (ldo < N || !aligned16(out) || ldo % 8 != 0) return fail(DOTL_EUNSUPPORTED, "%s: out must be 16-byte aligned with ldo >= N, ldo %% 8 == 0", who);
+    if (resid_mode != DOTL_RESID_NONE) {
+        if (resid == nullptr) return fail(DOTL_EINVAL, "%s: residual mode %d needs resid", who, resid_mode);
+        if (!aligned16(resid) || ldr % 4 != 0 || ldr < N) return fail(DOTL_EUNSUPPORTED, "%s: resid must be 16-byte aligned with ldr >= N, ldr %% 4 == 0", who);
+    }
+    if ((resid_mode == DOTL_RESID_ADD_MASKSUB || resid_mode == DOTL_RESID_ADD_MASKALL) && row_valid == nullptr)
+        return fail(DOTL_EINVAL, "%s: masked residual mode needs row_valid", who);
+    if (!aligned16(bias)) return fail(DOTL_EUNSUPPORTED, "%s: bias must be 16-byte aligned", who);
+
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    int bn = tile_n;
+    if (bn == 0) {
+        // 256-wide tiles halve the A re-reads; take them when they still fill the SMs.
+        const int64_t mt = (M + dotl::kGemmBM - 1) / dotl::kGemmBM;
+        bn = (N >= 256 && mt * ((N + 255) / 256) >= sm_count(dev)) ? 256 : 128;
+    }
+    if (bn != 128 && bn != 256) return fail(DOTL_EINVAL, "%s: tile_n must be 0, 128 or 256", who);
+
+    CUtensorMap ta, tw;
+    const cuuint64_t adims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+    const cuuint64_t astr[1] = {static_cast<cuuint64_t>(lda) * 2};
+    if (int rc = encode_f16_map(&ta, a, 2, adims, astr, dotl::kGemmBK, dotl::kGemmBM, who)) return rc;
+    const cuuint64_t wdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
+    const cuuint64_t wstr[1] = {static_cast<cuuint64_t>(ldw) * 2};
+    if (int rc = encode_f16_map(&tw, w, 2, wdims, wstr, dotl::kGemmBK, static_cast<uint32_t>(bn), who)) return rc;
+
+    dotl::GemmParams p;
+    p.M = static_cast<int>(M);
+    p.N = static_cast<int>(N);
+    p.K = static_cast<int>(K);
+    p.num_m_tiles = static_cast<int>((M + dotl::kGemmBM - 1) / dotl::kGemmBM);
+    p.num_n_tiles = static_cast<int>((N + bn - 1) / bn);
+    p.bias = bias;
+    p.resid = resid;
+    p.ldr = ldr;
+    p.row_valid = row_valid;
+    p.resid_mode = resid_mode;
+    p.act = act;
+    p.out = out;
+    p.ldo = ldo;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (bn == 256)
+        return out_dtype == DOTL_F16 ? launch_gemm<256, 4, true>(ta, tw, p, dev, s)
+                                     : launch_gemm<256, 4, false>(ta, tw, p, dev, s);
+    return out_dtype == DOTL_F16 ? launch_gemm<128, 6, true>(ta, tw, p, dev, s)
+                                 : launch_gemm<128, 6, false>(ta, tw, p, dev, s);
+}
+
+int dotl_attention(const void* q, const void* k, const void* v, int B, int H, int S, int head_dim,
+                   const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, const uint8_t* mask,
+                   int mask_kind, const int64_t* mask_strides, int causal, float scale, void* out, int out_layout,
+                   void* stream) {
+    const char* who = "fused_attention_forward";
+    if (B < 0 || H < 0 || S < 0) return fail(DOTL_EINVAL, "%s: negative shape", who);
+    if (out_layout != 0 && out_layout != 1)
+        return fail(DOTL_EINVAL, "%s: out_layout must be 0 ([B,H,S,head_dim]) or 1 ([B,S,H*head_dim])", who);
+    if (mask_kind < DOTL_MASK_NONE || mask_kind > DOTL_MASK_FULL) return fail(DOTL_EINVAL, "%s: unknown mask kind %d", who, mask_kind);
+    if (head_dim != 32 && head_dim != 64 && head_dim != 128)
+        return fail(DOTL_EUNSUPPORTED, "%s: the tcgen05 kernel covers head_dim 32, 64 and 128, got %d", who, head_dim);
+    if (B == 0 || H == 0 || S == 0) return DOTL_OK;
+    if (q == nullptr || k == nullptr || v == nullptr || out == nullptr || q_strides == nullptr ||
+        k_strides == nullptr || v_strides == nullptr)
+        return fail(DOTL_EINVAL, "%s: NULL pointer", who);
+    if (mask_kind != DOTL_MASK_NONE && (mask == nullptr || mask_strides == nullptr))
+        return fail(DOTL_EINVAL, "%s: mask kind %d needs mask and mask_strides", who, mask_kind);
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+        return fail(DOTL_EUNSUPPORTED, "%s: q, k, v and out must be 16-byte aligned", who);
+    const int64_t* st[3] = {q_strides, k_strides, v_strides};
+    for (int t = 0; t < 3; ++t)
+        for (int d = 0; d < 3; ++d)
+            if (st[t][d] % 8 != 0 || st[t][d] < 0)
+                return fail(DOTL_EUNSUPPORTED, "%s: q/k/v strides must be non-negative multiples of 8 elements (16 bytes)", who);
+    if (static_cast<int64_t>(B) * S > 0x7fffff00LL) return fail(DOTL_EUNSUPPORTED, "%s: B*S must fit in 31 bits", who);
+
+    // Packed tiles run over the flat token axis: every tensor must step from
+    // one batch to the next exactly one sequence length further on.
+    bool packed = true;
+    for (int t = 0; t < 3; ++t) packed = packed && (st[t][0] == static_cast<int64_t>(S) * st[t][2]);
+    // Per-sequence tiles when the sequences already fill 128-row tiles.
+    if (S % dotl::kAttnTile == 0) packed = false;
+
+    dotl::AttnParams p;
+    p.B = B;
+    p.H = H;
+    p.S = S;
+    p.packed = packed ? 1 : 0;
+    p.rows_total = packed ? B * S : S;
+    p.num_q_tiles = (p.rows_total + dotl::kAttnTile - 1) / dotl::kAttnTile;
+    p.num_streams = packed ? H : B * H;
+    p.causal = causal ? 1 : 0;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.mask_kind = mask_kind;
+    p.mask = mask;
+    p.ms0 = mask_strides ? mask_strides[0] : 0;
+    p.ms1 = mask_strides ? mask_strides[1] : 0;
+    p.ms2 = mask_strides ? mask_strides[2] : 0;
+    p.ms3 = mask_strides ? mask_strides[3] : 0;
+    p.out = out;
+    p.out_layout = out_layout;
+
+    const uint32_t box_cols = head_dim < 64 ? static_cast<uint32_t>(head_dim) : 64u;
+    const void* bases[3] = {q, k, v};
+    CUtensorMap maps[3];
+    p.head_inner = 0;
+    for (int t = 0; t < 3; ++t) {
+        if (st[t][1] == 0 || st[t][2] == 0)
+            return fail(DOTL_EUNSUPPORTED, "%s: zero sequence/head strides are not supported", who);
+        // Dimensions in memory order: the head axis goes inside the row axis
+        // when heads are closer together than rows (the fused QKV buffer).
+        const bool head_inner = st[t][1] < st[t][2];
+        const cuuint64_t rows = static_cast<cuuint64_t>(p.rows_total);
+        const cuuint64_t row_stride = static_cast<cuuint64_t>(st[t][2]) * 2;
+        const cuuint64_t head_stride = static_cast<cuuint64_t>(st[t][1]) * 2;
+        cuuint64_t batch_stride = packed ? row_stride * rows : static_cast<cuuint64_t>(st[t][0]) * 2;
+        if (batch_stride == 0) batch_stride = 16;
+        const cuuint64_t batches = packed ? 1 : static_cast<cuuint64_t>(B);
+        cuuint64_t dims[4], strides[3];
+        dims[0] = static_cast<cuuint64_t>(head_dim);
+        if (head_inner) {
+            dims[1] = static_cast<cuuint64_t>(H); dims[2] = rows;
+            strides[0] = head_stride; strides[1] = row_stride;
+        } else {
+            dims[1] = rows; dims[2] = static_cast<cuuint64_t>(H);
+            strides[0] = row_stride; strides[1] = head_stride;
+        }
+        dims[3] = batches;
+        strides[2] = batch_stride;
+        CUtensorMap* m = &maps[t];
+        EncodeTiledFn fn = encode_fn();
+        if (fn == nullptr) return fail(DOTL_ECUDA, "%s: cuTensorMapEncodeTiled is unavailable from the driver", who);
+        cuuint32_t box[4] = {box_cols, head_inner ? 1u : static_cast<cuuint32_t>(dotl::kAttnTile),
+                             head_inner ? static_cast<cuuint32_t>(dotl::kAttnTile) : 1u, 1u};
+        cuuint32_t estr[4] = {1, 1, 1, 1};
+        const CUtensorMapSwizzle swz = box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+        const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(bases[t]), dims, strides, box,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return fail(DOTL_ECUDA, "%s: cuTensorMapEncodeTiled failed (CUresult %d)", who, (int)r);
+        if (head_inner) p.head_inner |= (1 << t);
+    }
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (head_dim) {
+        case 32: return launch_attn<32, 4>(maps[0], maps[1], maps[2], p, dev, s);
+        case 64: return launch_attn<64, 3>(maps[0], maps[1], maps[2], p, dev, s);
+        default: return launch_attn<128, 2>(maps[0], maps[1], maps[2], p, dev, s);
+    }
+}
+
+}  // extern "C"

@@ -1,0 +1,298 @@
+// C = epilogue(A[M,K] * W[N,K]^T + bias) on the 5th-generation tensor cores.
+//
+// Replaces the reference's csrc/linear_gelu.cuh (gemm_bias_act_kernel
+// :186-462, wmma fp16 fragments on sm_80). Same arithmetic contract: fp16
+// operands, fp32 accumulation, bias added in fp32, exact erf GELU.
+//
+// Design (sm_100a):
+//   * persistent: one CTA per SM walks the output tiles with a stride of
+//     gridDim.x; tile (m, n) with n fastest, so CTAs running together share
+//     the same A row-block and the weight matrix stays L2 resident;
+//   * warp-specialised: warp 0 issues TMA loads into a STAGES-deep ring of
+//     128B-swizzled smem tiles, warp 1 issues tcgen05.mma (M=128, N=BN, K=16)
+//     into one of two TMEM accumulators, warps 2-5 drain the other
+//     accumulator through tcgen05.ld and run the fused epilogue, so the
+//     epilogue of tile i overlaps the main loop of tile i+1;
+//   * epilogues: bias, bias+GELU (fp16 out, the FFN hidden), bias + residual
+//     with an optional padded-row mask (fp32 out, the residual stream).
+//
+// A and W are K-major (rows contiguous along K), which is both nn.Linear's
+// weight layout and the activations' row layout: no transpose anywhere.
+
+#pragma once
+
+#include "dotl_common.cuh"
+
+namespace dotl {
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBK = 64;                  // one 128-byte swizzle atom of fp16
+constexpr int kGemmThreads = 192;            // 6 warps
+constexpr uint32_t kGemmATileBytes = kGemmBM * kGemmBK * 2;
+
+enum GemmResidMode : int {
+    kResidNone = 0,       // out = acc + bias (+ GELU)
+    kResidAdd = 1,        // out = resid + (acc + bias)
+    kResidAddMaskSub = 2, // out = resid + (row valid ? acc + bias : 0)
+    kResidAddMaskAll = 3, // out = row valid ? resid + acc + bias : 0
+};
+
+struct GemmParams {
+    int M, N, K;
+    int num_m_tiles, num_n_tiles;
+    const float* bias;       // [N]
+    const float* resid;      // [M, ldr] fp32, or null
+    int64_t ldr;
+    const uint8_t* row_valid;  // [M] (nonzero = valid) or null
+    int resid_mode;
+    int act;                 // 0 = none, 1 = exact GELU
+    void* out;               // [M, ldo], fp16 or fp32
+    int64_t ldo;
+};
+
+template <int BN, int STAGES>
+struct GemmSmem {
+    static constexpr uint32_t kBTileBytes = BN * kGemmBK * 2;
+    static constexpr uint32_t kStageBytes = kGemmATileBytes + kBTileBytes;
+    static constexpr uint32_t kOffA = 0;
+    static constexpr uint32_t kOffB = STAGES * kGemmATileBytes;
+    static constexpr uint32_t kOffBar = kOffB + STAGES * kBTileBytes;
+    // full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], drain
+    static constexpr uint32_t kNumBars = 2 * STAGES + 5;
+    static constexpr uint32_t kOffSlot = kOffBar + kNumBars * 8;
+    static constexpr uint32_t kOffAbort = kOffSlot + 4;
+    static constexpr uint32_t kBytes = kOffAbort + 4;
+    static constexpr uint32_t kAlloc = kBytes + 1024;   // room to align the base to 1024
+    static constexpr uint32_t kTmemCols = 2 * BN;
+};
+
+template <int BN, int STAGES, bool OUT_F16>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                   const __grid_constant__ CUtensorMap tmap_w, const GemmParams p) {
+    using L = GemmSmem<BN, STAGES>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t bar0 = sbase + L::kOffBar;
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+    auto accf_bar = [&](int b) { return bar0 + 8u * (2 * STAGES + b); };
+    auto acce_bar = [&](int b) { return bar0 + 8u * (2 * STAGES + 2 + b); };
+    const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 4);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffAbort);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffSlot);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(accf_bar(b), 1);
+            mbar_init(acce_bar(b), 128);
+        }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        tma_prefetch_map(&tmap_a);
+        tma_prefetch_map(&tmap_w);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), L::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int num_tiles = p.num_m_tiles * p.num_n_tiles;
+    const int num_kb = (p.K + kGemmBK - 1) / kGemmBK;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------------------------------------------- TMA producer --
+        int stage = 0;
+        uint32_t phase = 0;
+        int issued_phase[STAGES];
+        for (int s = 0; s < STAGES; ++s) issued_phase[s] = -1;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            const int m_blk = tile / p.num_n_tiles;
+            const int n_blk = tile - m_blk * p.num_n_tiles;
+            for (int kb = 0; kb < num_kb; ++kb) {
+                if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) goto producer_done;
+                mbar_arrive_expect_tx(full_bar(stage), L::kStageBytes);
+                tma_load_2d(sbase + L::kOffA + stage * kGemmATileBytes, &tmap_a, full_bar(stage),
+                            kb * kGemmBK, m_blk * kGemmBM);
+                tma_load_2d(sbase + L::kOffB + stage * L::kBTileBytes, &tmap_w, full_bar(stage),
+                            kb * kGemmBK, n_blk * BN);
+                issued_phase[stage] = static_cast<int>(phase);
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+        }
+    producer_done:
+        if (*abort_flag) {
+            // Copies still in flight land in this CTA's smem: wait them out.
+            for (int s = 0; s < STAGES; ++s)
+                if (issued_phase[s] >= 0) mbar_wait_drain(full_bar(s), static_cast<uint32_t>(issued_phase[s]));
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ------------------------------------------------------ MMA issuer --
+        constexpr uint32_t idesc = idesc_f16_f32(kGemmBM, BN, false, false);
+        int stage = 0;
+        uint32_t phase = 0;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            if (!mbar_wait(acce_bar(acc), acc_phase ^ 1u, abort_flag)) goto mma_done;
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+            for (int kb = 0; kb < num_kb; ++kb) {
+                if (!mbar_wait(full_bar(stage), phase, abort_flag)) goto mma_done;
+                tc_fence_after();
+                const uint32_t a_addr = sbase + L::kOffA + stage * kGemmATileBytes;
+                const uint32_t b_addr = sbase + L::kOffB + stage * L::kBTileBytes;
+#pragma unroll
+                for (int kk = 0; kk < kGemmBK / 16; ++kk) {
+                    const uint64_t ad = smem_desc(a_addr + kk * 32, 16, 1024, kSwizzle128);
+                    const uint64_t bd = smem_desc(b_addr + kk * 32, 16, 1024, kSwizzle128);
+                    mma_f16_ss(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+                }
+                tc_commit(empty_bar(stage));
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            tc_commit(accf_bar(acc));
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+    mma_done:
+        // Every MMA this thread issued has completed once drain_bar fires.
+        tc_commit(drain_bar);
+        mbar_wait_drain(drain_bar, 0);
+    } else if (warp >= 2) {
+        // -------------------------------------------------------- epilogue --
+        const int quarter = warp & 3;             // TMEM lanes this warp may read
+        const int row_in_tile = quarter * 32 + lane;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            const int m_blk = tile / p.num_n_tiles;
+            const int n_blk = tile - m_blk * p.num_n_tiles;
+            bool ok = mbar_wait(accf_bar(acc), acc_phase, abort_flag);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            tc_fence_after();
+            const int row = m_blk * kGemmBM + row_in_tile;
+            const int n0 = n_blk * BN;
+            const bool row_ok = row < p.M;
+            const bool valid = (p.row_valid == nullptr) || !row_ok || (p.row_valid[row] != 0);
+            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                   static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(t_row + c, r);
+                tmem_ld_wait(r);
+                const int nc = n0 + c;
+                if (!row_ok || nc >= p.N) continue;
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+                const bool full_chunk = (nc + 32 <= p.N);
+                if (full_chunk) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4) {
+                        const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + nc + j));
+                        v[j] += bb.x; v[j + 1] += bb.y; v[j + 2] += bb.z; v[j + 3] += bb.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (nc + j < p.N) v[j] += __ldg(p.bias + nc + j);
+                }
+                if (p.act == 1) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+                }
+                if (p.resid_mode != kResidNone) {
+                    const float* rp = p.resid + static_cast<int64_t>(row) * p.ldr + nc;
+                    const bool keep_sub = valid || p.resid_mode == kResidAdd;
+                    const bool keep_all = valid || p.resid_mode != kResidAddMaskAll;
+                    if (full_chunk) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4) {
+                            const float4 rr = *reinterpret_cast<const float4*>(rp + j);
+                            v[j] = keep_all ? rr.x + (keep_sub ? v[j] : 0.0f) : 0.0f;
+                            v[j + 1] = keep_all ? rr.y + (keep_sub ? v[j + 1] : 0.0f) : 0.0f;
+                            v[j + 2] = keep_all ? rr.z + (keep_sub ? v[j + 2] : 0.0f) : 0.0f;
+                            v[j + 3] = keep_all ? rr.w + (keep_sub ? v[j + 3] : 0.0f) : 0.0f;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (nc + j < p.N)
+                                v[j] = keep_all ? rp[j] + (keep_sub ? v[j] : 0.0f) : 0.0f;
+                    }
+                }
+                if constexpr (OUT_F16) {
+                    __half* op = reinterpret_cast<__half*>(p.out) + static_cast<int64_t>(row) * p.ldo + nc;
+                    if (full_chunk) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 8) {
+                            uint4 h;
+                            h.x = pack_half2(v[j], v[j + 1]);
+                            h.y = pack_half2(v[j + 2], v[j + 3]);
+                            h.z = pack_half2(v[j + 4], v[j + 5]);
+                            h.w = pack_half2(v[j + 6], v[j + 7]);
+                            *reinterpret_cast<uint4*>(op + j) = h;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (nc + j < p.N) op[j] = __float2half_rn(v[j]);
+                    }
+                } else {
+                    float* op = reinterpret_cast<float*>(p.out) + static_cast<int64_t>(row) * p.ldo + nc;
+                    if (full_chunk) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4)
+                            *reinterpret_cast<float4*>(op + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (nc + j < p.N) op[j] = v[j];
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(acce_bar(acc));
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+    }
+
+    // ------------------------------------------------------------ teardown --
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, L::kTmemCols);
+    }
+}
+
+}  // namespace dotl

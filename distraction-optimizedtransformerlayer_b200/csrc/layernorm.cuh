@@ -1,0 +1,179 @@
+// Residual add + LayerNorm, one warp per row, the row held in registers.
+//
+// Replaces the reference's csrc/add_layernorm.cuh (block-per-row kernel
+// :131-214 and warp-per-row kernel :244-318). Same contract:
+//
+//   x_new  = x + sub                       (only when sub is given)
+//   normed = (x_new - mean) * rstd * w + b  over the last dimension, eps as given
+//
+// plus an optional row-valid mask that writes 0 to `normed` on padded rows,
+// which is the model's final masked_fill folded into the final LayerNorm.
+//
+// The statistics are two-pass over the registers: the mean first, then the
+// mean of squared deviations from it. That is the corrected form the reference
+// adopted for large-mean rows (add_layernorm.cuh:168-207), here with no extra
+// memory pass because the row never leaves the registers.
+//
+// Bandwidth: every byte is read or written once, with 16-byte accesses when D
+// is a multiple of 128. The kernel is HBM-bound; its roofline is bytes moved
+// over the measured copy bandwidth.
+
+#pragma once
+
+#include "dotl_common.cuh"
+
+namespace dotl {
+
+constexpr int kLnWarpsPerBlock = 8;
+
+template <typename T>
+__device__ __forceinline__ void store_val(T* p, float v);
+template <>
+__device__ __forceinline__ void store_val<float>(float* p, float v) { *p = v; }
+template <>
+__device__ __forceinline__ void store_val<__half>(__half* p, float v) { *p = __float2half_rn(v); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    return v;
+}
+
+// EPL = elements per lane (D <= 32 * EPL). VEC4: D % 128 == 0 and every row
+// 16-byte aligned, so each lane moves float4 chunks at (i * 32 + lane) * 4.
+template <int EPL, bool VEC4, typename NormT>
+__global__ void __launch_bounds__(kLnWarpsPerBlock * 32)
+    ln_rows_kernel(const float* __restrict__ x, const float* __restrict__ sub,
+                   const float* __restrict__ w, const float* __restrict__ b,
+                   float* __restrict__ x_new, NormT* __restrict__ normed,
+                   const uint8_t* __restrict__ row_valid, int64_t rows, int D, float eps) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * kLnWarpsPerBlock + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const int64_t base = row * D;
+    float v[EPL];
+
+    if constexpr (VEC4) {
+#pragma unroll
+        for (int i = 0; i < EPL / 4; ++i) {
+            const int c = (i * 32 + lane) * 4;
+            if (c < D) {
+                float4 a = *reinterpret_cast<const float4*>(x + base + c);
+                if (sub != nullptr) {
+                    const float4 s = *reinterpret_cast<const float4*>(sub + base + c);
+                    a.x += s.x; a.y += s.y; a.z += s.z; a.w += s.w;
+                    if (x_new != nullptr) *reinterpret_cast<float4*>(x_new + base + c) = a;
+                }
+                v[4 * i] = a.x; v[4 * i + 1] = a.y; v[4 * i + 2] = a.z; v[4 * i + 3] = a.w;
+            } else {
+                v[4 * i] = v[4 * i + 1] = v[4 * i + 2] = v[4 * i + 3] = 0.0f;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) {
+            const int c = i * 32 + lane;
+            float a = 0.0f;
+            if (c < D) {
+                a = x[base + c];
+                if (sub != nullptr) {
+                    a += sub[base + c];
+                    if (x_new != nullptr) x_new[base + c] = a;
+                }
+            }
+            v[i] = a;
+        }
+    }
+
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) s += v[i];
+    const float mean = warp_sum(s) / static_cast<float>(D);
+
+    float ss = 0.0f;
+    if constexpr (VEC4) {
+#pragma unroll
+        for (int i = 0; i < EPL / 4; ++i) {
+            if ((i * 32 + lane) * 4 < D) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float c = v[4 * i + j] - mean;
+                    ss += c * c;
+                }
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) {
+            if (i * 32 + lane < D) {
+                const float c = v[i] - mean;
+                ss += c * c;
+            }
+        }
+    }
+    const float rstd = rsqrtf(warp_sum(ss) / static_cast<float>(D) + eps);
+    const bool keep = (row_valid == nullptr) || (row_valid[row] != 0);
+
+    if constexpr (VEC4) {
+#pragma unroll
+        for (int i = 0; i < EPL / 4; ++i) {
+            const int c = (i * 32 + lane) * 4;
+            if (c < D) {
+                const float4 ww = *reinterpret_cast<const float4*>(w + c);
+                const float4 bb = *reinterpret_cast<const float4*>(b + c);
+                float o0 = (v[4 * i] - mean) * rstd * ww.x + bb.x;
+                float o1 = (v[4 * i + 1] - mean) * rstd * ww.y + bb.y;
+                float o2 = (v[4 * i + 2] - mean) * rstd * ww.z + bb.z;
+                float o3 = (v[4 * i + 3] - mean) * rstd * ww.w + bb.w;
+                if (!keep) o0 = o1 = o2 = o3 = 0.0f;
+                if constexpr (sizeof(NormT) == 4) {
+                    *reinterpret_cast<float4*>(reinterpret_cast<float*>(normed) + base + c) =
+                        make_float4(o0, o1, o2, o3);
+                } else {
+                    uint2 h;
+                    h.x = pack_half2(o0, o1);
+                    h.y = pack_half2(o2, o3);
+                    *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(normed) + base + c) = h;
+                }
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) {
+            const int c = i * 32 + lane;
+            if (c < D) {
+                const float o = keep ? (v[i] - mean) * rstd * w[c] + b[c] : 0.0f;
+                store_val<NormT>(normed + base + c, o);
+            }
+        }
+    }
+}
+
+// Elementwise fp32 -> fp16 (round to nearest even), for callers that hand the
+// fp16 GEMM an fp32 activation.
+__global__ void cast_f32_f16_kernel(const float* __restrict__ in, __half* __restrict__ out, int64_t n) {
+    const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+    if (i + 3 < n) {
+        const float4 a = *reinterpret_cast<const float4*>(in + i);
+        uint2 h;
+        h.x = pack_half2(a.x, a.y);
+        h.y = pack_half2(a.z, a.w);
+        *reinterpret_cast<uint2*>(out + i) = h;
+    } else {
+        for (int64_t j = i; j < n; ++j) out[j] = __float2half_rn(in[j]);
+    }
+}
+
+// Elementwise fp16 -> fp32.
+__global__ void cast_f16_f32_kernel(const __half* __restrict__ in, float* __restrict__ out, int64_t n) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = __half2float(in[i]);
+}
+
+// The build's smoke test: a plain copy (the reference's identity_kernel).
+__global__ void identity_f32_kernel(const float* __restrict__ in, float* __restrict__ out, int64_t n) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = in[i];
+}
+
+}  // namespace dotl

@@ -1,0 +1,94 @@
+"""Runtime knobs for the optimized model (optimized/config.py upstream).
+
+Read at call time, so a script can flip one between runs:
+
+    from optimized import config
+    config.CUDA_GRAPH = "off"
+
+The names are the reference's. What differs is what a value can select: this
+build has one implementation of every op (libdotl's sm_100a kernels) and no
+prebuilt fallback, so a value that would select cuBLAS, ATen or SDPA upstream
+("off" for LINEAR_GELU / LINEAR_BIAS / LAYERNORM, "sdpa") is refused with an
+error at the first forward pass instead of silently computing something else.
+"""
+
+# Attention backend: one legal value, as upstream.
+ATTENTION_BACKEND = "custom"
+
+# Which attention kernel: "auto" and "wmma" both mean the tcgen05 tensor-core
+# kernel (the reference's name for its tensor-core kernel is kept so command
+# lines keep working). "scalar" and "tile" are not built and raise.
+ATTENTION_IMPL = "auto"
+_IMPL_CODE = {"auto": 0, "scalar": 1, "wmma": 2, "tile": 3}
+
+# Attention arithmetic: "auto" / "fp16" (fp16 operands, fp32 softmax and
+# accumulation). "fp32", "tf32" and "bf16" are not built and raise.
+ATTENTION_PRECISION = "auto"
+_PRECISION_CODE = {"auto": 0, "fp32": 1, "tf32": 2, "fp16": 3, "bf16": 4}
+
+# The attention kernel writes [B, S, H*head_dim], the layout out_proj reads.
+_OUT_LAYOUT_BSHD = 1
+
+# GEMM epilogue fusions. "auto" = the tcgen05 GEMM with bias (+GELU) fused.
+LINEAR_GELU = "auto"
+LINEAR_BIAS = "auto"
+
+# Entry LayerNorm on libdotl's warp-per-row kernel.
+LAYERNORM = "auto"
+
+# fp16 edges. Every GEMM here reads fp16 A from TMA, so the producer of a GEMM
+# input always stores fp16 (the same RNE the reference's GEMM applied while
+# staging, one pass earlier). "off" is accepted and changes no value.
+QKV_FP16 = "auto"
+NORMED_FP16 = "auto"
+
+# The reference's fused FFN kernel only covered d_model <= 128; here the FFN
+# always runs as LN -> GEMM(+GELU) -> GEMM(+residual, +row mask) -> LN.
+FFN_BLOCK = "auto"
+
+# cp.async knob of the reference's wmma kernel; TMA does the staging here.
+CP_ASYNC = "auto"
+_CP_ASYNC_CODE = {"off": 0, "sync": 1, "auto": 2}
+
+_GEMM_MATH_CODE = {"auto": -1, "tf32": 0}
+
+# CUDA graph capture of the whole forward: "off", "auto" (capture when the
+# activation B*S*d_model is at or under _GRAPH_MAX_ACTIVATION) or "always".
+CUDA_GRAPH = "auto"
+
+# Re-derived for B200. The upstream 524288 was measured on an RTX 3070, where
+# the GPU stopped starving at ~0.5 M activation elements; a B200 finishes the
+# same work ~30x sooner, so launch overhead dominates to much larger shapes.
+# Replay is bit-identical to eager, so the bound only caps the pinned pool.
+_GRAPH_MAX_ACTIVATION = 1 << 27
+_GRAPH_POOL_SAFETY_FRACTION = 0.25
+_GRAPH_MAX_ENTRIES = 4
+_GRAPH_WARMUP_ITERS = 3
+_GRAPH_MIN_FREE_BYTES = 512 << 20
+_GRAPH_SEED = 20240827
+
+# Split the batch and retry when a forward runs out of memory.
+MICROBATCH_FALLBACK = True
+_MICROBATCH_MIN_ROWS = 1
+_MICROBATCH_PEAK_FACTOR = 10
+_MICROBATCH_BUDGET_FRACTION = 0.85
+
+
+def validate() -> None:
+    """Raise ValueError for knob values that would need a fallback this build refuses."""
+    if ATTENTION_BACKEND != "custom":
+        raise ValueError(f"ATTENTION_BACKEND={ATTENTION_BACKEND!r}: only 'custom' exists")
+    if ATTENTION_IMPL not in ("auto", "wmma"):
+        raise ValueError(f"ATTENTION_IMPL={ATTENTION_IMPL!r} is not built: the tcgen05 kernel "
+                         "('auto' or 'wmma') is the only attention here")
+    if ATTENTION_PRECISION not in ("auto", "fp16"):
+        raise ValueError(f"ATTENTION_PRECISION={ATTENTION_PRECISION!r} is not built: the "
+                         "tensor-core kernel contracts fp16 operands ('auto' or 'fp16')")
+    for name in ("LINEAR_GELU", "LINEAR_BIAS"):
+        if globals()[name] != "auto":
+            raise ValueError(f"{name}={globals()[name]!r}: only 'auto' (the tcgen05 GEMM) exists; "
+                             "there is no cuBLAS or tf32 path")
+    if LAYERNORM != "auto":
+        raise ValueError(f"LAYERNORM={LAYERNORM!r}: only 'auto' exists; there is no ATen fallback")
+    if CUDA_GRAPH not in ("off", "auto", "always"):
+        raise ValueError(f"CUDA_GRAPH={CUDA_GRAPH!r}: expected 'off', 'auto' or 'always'")

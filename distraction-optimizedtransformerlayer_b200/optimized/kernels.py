@@ -1,0 +1,93 @@
+"""Dispatch into libdotl (optimized/kernels.py upstream).
+
+The boundary between torch and the sm_100a kernels: every helper here calls
+the library through `kernel_ext.get_kernels()` and raises when it is missing.
+There is no torch fallback for any op (the reference fell back to cuBLAS and
+ATen for the GEMMs and LayerNorm; the B200 build refuses instead).
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+from . import config
+
+
+def _custom_kernels():
+    """The kernel module; raises if the library cannot be loaded."""
+    import kernel_ext
+
+    kernels = kernel_ext.get_kernels()
+    if kernels is None:
+        raise RuntimeError(
+            "libdotl (the sm_100a kernel library) failed to load, and there is no fallback: "
+            "this project implements every op of the layer itself. Build it with "
+            f"kernel_ext.build(). Cause: {kernel_ext.load_error()}")
+    return kernels
+
+
+def _f32_param(module, name: str) -> torch.Tensor:
+    """A parameter as a contiguous fp32 tensor, cached per parameter version
+    (parameters may have been moved to fp16/bf16 by model.to(dtype))."""
+    p = getattr(module, name)
+    if p.dtype == torch.float32 and p.is_contiguous():
+        return p
+    cache = module.__dict__.setdefault("_f32_cache", {})
+    key = (name, p.data_ptr(), p.device, p.dtype, getattr(p, "_version", None))
+    hit = cache.get(name)
+    if hit is not None and hit[0] == key:
+        return hit[1]
+    t = p.detach().float().contiguous()
+    cache[name] = (key, t)
+    return t
+
+
+def _layernorm(x: torch.Tensor, norm, out_half: bool = False,
+               row_valid: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """LayerNorm(x) * w + b over the last dim of fp32 x; padded rows -> 0 if row_valid."""
+    k = _custom_kernels()
+    return k.layernorm_rows(x, _f32_param(norm, "weight"), _f32_param(norm, "bias"), norm.eps,
+                            out_half=out_half, row_valid=row_valid)
+
+
+def _add_layernorm(x: torch.Tensor, sub: torch.Tensor, norm,
+                   normed_half: bool = False) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(x + sub, norm(x + sub)) in one kernel."""
+    k = _custom_kernels()
+    return k.layernorm_rows(x, _f32_param(norm, "weight"), _f32_param(norm, "bias"), norm.eps,
+                            sub=sub, out_half=normed_half)
+
+
+def _linear(a16: torch.Tensor, w16: torch.Tensor, bias32: torch.Tensor, act: int = 0,
+            resid: Optional[torch.Tensor] = None, row_valid: Optional[torch.Tensor] = None,
+            resid_mode: int = 0, out_half: bool = False) -> torch.Tensor:
+    """epilogue(a16 @ w16^T + bias) on the tcgen05 GEMM."""
+    k = _custom_kernels()
+    return k.linear_fp16(a16, w16, bias32, act=act, resid=resid, row_valid=row_valid,
+                         resid_mode=resid_mode, out_half=out_half)
+
+
+def _linear_bias(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,
+                 out_half: bool = False) -> torch.Tensor:
+    """x @ weight^T + bias with the reference signature (fp32 weight)."""
+    return _custom_kernels().linear_bias(x, weight, bias, -1, -1, out_half)
+
+
+def _linear_gelu(x: torch.Tensor, lin) -> torch.Tensor:
+    """GELU(lin(x)) with the reference signature."""
+    return _custom_kernels().linear_gelu(x, lin.weight, lin.bias, -1, -1)
+
+
+def _attention_dispatch(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                        key_mask: Optional[torch.Tensor], is_causal: bool, scale: float,
+                        out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Attention on the tcgen05 kernel; q/k/v fp16 [B,H,S,hd] views; returns [B,S,H*hd] fp16.
+
+    key_mask: bool [B,S], True = may attend (the [B,1,1,S] mask upstream).
+    """
+    config.validate()
+    kernels = _custom_kernels()
+    return kernels.attention_packed(q, k, v, is_causal, scale, key_mask=key_mask,
+                                    out_layout=config._OUT_LAYOUT_BSHD, out=out)

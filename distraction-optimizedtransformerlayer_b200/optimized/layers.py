@@ -1,0 +1,170 @@
+"""Drop-in replacements for the baseline's submodules (optimized/layers.py upstream).
+
+Parameter and submodule names match BaselineTransformer exactly, so one
+state_dict loads into either model with strict=True.
+
+Data flow of one block (T = B*S rows, d = d_model):
+
+    normed [T,d] fp16 --QKV GEMM--> qkv [T,3d] fp16 --attention--> ctx [T,d] fp16
+    ctx --out_proj GEMM, epilogue: + bias, padded rows -> 0, + residual x--> x1 [T,d] fp32
+    x1 --LayerNorm--> n2 fp16 --ffn_in GEMM, epilogue: + bias, GELU--> h [T,F] fp16
+    h --ffn_out GEMM, epilogue: + bias + residual x1, padded rows -> 0--> x2 [T,d] fp32
+    x2 --next_norm (fp16 for a next block; fp32 with padded rows -> 0 if final)--> normed
+
+Every residual add and masked_fill of the reference block
+(torch_transformer_benchmark.py:234-245) is folded into a GEMM epilogue or a
+LayerNorm, so a block is 6 kernels and never writes an intermediate it reads
+back only to add it.
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+import torch.nn as nn
+
+from . import config
+from .kernels import (_attention_dispatch, _f32_param, _layernorm, _linear, _linear_bias)
+from .util import _version_or_none
+
+RESID_ADD, RESID_ADD_MASKSUB, RESID_ADD_MASKALL = 1, 2, 3
+
+
+class MyLinear(nn.Module):
+    """Same parameter names/shapes as nn.Linear -> free strict weight loading."""
+
+    def __init__(self, in_features: int, out_features: int, bias: bool = True) -> None:
+        super().__init__()
+        self.weight = nn.Parameter(torch.empty(out_features, in_features))
+        self.bias = nn.Parameter(torch.empty(out_features)) if bias else None
+        self._w16_key = None
+        self._w16: Optional[torch.Tensor] = None
+
+    def half_weight(self) -> torch.Tensor:
+        """The weight narrowed to fp16 once per version (the GEMM's B operand)."""
+        w = self.weight
+        key = (w.device, w.dtype, w.data_ptr(), _version_or_none(w))
+        if self._w16_key != key:
+            self._w16 = w.detach().to(torch.float16).contiguous()
+            self._w16_key = key
+        return self._w16
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.bias is None:
+            raise RuntimeError("MyLinear: the GEMM epilogue always adds a bias; every Linear "
+                               "of this model has one")
+        return _linear_bias(x, self.weight, self.bias)
+
+
+class MyLayerNorm(nn.Module):
+    """Same parameter names/shapes as nn.LayerNorm -> free strict weight loading."""
+
+    def __init__(self, d_model: int, eps: float = 1e-5) -> None:
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(d_model))
+        self.bias = nn.Parameter(torch.zeros(d_model))
+        self.eps = eps
+
+    def forward(self, x: torch.Tensor, out_half: bool = False) -> torch.Tensor:
+        return _layernorm(x.float().contiguous(), self, out_half=out_half)
+
+
+class MySelfAttention(nn.Module):
+    """Same submodule names as BaselineSelfAttention -> free strict weight loading."""
+
+    def __init__(self, d_model: int, num_heads: int) -> None:
+        super().__init__()
+        self.num_heads = num_heads
+        self.head_dim = d_model // num_heads
+        self.scale = self.head_dim ** -0.5
+        self.q_proj = MyLinear(d_model, d_model)
+        self.k_proj = MyLinear(d_model, d_model)
+        self.v_proj = MyLinear(d_model, d_model)
+        self.out_proj = MyLinear(d_model, d_model)
+        self._qkv_key: Optional[Tuple] = None
+        self._qkv_weight: Optional[torch.Tensor] = None
+        self._qkv_bias: Optional[torch.Tensor] = None
+
+    def _get_qkv_weight(self) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Q, K and V as one fp16 [3d, d] weight and one fp32 [3d] bias
+        (layers.py:88-110 upstream: one wide GEMM instead of three narrow
+        ones), rebuilt when any of the three weights changes version."""
+        w_q, w_k, w_v = self.q_proj.weight, self.k_proj.weight, self.v_proj.weight
+        key = (w_q.device, w_q.dtype, _version_or_none(w_q), _version_or_none(w_k),
+               _version_or_none(w_v), _version_or_none(self.q_proj.bias),
+               _version_or_none(self.k_proj.bias), _version_or_none(self.v_proj.bias),
+               w_q.data_ptr(), w_k.data_ptr(), w_v.data_ptr())
+        if self._qkv_key != key:
+            self._qkv_weight = torch.cat([w_q, w_k, w_v], dim=0).detach().to(torch.float16).contiguous()
+            self._qkv_bias = torch.cat([self.q_proj.bias, self.k_proj.bias, self.v_proj.bias],
+                                       dim=0).detach().float().contiguous()
+            self._qkv_key = key
+        return self._qkv_weight, self._qkv_bias
+
+    def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None,
+                causal: bool = False, mask_is_trivial: bool = False,
+                residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """out_proj(attention(x)) with padded rows zeroed, plus `residual` if given.
+
+        x is the block's normalised input [B,S,d] (fp16 or fp32). With
+        `residual`, the add x + attn happens in the out_proj epilogue and the
+        fp32 sum is returned; without it, the attention output alone.
+        """
+        batch, seq_len, d_model = x.shape
+        x16 = x if x.dtype == torch.float16 else x.to(torch.float16)
+        x16 = x16.contiguous()
+        qkv_w, qkv_b = self._get_qkv_weight()
+        qkv = _linear(x16, qkv_w, qkv_b, out_half=True)           # [B, S, 3d] fp16
+        q, k, v = (qkv.view(batch, seq_len, 3, self.num_heads, self.head_dim)
+                   .permute(2, 0, 3, 1, 4).unbind(0))              # [B, H, S, hd] views
+        use_mask = valid_token_mask is not None and not mask_is_trivial
+        key_mask = valid_token_mask if use_mask else None
+        context = _attention_dispatch(q, k, v, key_mask, causal, self.scale)   # [B, S, d] fp16
+        row_valid = valid_token_mask.reshape(-1) if use_mask else None
+        if residual is None:
+            # Plain attention output, padded rows zeroed: residual is zero.
+            zeros = torch.zeros(batch, seq_len, d_model, device=x.device, dtype=torch.float32)
+            return _linear(context, self.out_proj.half_weight(), _f32_param(self.out_proj, "bias"),
+                           resid=zeros, row_valid=row_valid,
+                           resid_mode=RESID_ADD_MASKSUB if use_mask else RESID_ADD)
+        return _linear(context, self.out_proj.half_weight(), _f32_param(self.out_proj, "bias"),
+                       resid=residual, row_valid=row_valid,
+                       resid_mode=RESID_ADD_MASKSUB if use_mask else RESID_ADD)
+
+
+class MyTransformerBlock(nn.Module):
+    """Same submodule names as BaselineTransformerBlock -> free strict weight loading."""
+
+    def __init__(self, d_model: int, num_heads: int, ffn_dim: int, causal: bool) -> None:
+        super().__init__()
+        self.norm1 = MyLayerNorm(d_model)
+        self.attention = MySelfAttention(d_model, num_heads)
+        self.norm2 = MyLayerNorm(d_model)
+        self.ffn_in = MyLinear(d_model, ffn_dim)
+        self.ffn_out = MyLinear(ffn_dim, d_model)
+        self.causal = causal
+
+    def forward(self, x: torch.Tensor, normed: torch.Tensor, next_norm: "MyLayerNorm",
+                valid_token_mask: Optional[torch.Tensor] = None, mask_is_trivial: bool = False,
+                next_norm_is_output: bool = False) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Returns (residual stream, next_norm applied to it) (layers.py:206-262 upstream).
+
+        `normed` is norm1(x), produced by whoever produced x. `next_norm` is
+        the next block's norm1 or the model's final_norm; when it is the final
+        norm (next_norm_is_output) its output is fp32 with padded rows zeroed
+        (the model's final masked_fill), otherwise fp16 for the next QKV GEMM.
+        """
+        use_mask = valid_token_mask is not None and not mask_is_trivial
+        row_valid = valid_token_mask.reshape(-1) if use_mask else None
+        x1 = self.attention(normed, valid_token_mask, self.causal, mask_is_trivial, residual=x)
+        n2 = _layernorm(x1, self.norm2, out_half=True)
+        h = _linear(n2, self.ffn_in.half_weight(), _f32_param(self.ffn_in, "bias"), act=1,
+                    out_half=True)
+        # x1 + ffn_out(h); padded rows of the whole sum zeroed (the block's
+        # trailing masked_fill), before the next LayerNorm reads it.
+        x2 = _linear(h, self.ffn_out.half_weight(), _f32_param(self.ffn_out, "bias"), resid=x1,
+                     row_valid=row_valid, resid_mode=RESID_ADD_MASKALL if use_mask else RESID_ADD)
+        if next_norm_is_output:
+            return x2, _layernorm(x2, next_norm, out_half=False, row_valid=row_valid)
+        return x2, _layernorm(x2, next_norm, out_half=True)

@@ -1,0 +1,154 @@
+"""The optimized transformer (optimized/model.py upstream)."""
+
+from __future__ import annotations
+
+import weakref
+from typing import TYPE_CHECKING, Dict, Optional, Tuple
+
+import torch
+import torch.nn as nn
+
+from . import config
+from .graphs import _GraphRunner, _capture_graph, _graph_eligible, _graph_key
+from .kernels import _layernorm
+from .layers import MyLayerNorm, MyTransformerBlock
+from .util import _version_or_none
+
+if TYPE_CHECKING:
+    from torch_transformer_benchmark import TransformerConfig
+
+
+class OptimizedTransformer(nn.Module):
+    """Pre-LN transformer layers + final LayerNorm on libdotl's sm_100a kernels.
+
+    Parameter and submodule names match BaselineTransformer exactly, so
+    copy_model_weights() loads one state_dict into either with strict=True,
+    and the harness's `class UserOptimizedTransformer(OptimizedTransformer,
+    BaselineTransformer)` works unchanged. forward(x, valid_token_mask=None)
+    has the reference's signature and returns [B, S, d_model] in x's dtype.
+    """
+
+    def __init__(self, config: "TransformerConfig") -> None:
+        nn.Module.__init__(self)
+        self.config = config
+        self.layers = nn.ModuleList([
+            MyTransformerBlock(config.d_model, config.num_heads, config.ffn_dim, config.causal)
+            for _ in range(config.num_layers)
+        ])
+        self.final_norm = MyLayerNorm(config.d_model)
+        self._triv_ref: Optional[weakref.ReferenceType] = None
+        self._triv_version: Optional[int] = None
+        self._triv: bool = False
+        self._graphs: Dict[Tuple, _GraphRunner] = {}
+        self._graph_denied: set = set()
+        self._chunk_rows: Dict[Tuple, int] = {}
+        self._device_budget: Optional[int] = None
+
+    def _mask_is_trivial(self, mask: Optional[torch.Tensor]) -> bool:
+        """True when every position is valid (model.py:68-93 upstream): one
+        device->host sync per new mask object, memoised by weakref + version."""
+        if mask is None:
+            return False
+        version = _version_or_none(mask)
+        cached = self._triv_ref() if self._triv_ref is not None else None
+        if cached is mask and self._triv_version == version and version is not None:
+            return self._triv
+        self._triv = bool(mask.all().item())
+        self._triv_ref = weakref.ref(mask)
+        self._triv_version = version
+        return self._triv
+
+    def _forward_eager(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor],
+                       use_mask: bool) -> torch.Tensor:
+        """The whole model with every host decision made: capturable (no host
+        reads, no lazily built state that outlives the call)."""
+        dtype = x.dtype
+        x = x.float().contiguous()
+        mask = valid_token_mask.contiguous() if use_mask else None
+        normed = _layernorm(x, self.layers[0].norm1, out_half=True)
+        last = len(self.layers) - 1
+        for index, layer in enumerate(self.layers):
+            next_norm = self.final_norm if index == last else self.layers[index + 1].norm1
+            x, normed = layer(x, normed, next_norm, mask, not use_mask, index == last)
+        # The last block folded final_norm and the final masked_fill into its
+        # trailing LayerNorm, so `normed` is already the model's output.
+        return normed if dtype == torch.float32 else normed.to(dtype)
+
+    def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        config.validate()
+        mask_is_trivial = self._mask_is_trivial(valid_token_mask)
+        use_mask = valid_token_mask is not None and not mask_is_trivial
+        key = _graph_key(x, use_mask)
+        runner = self._graphs.get(key)
+        if runner is None:
+            runner = self._maybe_capture(key, x, valid_token_mask, use_mask)
+        if runner is not None:
+            return runner.replay(x, valid_token_mask)
+        if config.MICROBATCH_FALLBACK and x.is_cuda and x.shape[0] > 1:
+            return self._forward_chunk_on_oom(x, valid_token_mask, use_mask)
+        return self._forward_eager(x, valid_token_mask, use_mask)
+
+    def _rows_within_budget(self, x: torch.Tensor) -> int:
+        rows = x.shape[0]
+        per_row = x.shape[1] * x.shape[2] * x.element_size() * config._MICROBATCH_PEAK_FACTOR
+        if per_row <= 0:
+            return rows
+        budget = self._device_budget
+        if budget is None:
+            _, total = torch.cuda.mem_get_info(x.device)
+            budget = int(total * config._MICROBATCH_BUDGET_FRACTION)
+            self._device_budget = budget
+        if per_row * rows <= budget:
+            return rows
+        return max(config._MICROBATCH_MIN_ROWS, min(rows, budget // per_row))
+
+    def _forward_chunk_on_oom(self, x, valid_token_mask, use_mask):
+        """_forward_eager, retried over batch chunks if it runs out of memory
+        (model.py:194-246 upstream). Rows never interact, so chunking changes
+        no value: every kernel here computes a row independently of M."""
+        rows = x.shape[0]
+        key = (rows, x.shape[1], x.shape[2], x.dtype, use_mask)
+        n = self._chunk_rows.get(key)
+        if n is None:
+            n = self._rows_within_budget(x)
+        if n >= rows:
+            try:
+                return self._forward_eager(x, valid_token_mask, use_mask)
+            except torch.OutOfMemoryError:
+                torch.cuda.empty_cache()
+                n = rows // 2
+        while n >= config._MICROBATCH_MIN_ROWS:
+            out = None
+            try:
+                out = torch.empty_like(x)
+                for lo in range(0, rows, n):
+                    hi = min(lo + n, rows)
+                    m = valid_token_mask[lo:hi] if valid_token_mask is not None else None
+                    out[lo:hi] = self._forward_eager(x[lo:hi], m, use_mask)
+                self._chunk_rows[key] = n
+                return out
+            except torch.OutOfMemoryError:
+                del out
+                torch.cuda.empty_cache()
+                if n <= config._MICROBATCH_MIN_ROWS:
+                    raise
+                n //= 2
+        return self._forward_eager(x, valid_token_mask, use_mask)
+
+    def _maybe_capture(self, key, x, valid_token_mask, use_mask) -> Optional[_GraphRunner]:
+        if key in self._graph_denied:
+            return None
+        if not _graph_eligible(x, len(self._graphs)):
+            return None
+        runner = _capture_graph(self, x, valid_token_mask, use_mask)
+        if runner is None:
+            self._graph_denied.add(key)
+            return None
+        self._graphs[key] = runner
+        return runner
+
+    def release_graphs(self) -> None:
+        """Free every captured graph of this model (before process-group teardown)."""
+        for runner in self._graphs.values():
+            runner.release()
+        self._graphs.clear()

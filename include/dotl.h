@@ -1,0 +1,123 @@
+/*
+ * libdotl: the C ABI of the B200 (sm_100a) single-transformer-layer forward.
+ *
+ * Every entry point takes plain device pointers, sizes and strides, and a
+ * cudaStream_t passed as `void* stream`. No entry point allocates device
+ * memory or synchronises: outputs and temporaries are the caller's, and work
+ * is enqueued on `stream` (so the calls can be captured in a CUDA graph).
+ *
+ * Return value: 0 on success; a nonzero DOTL_E* code otherwise, with a
+ * message for the calling thread in dotl_last_error(). A rejected call
+ * enqueues nothing.
+ *
+ * Each declaration names the reference entry point it replaces
+ * (jazwinn/Distraction-OptimizedTransformerLayer, pybind module
+ * `transformer_kernels`, csrc/fused_attention.cu:118-376). The reference binds
+ * torch tensors through pybind; this ABI takes their data pointers, so any FFI
+ * (ctypes, cffi, cgo, JNI) can bind it. The Python binding that rebuilds the
+ * reference's tensor-level functions on top of it is
+ * distraction-optimizedtransformerlayer_b200/dotl_ops.py.
+ */
+#ifndef DOTL_H_
+#define DOTL_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DOTL_ABI_VERSION 1
+
+/* status codes */
+#define DOTL_OK 0
+#define DOTL_EINVAL 1      /* an argument is out of the supported range */
+#define DOTL_EUNSUPPORTED 2 /* a valid request no kernel here covers */
+#define DOTL_ECUDA 3       /* the CUDA runtime/driver reported an error */
+
+/* element types */
+#define DOTL_F32 0
+#define DOTL_F16 1
+
+/* dotl_linear residual modes */
+#define DOTL_RESID_NONE 0        /* out = act(a w^T + bias) */
+#define DOTL_RESID_ADD 1         /* out = resid + (a w^T + bias) */
+#define DOTL_RESID_ADD_MASKSUB 2 /* out = resid + (valid ? a w^T + bias : 0) */
+#define DOTL_RESID_ADD_MASKALL 3 /* out = valid ? resid + a w^T + bias : 0 */
+
+/* dotl_attention mask kinds */
+#define DOTL_MASK_NONE 0
+#define DOTL_MASK_KEY 1  /* per-key bool: mask[b*ms[0] + key*ms[3]], 1 = may attend */
+#define DOTL_MASK_FULL 2 /* bool [B,H,S,S] via strides ms[0..3], 1 = may attend */
+
+int dotl_abi_version(void);
+
+/* Message for the last failed call on this thread ("" if none). */
+const char* dotl_last_error(void);
+
+/* Number of SMs of the current device (for sizing persistent grids). */
+int dotl_num_sms(int* out);
+
+/*
+ * Sticky device-side error word. Kernels that give up a bounded wait (two
+ * seconds on an mbarrier) set a bit here instead of hanging. Reading it
+ * synchronises the current device. clear != 0 resets it.
+ */
+int dotl_device_error(int clear, unsigned int* word);
+
+/* Copies n floats. Replaces smoke_test_identity (fused_attention.cu:97-116). */
+int dotl_identity_f32(const float* in, float* out, int64_t n, void* stream);
+
+/* fp32 -> fp16 (round to nearest even) and back, elementwise. */
+int dotl_cast_f32_f16(const float* in, void* out_f16, int64_t n, void* stream);
+int dotl_cast_f16_f32(const void* in_f16, float* out, int64_t n, void* stream);
+
+/*
+ * Residual add + LayerNorm over the last dimension of a [rows, D] fp32 tensor.
+ * Replaces fused_add_layernorm (sub != NULL) and fused_layernorm (sub == NULL)
+ * (add_layernorm.cuh:663-692; pybind fused_attention.cu:149-164).
+ *   x_new  = x + sub                 written when sub and x_new are non-NULL
+ *   normed = LN(x_new) * weight + bias, stored as fp32 or fp16 (normed_dtype)
+ *   row_valid (optional, [rows] uint8): rows with 0 get normed = 0
+ * All row pointers must be 16-byte aligned for the vectorised path; other
+ * alignments take a scalar path. D <= 2048.
+ */
+int dotl_layernorm(const float* x, const float* sub, const float* weight, const float* bias,
+                   float* x_new, void* normed, int normed_dtype, const uint8_t* row_valid,
+                   int64_t rows, int64_t D, float eps, void* stream);
+
+/*
+ * out[M,N] = epilogue(a[M,K] w[N,K]^T + bias[N]) with fp16 a and w, fp32
+ * accumulation on tcgen05 tensor cores. Replaces linear_bias and linear_gelu
+ * (linear_gelu.cuh:598-756; pybind fused_attention.cu:129-148).
+ *   act: 0 none, 1 exact erf GELU (applied before any residual)
+ *   resid_mode: DOTL_RESID_*; resid is fp32 [M, ldr]; row_valid [M] uint8
+ *   out_dtype: DOTL_F32 or DOTL_F16, leading dimension ldo
+ * Requirements: K % 8 == 0, lda % 8 == 0, ldw % 8 == 0, a/w 16-byte aligned
+ * (TMA), N % 8 == 0. tile_n: 0 = auto, else 128 or 256.
+ */
+int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N,
+                int64_t ldw, const float* bias, int act, const float* resid, int64_t ldr,
+                const uint8_t* row_valid, int resid_mode, void* out, int out_dtype, int64_t ldo,
+                int tile_n, void* stream);
+
+/*
+ * Flash attention forward, fp16 q/k/v, fp32 softmax, fp16 output.
+ * Replaces fused_attention_forward (attention_dispatch.cuh:332-519).
+ *   q/k/v: [B,H,S,head_dim] addressed by {batch, head, seq} element strides
+ *          (head_dim stride 1), 16-byte aligned, strides multiples of 8.
+ *   mask_kind: DOTL_MASK_*; mask strides ms[4] in elements (b, h, query, key).
+ *   causal: key j may be attended by query i only if j <= i (combinable).
+ *   out: fp16, layout 0 = [B,H,S,head_dim], 1 = [B,S,H*head_dim].
+ * Fully masked query rows are written as 0. head_dim in {32, 64, 128}.
+ */
+int dotl_attention(const void* q, const void* k, const void* v, int B, int H, int S, int head_dim,
+                   const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                   const uint8_t* mask, int mask_kind, const int64_t* mask_strides, int causal,
+                   float scale, void* out, int out_layout, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DOTL_H_ */

@@ -1,0 +1,111 @@
+"""tcgen05 GEMM with fused epilogues against a float64 reference (gpu).
+
+The reference product uses the same fp16-rounded operands, so the only
+differences are fp32 accumulation order and the output rounding: the bound is
+relative to the row's scale (sum |a||w|), 1e-5 for fp32 output and one fp16
+ulp (2^-10 relative) for fp16 output.
+"""
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+def _operands(M, N, K, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    a = torch.randn(M, K, device="cuda", generator=g).half()
+    w = (torch.randn(N, K, device="cuda", generator=g) * K ** -0.5).half()
+    b = torch.randn(N, device="cuda", generator=g) * 0.1
+    return a, w, b
+
+
+def _ref(a, w, b, act=False):
+    y = a.double() @ w.double().t() + b.double()
+    if act:
+        y = F.gelu(y, approximate="none")
+    return y
+
+
+def _scale(a, w):
+    return (a.double().abs() @ w.double().abs().t()).clamp_min(1e-3)
+
+
+@pytest.mark.parametrize("M,N,K,tile", [
+    (128, 128, 64, 128), (256, 256, 64, 256), (300, 384, 256, 0), (1, 128, 64, 0),
+    (129, 136, 72, 128), (2048, 1536, 512, 0), (512, 1024, 2048, 256), (1000, 8, 8, 128),
+    (4096, 2048, 8192, 0)])
+def test_linear_bias_f32(kernels, M, N, K, tile):
+    a, w, b = _operands(M, N, K, M + N + K)
+    out = kernels.linear_fp16(a, w, b, tile_n=tile)
+    ref = _ref(a, w, b)
+    err = ((out.double() - ref).abs() / _scale(a, w)).max().item()
+    assert err < 1e-5, err
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 1024, 256), (2048, 2048, 512), (77, 264, 128)])
+def test_linear_gelu_f16(kernels, M, N, K):
+    a, w, b = _operands(M, N, K, 11)
+    out = kernels.linear_fp16(a, w, b, act=1, out_half=True)
+    assert out.dtype == torch.float16
+    ref = _ref(a, w, b, act=True)
+    err = (out.double() - ref).abs() / (ref.abs() + 1e-2)
+    assert err.max().item() < 2 ** -10
+
+
+@pytest.mark.parametrize("mode", [1, 2, 3])
+def test_linear_residual_modes(kernels, mode):
+    M, N, K = 384, 512, 256
+    a, w, b = _operands(M, N, K, 21)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    resid = torch.randn(M, N, device="cuda", generator=g)
+    valid = torch.rand(M, device="cuda", generator=g) > 0.25
+    out = kernels.linear_fp16(a, w, b, resid=resid, row_valid=valid, resid_mode=mode)
+    proj = _ref(a, w, b)
+    if mode == 1:
+        ref = resid.double() + proj
+    elif mode == 2:
+        ref = resid.double() + proj.masked_fill(~valid[:, None], 0)
+    else:
+        ref = (resid.double() + proj).masked_fill(~valid[:, None], 0)
+    err = ((out.double() - ref).abs() / (_scale(a, w) + resid.double().abs())).max().item()
+    assert err < 1e-5, err
+    if mode == 3:
+        assert torch.all(out[~valid] == 0)
+
+
+def test_reference_named_entry_points(kernels):
+    """linear_bias / linear_gelu take fp32 x and fp32 nn.Linear weights, as upstream."""
+    g = torch.Generator(device="cuda").manual_seed(9)
+    x = torch.randn(2, 64, 256, device="cuda", generator=g)
+    w = torch.randn(512, 256, device="cuda", generator=g) * 0.05
+    b = torch.randn(512, device="cuda", generator=g) * 0.02
+    y = kernels.linear_bias(x, w, b)
+    assert y.shape == (2, 64, 512) and y.dtype == torch.float32
+    ref = x.half().double() @ w.half().double().t() + b.double()
+    assert (y.double() - ref).abs().max().item() < 1e-4
+    y16 = kernels.linear_bias(x, w, b, -1, -1, True)
+    assert y16.dtype == torch.float16
+    yg = kernels.linear_gelu(x, w, b)
+    refg = F.gelu(ref, approximate="none")
+    assert (yg.double() - refg).abs().max().item() < 1e-4
+    # deterministic: the same call gives the same bits
+    assert torch.equal(kernels.linear_bias(x, w, b), y)
+
+
+def test_rows_independent_of_m(kernels):
+    """A row's result does not depend on how many rows share the launch."""
+    a, w, b = _operands(1024, 512, 512, 5)
+    full = kernels.linear_fp16(a, w, b)
+    part = kernels.linear_fp16(a[100:357].contiguous(), w, b)
+    assert torch.equal(full[100:357], part)
+
+
+def test_gemm_rejects(kernels):
+    a, w, b = _operands(64, 64, 64, 1)
+    with pytest.raises(RuntimeError, match="multiples? of 8"):
+        kernels.linear_fp16(a[:, :60], w[:, :60], b)
+    with pytest.raises(RuntimeError, match="x's last dimension must match"):
+        kernels.linear_bias(torch.randn(4, 32, device="cuda"), torch.randn(8, 16, device="cuda"),
+                            torch.randn(8, device="cuda"))

@@ -1,0 +1,144 @@
+"""tcgen05 flash attention against the reference's own attention math (gpu).
+
+Cases are the reference's scripts/verify_kernel.py:39-55 set (shapes, causal,
+padded, causal+padded folded into a [B,1,S,S] mask) plus the packed-view
+bit-identity check (:110-129, :241-249) and the fp16 tolerance it uses for the
+tensor-core kernel (3e-3, :171-182). The reference here is
+reference_attention_f64 (:74-91): the baseline's arithmetic in float64 with
+fully masked rows mapped to 0.
+"""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+# (label, batch, heads, seq_len, head_dim, causal, padded)
+CASES = [
+    ("tiny", 1, 1, 8, 32, False, False),
+    ("tiny causal", 1, 1, 8, 32, True, False),
+    ("tiny padded", 2, 1, 8, 32, False, True),
+    ("tiny causal+pad", 2, 1, 8, 32, True, True),
+    ("default", 8, 8, 128, 64, False, False),
+    ("default causal", 8, 8, 128, 64, True, False),
+    ("default padded", 8, 8, 128, 64, False, True),
+    ("default caus+pad", 8, 8, 128, 64, True, True),
+    ("long seq", 1, 8, 2048, 64, False, False),
+    ("long seq causal", 1, 8, 2048, 64, True, False),
+    ("odd shape", 3, 5, 37, 32, True, True),
+    ("wide head_dim", 2, 4, 64, 128, False, False),
+    ("wide caus+pad", 2, 4, 128, 128, True, True),
+    ("odd hd128", 3, 2, 200, 128, True, False),
+    ("short packed", 64, 4, 32, 64, False, False),
+]
+
+TOL = 3e-3
+
+
+def reference_attention_f64(q, k, v, attn_mask, is_causal, scale):
+    q, k, v = q.double(), k.double(), v.double()
+    S = q.shape[2]
+    scores = torch.matmul(q, k.transpose(-2, -1)) * scale
+    if is_causal:
+        blocked = torch.ones(S, S, device=q.device, dtype=torch.bool).triu(1)
+        scores = scores.masked_fill(blocked, float("-inf"))
+    if attn_mask is not None:
+        scores = scores.masked_fill(~attn_mask, float("-inf"))
+    probs = torch.softmax(scores, dim=-1)
+    return torch.nan_to_num(torch.matmul(probs, v), nan=0.0)
+
+
+def build_case(b, h, s, d, causal, padded, seed=0):
+    """scripts/verify_kernel.py:93-107: padding folds causal into the mask."""
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    q = torch.randn(b, h, s, d, generator=g, device="cuda")
+    k = torch.randn(b, h, s, d, generator=g, device="cuda")
+    v = torch.randn(b, h, s, d, generator=g, device="cuda")
+    attn_mask, is_causal = None, causal
+    if padded:
+        lengths = torch.randint(1, s + 1, (b,), generator=g, device="cuda")
+        valid = torch.arange(s, device="cuda")[None, :] < lengths[:, None]
+        key_mask = valid[:, None, None, :]
+        if causal:
+            attn_mask = key_mask & torch.ones(s, s, device="cuda", dtype=torch.bool).tril()
+            is_causal = False
+        else:
+            attn_mask = key_mask.expand(b, 1, s, s).contiguous()
+    return q, k, v, attn_mask, is_causal
+
+
+def as_packed_views(q, k, v):
+    """q/k/v as strided views of one [B,S,3,H,hd] buffer (the fused QKV layout)."""
+    b, h, s, d = q.shape
+    packed = torch.empty(b, s, 3, h, d, device=q.device, dtype=q.dtype)
+    for i, t in enumerate((q, k, v)):
+        packed[:, :, i] = t.permute(0, 2, 1, 3)
+    return packed.permute(2, 0, 3, 1, 4).unbind(0)
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
+def test_attention_cases(kernels, case):
+    _, b, h, s, d, causal, padded = case
+    q, k, v, mask, is_causal = build_case(b, h, s, d, causal, padded)
+    scale = d ** -0.5
+    out = kernels.fused_attention_forward(q, k, v, mask, is_causal, scale, 0, 0, 0)
+    assert out.shape == q.shape and out.dtype == q.dtype
+    ref = reference_attention_f64(q, k, v, mask, is_causal, scale)
+    err = (out.double() - ref).abs().max().item()
+    assert err <= TOL, err
+    assert torch.isfinite(out).all()
+    # layout 1 is the same values as [B,S,H*hd]
+    out1 = kernels.fused_attention_forward(q, k, v, mask, is_causal, scale, 0, 1, 0)
+    assert torch.equal(out1, out.transpose(1, 2).reshape(b, s, h * d))
+    # The fused-QKV strided views give the same bits as contiguous inputs
+    # whenever both take the same tiling. Sequences that are a multiple of
+    # 128 long always do; shorter ones are packed several to a tile when the
+    # layout allows it (the fused buffer does, a contiguous [B,H,S,hd] with
+    # H > 1 does not), which moves keys to other tile columns and so can
+    # change the last bit of an fp32 sum.
+    q16, k16, v16 = (t.half() for t in (q, k, v))
+    qp, kp, vp = as_packed_views(q16, k16, v16)
+    a = kernels.fused_attention_forward(q16, k16, v16, mask, is_causal, scale, 0, 0, 0)
+    p = kernels.fused_attention_forward(qp, kp, vp, mask, is_causal, scale, 0, 0, 0)
+    if s % 128 == 0:
+        assert torch.equal(a, p)
+    else:
+        assert (a.float() - p.float()).abs().max().item() <= 1e-3
+
+
+def test_key_mask_with_causal_unfolded(kernels):
+    """A [B,1,1,S] key mask plus is_causal (the model's call), not folded."""
+    b, h, s, d = 3, 4, 256, 64
+    q, k, v, _, _ = build_case(b, h, s, d, False, False, seed=4)
+    lengths = torch.tensor([256, 130, 1], device="cuda")
+    valid = torch.arange(s, device="cuda")[None, :] < lengths[:, None]
+    mask = valid[:, None, None, :]
+    out = kernels.fused_attention_forward(q, k, v, mask, True, d ** -0.5, 0, 0, 0)
+    ref = reference_attention_f64(q, k, v, mask, True, d ** -0.5)
+    assert (out.double() - ref).abs().max().item() <= TOL
+
+
+def test_fully_masked_rows_are_zero(kernels):
+    b, h, s, d = 2, 2, 64, 64
+    q, k, v, _, _ = build_case(b, h, s, d, False, False, seed=5)
+    mask = torch.zeros(b, 1, 1, s, dtype=torch.bool, device="cuda")
+    mask[0, ..., :10] = True
+    out = kernels.fused_attention_forward(q, k, v, mask, False, d ** -0.5, 0, 0, 0)
+    assert torch.all(out[1] == 0)
+    ref = reference_attention_f64(q, k, v, mask, False, d ** -0.5)
+    assert (out.double() - ref).abs().max().item() <= TOL
+
+
+@pytest.mark.parametrize("hd", [8, 16, 256])
+def test_uncovered_head_dims_raise(kernels, hd):
+    q = torch.randn(1, 1, 16, hd, device="cuda")
+    with pytest.raises(RuntimeError, match="head_dim"):
+        kernels.fused_attention_forward(q, q, q, None, False, hd ** -0.5, 0, 0, 0)
+
+
+def test_uncovered_precision_raises(kernels):
+    q = torch.randn(1, 1, 16, 64, device="cuda")
+    with pytest.raises(RuntimeError, match="not covered"):
+        kernels.fused_attention_forward(q, q, q, None, False, 0.125, 1, 0, 0)
+    with pytest.raises(RuntimeError, match="not covered"):
+        kernels.fused_attention_forward(q, q, q, None, False, 0.125, 0, 0, 4)

@@ -1,0 +1,104 @@
+"""The whole layer against the oracle and the golden fixtures (gpu).
+
+The pass rule is the reference harness's (torch_transformer_benchmark.py:
+557-624): every element within 2e-3 absolute OR 2% relative of the
+reference, both finite, zero failures.
+"""
+
+import dataclasses
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+from oracle import layer as O
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 2e-3, 0.02
+
+
+def _model(cfg, seed):
+    from optimized import OptimizedTransformer
+
+    params = O.init_params(cfg, seed)
+    m = OptimizedTransformer(cfg)
+    m.load_state_dict(params, strict=True)
+    return m.cuda().eval(), params
+
+
+GOLDEN_CASES = sorted(f[:-4] for f in os.listdir(GOLDEN) if f.endswith(".npz"))
+
+
+@pytest.mark.parametrize("name", GOLDEN_CASES)
+@pytest.mark.parametrize("graph", ["off", "always"])
+def test_layer_matches_golden(kernels, name, graph):
+    from optimized import config
+
+    z = np.load(os.path.join(GOLDEN, f"{name}.npz"))
+    B, S, d, H, F, L, causal = (int(v) for v in z["cfg"])
+    cfg = O.TransformerConfig(B, S, d, H, F, L, bool(causal))
+    model, params = _model(cfg, int(z["seed"]))
+    assert abs(O.param_checksum(params) - float(z["param_checksum"])) < 1e-9
+    x = torch.from_numpy(z["x"]).cuda()
+    mask = torch.from_numpy(z["mask"]).cuda()
+    old = config.CUDA_GRAPH
+    config.CUDA_GRAPH = graph
+    try:
+        with torch.inference_mode():
+            out = model(x, mask)
+            out2 = model(x, mask)
+    finally:
+        config.CUDA_GRAPH = old
+    torch.cuda.synchronize()
+    assert torch.equal(out, out2), "two identical calls must give identical bits"
+    r = O.compare_outputs(torch.from_numpy(z["out"]), out.cpu(), rtol=RTOL, atol=ATOL)
+    assert r.passed, (r.failed_elements, r.max_abs_error, r.worst_index)
+    if graph == "always":
+        assert len(model._graphs) == 1, "graph capture declined"
+
+
+@pytest.mark.parametrize("cfg_id", [1, 2, 3, 4, 5])
+def test_baseline_configs_full_size(kernels, cfg_id):
+    """Each BASELINE config at its full size on the GPU; the oracle checks a
+    subset of batch rows (rows never interact, so a row's output does not
+    depend on the rest of the batch)."""
+    cfg, pad = O.BASELINE_CONFIGS[cfg_id]
+    model, params = _model(cfg, 1234)
+    x, mask = O.generate_random_case(cfg, 1234, pad, 1.0)
+    with torch.inference_mode():
+        out = model(x.cuda(), mask.cuda()).cpu()
+    rows = {1: 2, 2: 4, 3: 2, 4: 256, 5: 2}[cfg_id]
+    sub = dataclasses.replace(cfg, batch_size=rows)
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    ref = O.baseline_forward(params, sub, x[:rows], mask[:rows] if pad > 0 else None,
+                             query_block=256)
+    r = O.compare_outputs(ref, out[:rows], rtol=RTOL, atol=ATOL)
+    assert r.passed, (r.failed_elements, r.max_abs_error, r.worst_index)
+    assert torch.isfinite(out).all()
+    if pad > 0:
+        assert torch.all(out[~mask] == 0)
+
+
+def test_batch_rows_independent(kernels):
+    """A batch row's output is bit-identical whether it runs alone or in a batch."""
+    cfg, pad = O.BASELINE_CONFIGS[1]
+    model, _ = _model(cfg, 7)
+    x, mask = O.generate_random_case(cfg, 99, pad, 1.0)
+    x, mask = x.cuda(), mask.cuda()
+    with torch.inference_mode():
+        full = model(x, mask)
+        one = model(x[1:2].contiguous(), mask[1:2].contiguous())
+    assert torch.equal(full[1:2], one)
+
+
+def test_missing_library_raises(monkeypatch):
+    """The product path fails loudly without libdotl (no CPU or torch fallback)."""
+    import kernel_ext
+    from optimized import kernels as okernels
+
+    monkeypatch.setattr(kernel_ext, "get_kernels", lambda verbose=False: None)
+    with pytest.raises(RuntimeError, match="no fallback"):
+        okernels._custom_kernels()
