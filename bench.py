@@ -1,0 +1,545 @@
+#!/usr/bin/env python3
+"""Layer-forward throughput of the B200 build, one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
+
+A step is one forward of one BASELINE config's layer (default: config 2,
+B=4 S=512 d=512 8x64 heads FFN 2048 causal) through the public API
+`optimized.OptimizedTransformer.forward` on synthetic seeded data of that
+shape, with inputs already in HBM. Under torchrun each rank (one per GPU) runs
+its own full batch of the config (weak scaling, no data-path collective; NCCL
+is used only for the barrier and the max-over-ranks time).
+
+Timing: W warm-up steps (the first captures the CUDA graph), then exactly K
+steps, each bracketed by CUDA events on the launching stream, with a 256 MiB
+write between steps to flush the 126 MB L2 (the inputs are smaller than L2).
+`value` = tokens processed by all ranks / max over ranks of the summed step
+time. `e2e` repeats the steps with the input copied in from pinned host memory
+and the output copied back inside the timed region. `roofline` is the
+dominant kernel of the layer, timed alone with CUDA events. `cpu_baseline` is
+the reference's CPU layer (the oracle port of BaselineTransformer) on this
+host's cores, rank 0 at N=1 only.
+
+--impl reference times that CPU layer alone and prints the same JSON line
+with "impl": "reference" (rank 0 only; other ranks exit 0).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "distraction-optimizedtransformerlayer_b200")
+for _p in (REPO, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+METRIC = "layer-forward tokens/sec per config at 1/2/4/8 B200; geomean speedup vs CPU ref"
+
+# (B, S, d_model, heads, ffn, causal, padding_ratio)
+CONFIGS = {
+    1: (2, 128, 256, 4, 1024, False, 0.5),
+    2: (4, 512, 512, 8, 2048, True, 0.0),
+    3: (8, 2048, 1024, 16, 4096, False, 0.5),
+    4: (8192, 32, 256, 4, 1024, False, 0.0),
+    5: (16, 1024, 2048, 16, 8192, True, 0.0),
+}
+FLUSH_BYTES = 256 << 20
+SEED = 1234
+
+
+def _describe(cid):
+    B, S, d, H, F, causal, pad = CONFIGS[cid]
+    mask = "causal" if causal else ("key-padding, lengths U[S/2,S]" if pad > 0 else "no mask")
+    return f"cfg{cid}: B={B} S={S} d_model={d} heads={H}x{d // H} ffn={F} {mask}, 1 layer, fp32 I/O"
+
+
+class _Cfg:
+    def __init__(self, cid, layers):
+        B, S, d, H, F, causal, pad = CONFIGS[cid]
+        self.batch_size, self.seq_len, self.d_model, self.num_heads = B, S, d, H
+        self.ffn_dim, self.num_layers, self.causal, self.padding_ratio = F, layers, causal, pad
+
+
+def _synthetic_case(cfg, seed, rows):
+    """x ~ N(0,1) and a prefix key-padding mask (lengths U[round(S(1-p)), S]),
+    padded rows of x zeroed: the reference's generate_random_case
+    (torch_transformer_benchmark.py:500-540) drawn on the CPU."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    x = torch.randn(rows, cfg.seq_len, cfg.d_model, generator=g)
+    if cfg.padding_ratio <= 0:
+        return x, None
+    lo = max(1, int(round(cfg.seq_len * (1.0 - cfg.padding_ratio))))
+    lengths = torch.randint(lo, cfg.seq_len + 1, (rows,), generator=g)
+    mask = torch.arange(cfg.seq_len)[None, :] < lengths[:, None]
+    return x.masked_fill(~mask[..., None], 0), mask
+
+
+def _init_model(model, seed):
+    """The benchmark init: Xavier-uniform weights, U(-0.02,0.02) biases, LN 1/0."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            if "norm" in name:
+                p.fill_(1.0 if name.endswith("weight") else 0.0)
+            elif name.endswith("weight"):
+                bound = math.sqrt(6.0 / (p.shape[0] + p.shape[1]))
+                p.copy_((torch.rand(p.shape, generator=g) * 2 - 1) * bound)
+            else:
+                p.copy_((torch.rand(p.shape, generator=g) * 2 - 1) * 0.02)
+
+
+def _peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", 0)), "measured"
+    except Exception:  # noqa: BLE001
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# ---------------------------------------------------------------- CPU side --
+
+class _CpuLayer:
+    """The reference's CPU layer (oracle port of BaselineTransformer) on a
+    bounded sample of batch rows, sized so one forward takes about a second."""
+
+    def __init__(self, cfg):
+        from oracle import layer as O
+
+        self.O = O
+        self.threads = os.cpu_count() or 1
+        torch.set_num_threads(self.threads)
+        self.cfg = cfg
+        ocfg = O.TransformerConfig(cfg.batch_size, cfg.seq_len, cfg.d_model, cfg.num_heads,
+                                   cfg.ffn_dim, cfg.num_layers, cfg.causal)
+        self.params = O.init_params(ocfg, SEED)
+        self.qb = 256 if cfg.seq_len > 512 else 0
+        rows = cfg.batch_size
+        while True:
+            self._prepare(rows)
+            dt = self.forward_s()
+            if dt <= 1.5 or rows == 1:
+                break
+            rows = max(1, rows // 2)
+
+    def _prepare(self, rows):
+        O, cfg = self.O, self.cfg
+        self.rows = rows
+        self.sub = O.TransformerConfig(rows, cfg.seq_len, cfg.d_model, cfg.num_heads, cfg.ffn_dim,
+                                       cfg.num_layers, cfg.causal)
+        x, mask = O.generate_random_case(self.sub, SEED, cfg.padding_ratio, 1.0)
+        self.x, self.mask = x, (mask if cfg.padding_ratio > 0 else None)
+
+    def forward_s(self):
+        t0 = time.perf_counter_ns()
+        self.O.baseline_forward(self.params, self.sub, self.x, self.mask, query_block=self.qb)
+        return (time.perf_counter_ns() - t0) / 1e9
+
+    def sample(self, med, n):
+        return (f"{self.rows} of {self.cfg.batch_size} batch rows x {self.cfg.seq_len} tokens per "
+                f"forward, median of {n} fp32 CPU forwards ({med * 1e3:.1f} ms each), "
+                f"torch {torch.__version__} on {self.threads} threads")
+
+
+def _cpu_layer_tokens_per_s(cfg, budget_s=10.0):
+    layer = _CpuLayer(cfg)
+    samples = []
+    t_end = time.perf_counter() + budget_s
+    while (time.perf_counter() < t_end and len(samples) < 200) or len(samples) < 3:
+        samples.append(layer.forward_s())
+    med = statistics.median(samples)
+    return {"value": layer.rows * cfg.seq_len / med, "unit": "tokens/s", "cores": layer.threads,
+            "kind": "port", "sample": layer.sample(med, len(samples))}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return 0
+    cfg = _Cfg(args.config, args.layers)
+    layer = _CpuLayer(cfg)
+    for _ in range(args.warmup):
+        layer.forward_s()
+    per_step = [layer.forward_s() for _ in range(args.steps)]
+    med = statistics.median(per_step)
+    value = layer.rows * cfg.seq_len / med
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": med * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": _describe(args.config), "batch_per_gpu": cfg.batch_size,
+                   "seq_len": cfg.seq_len, "layers": cfg.num_layers, "device": "cpu",
+                   "step": "one fp32 CPU forward of the sample below"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": layer.threads, "kind": "port",
+                         "sample": layer.sample(med, len(per_step))},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- GPU side --
+
+class _ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled while the GPU works."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.path = tempfile.mktemp(suffix=".csv")
+        self.proc = None
+        self.gpu_index = gpu_index
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50", "-i", str(self.gpu_index)], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:  # noqa: BLE001
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:  # noqa: BLE001
+            self.proc.kill()
+        self.f.close()
+        sm, smax, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    smax.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _attention_pairs(cfg, mask):
+    """Allowed (query, key) pairs per head, summed over the batch."""
+    S = cfg.seq_len
+    if mask is not None:
+        total = 0
+        for n in (int(v) for v in mask.sum(dim=1).tolist()):
+            # every query row (padded ones too) sees keys < n, and j <= i if causal
+            total += (n * (n + 1) // 2 + (S - n) * n) if cfg.causal else S * n
+        return total
+    return cfg.batch_size * (S * (S + 1) // 2 if cfg.causal else S * S)
+
+
+def _layer_ops(model, x, mask, kernels, cfg):
+    """The kernels of one layer forward as separate calls on preallocated
+    buffers: (name, bound, algorithmic work per launch, call)."""
+    from optimized.kernels import _f32_param
+
+    B, S, d = x.shape
+    T, F, H, hd = B * S, cfg.ffn_dim, cfg.num_heads, d // cfg.num_heads
+    layer = model.layers[0]
+    use_mask = mask is not None
+    row_valid = mask.reshape(-1) if use_mask else None
+    qkv_w, qkv_b = layer.attention._get_qkv_weight()
+    n1 = kernels.layernorm_rows(x, _f32_param(layer.norm1, "weight"), _f32_param(layer.norm1, "bias"),
+                                1e-5, out_half=True)
+    qkv = kernels.linear_fp16(n1, qkv_w, qkv_b, out_half=True)
+    q, k, v = qkv.view(B, S, 3, H, hd).permute(2, 0, 3, 1, 4).unbind(0)
+    ctx = kernels.attention_packed(q, k, v, cfg.causal, hd ** -0.5, key_mask=mask)
+    x1 = kernels.linear_fp16(ctx, layer.attention.out_proj.half_weight(),
+                             _f32_param(layer.attention.out_proj, "bias"), resid=x,
+                             row_valid=row_valid, resid_mode=2 if use_mask else 1)
+    n2 = kernels.layernorm_rows(x1, _f32_param(layer.norm2, "weight"), _f32_param(layer.norm2, "bias"),
+                                1e-5, out_half=True)
+    h = kernels.linear_fp16(n2, layer.ffn_in.half_weight(), _f32_param(layer.ffn_in, "bias"), act=1,
+                            out_half=True)
+    x2 = kernels.linear_fp16(h, layer.ffn_out.half_weight(), _f32_param(layer.ffn_out, "bias"), resid=x1,
+                             row_valid=row_valid, resid_mode=3 if use_mask else 1)
+    pairs = _attention_pairs(cfg, mask.cpu() if use_mask else None)
+    ops = [
+        ("layernorm_entry", "hbm", T * d * 6,
+         lambda: kernels.layernorm_rows(x, _f32_param(layer.norm1, "weight"),
+                                        _f32_param(layer.norm1, "bias"), 1e-5, out_half=True, out=n1)),
+        ("gemm_qkv", "tensor", 2 * T * 3 * d * d,
+         lambda: kernels.linear_fp16(n1, qkv_w, qkv_b, out_half=True, out=qkv)),
+        ("attention", "tensor", 4 * hd * H * pairs,
+         lambda: kernels.attention_packed(q, k, v, cfg.causal, hd ** -0.5, key_mask=mask, out=ctx)),
+        ("gemm_out_proj_residual", "tensor", 2 * T * d * d,
+         lambda: kernels.linear_fp16(ctx, layer.attention.out_proj.half_weight(),
+                                     _f32_param(layer.attention.out_proj, "bias"), resid=x,
+                                     row_valid=row_valid, resid_mode=2 if use_mask else 1, out=x1)),
+        ("layernorm_2", "hbm", T * d * 6,
+         lambda: kernels.layernorm_rows(x1, _f32_param(layer.norm2, "weight"),
+                                        _f32_param(layer.norm2, "bias"), 1e-5, out_half=True, out=n2)),
+        ("gemm_ffn_in_gelu", "tensor", 2 * T * d * F,
+         lambda: kernels.linear_fp16(n2, layer.ffn_in.half_weight(), _f32_param(layer.ffn_in, "bias"),
+                                     act=1, out_half=True, out=h)),
+        ("gemm_ffn_out_residual", "tensor", 2 * T * F * d,
+         lambda: kernels.linear_fp16(h, layer.ffn_out.half_weight(), _f32_param(layer.ffn_out, "bias"),
+                                     resid=x1, row_valid=row_valid, resid_mode=3 if use_mask else 1,
+                                     out=x2)),
+        ("layernorm_final", "hbm", T * d * 8,
+         lambda: kernels.layernorm_rows(x2, _f32_param(model.final_norm, "weight"),
+                                        _f32_param(model.final_norm, "bias"), 1e-5, row_valid=row_valid)),
+    ]
+    return ops
+
+
+def _op_breakdown(model, x, mask, reps, kernels, cfg):
+    """Each kernel of one layer forward timed alone (CUDA events on the
+    launching stream, back to back, steady state), with its algorithmic work."""
+    ops = _layer_ops(model, x, mask, kernels, cfg)
+    stream = torch.cuda.current_stream()
+    out = []
+    for name, bound, work, fn in ops:
+        for _ in range(3):
+            fn()
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(reps):
+            fn()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1) / reps
+        out.append({"kernel": name, "bound": bound, "work": work, "ms": ms})
+    return out
+
+
+def _traffic_for(config_id, kernel):
+    path = os.path.join(REPO, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d.get(f"cfg{config_id}", {}).get(kernel)
+    except Exception:  # noqa: BLE001
+        return None
+
+
+def run_ours(args, rank, world, local_rank):
+    import kernel_ext
+    from optimized import OptimizedTransformer, config as oconfig
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+    kernels = kernel_ext.get_kernels()
+    if kernels is None:
+        raise RuntimeError(f"libdotl failed to load: {kernel_ext.load_error()}")
+    if args.no_graph:
+        oconfig.CUDA_GRAPH = "off"
+    if args.profile_kernel:
+        return _profile_kernel(args, kernels, dev)
+
+    cfg = _Cfg(args.config, args.layers)
+    model = OptimizedTransformer(cfg)
+    _init_model(model, SEED)
+    model = model.to(dev).eval()
+    x_cpu, mask_cpu = _synthetic_case(cfg, SEED + 17 * rank, cfg.batch_size)
+    x = x_cpu.to(dev)
+    mask = mask_cpu.to(dev) if mask_cpu is not None else None
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    tokens_per_rank = cfg.batch_size * cfg.seq_len
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    sampler = _ClockSampler(local_rank)
+    sampler.start()
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            model(x, mask)
+        # about a second of untimed steps so the clocks settle before timing
+        t_end = time.perf_counter() + args.settle
+        while time.perf_counter() < t_end:
+            model(x, mask)
+            torch.cuda.synchronize(dev)
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        barrier()
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            model(x, mask)
+            ends[i].record(stream)
+        barrier()
+    clocks = sampler.stop()
+    total_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+
+    # e2e: pinned host input -> forward -> pinned host output, every step
+    x_host = x_cpu.pin_memory()
+    mask_host = mask_cpu.pin_memory() if mask_cpu is not None else None
+    out_host = torch.empty(x_cpu.shape, dtype=torch.float32).pin_memory()
+    x_dev = torch.empty_like(x)
+    mask_dev = torch.empty_like(mask) if mask is not None else None
+    with torch.inference_mode():
+        for _ in range(3):
+            x_dev.copy_(x_host, non_blocking=True)
+            if mask_dev is not None:
+                mask_dev.copy_(mask_host, non_blocking=True)
+            out_host.copy_(model(x_dev, mask_dev), non_blocking=True)
+        e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        barrier()
+        for i in range(args.steps):
+            flush.zero_()
+            e_starts[i].record(stream)
+            x_dev.copy_(x_host, non_blocking=True)
+            if mask_dev is not None:
+                mask_dev.copy_(mask_host, non_blocking=True)
+            out_host.copy_(model(x_dev, mask_dev), non_blocking=True)
+            e_ends[i].record(stream)
+        barrier()
+    e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e_starts, e_ends))
+    h2d = x_cpu.numel() * 4 + (mask_cpu.numel() if mask_cpu is not None else 0)
+    d2h = x_cpu.numel() * 4
+
+    times = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    total_ms, e2e_ms = float(times[0]), float(times[1])
+
+    breakdown = None
+    if rank == 0:
+        with torch.inference_mode():
+            breakdown = _op_breakdown(model, x, mask, max(20, min(args.steps, 200)), kernels, cfg)
+    word = kernels.device_error(clear=True)
+    if word:
+        raise RuntimeError(f"device error word {word:#x} after the timed run")
+
+    if rank == 0:
+        hbm, tflops, _tsus, peak_kind = _peaks()
+        dom = max(breakdown, key=lambda r: r["ms"])
+        if dom["bound"] == "tensor":
+            achieved = dom["work"] / (dom["ms"] / 1e3) / 1e12
+            peak, unit = tflops, "TFLOP/s"
+        else:
+            achieved = dom["work"] / (dom["ms"] / 1e3) / 1e9
+            peak, unit = hbm, "GB/s"
+        launches_per_step = 1 + 7 * cfg.num_layers
+        value = world * tokens_per_rank * args.steps / (total_ms / 1e3)
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+            "data": "synthetic",
+            "config": {"workload": _describe(args.config), "batch_per_gpu": cfg.batch_size,
+                       "global_batch": cfg.batch_size * world, "seq_len": cfg.seq_len,
+                       "layers": cfg.num_layers, "parallelism": f"dp{world}",
+                       "l2": "flushed between steps (256 MiB write); inputs smaller than L2",
+                       "cuda_graph": oconfig.CUDA_GRAPH != "off",
+                       "arithmetic": "fp16 tensor-core operands, fp32 accumulate, fp32 I/O and LN"},
+            "clocks": clocks,
+            "e2e": {"value": world * tokens_per_rank * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches_per_step * args.steps,
+            "roofline": {"kernel": dom["kernel"], "bound": "tensor" if dom["bound"] == "tensor" else "hbm",
+                         "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
+                         "peak_source": f"{peak_kind} ({'bf16_tflops burst' if unit == 'TFLOP/s' else 'hbm_gbs'})",
+                         "traffic": _traffic_for(args.config, dom["kernel"])},
+            "kernels": [{"kernel": r["kernel"], "us": round(r["ms"] * 1e3, 2),
+                         ("tflops" if r["bound"] == "tensor" else "gbs"):
+                             round(r["work"] / (r["ms"] / 1e3) / (1e12 if r["bound"] == "tensor" else 1e9), 1)}
+                        for r in breakdown],
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = _cpu_layer_tokens_per_s(cfg, budget_s=10.0)
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        model.release_graphs()
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def _profile_kernel(args, kernels, dev):
+    """Runs one kernel of the layer 3 times inside the NVTX range
+    "dotl_profile" (for ncu --nvtx --nvtx-include dotl_profile/), nothing else
+    timed."""
+    from optimized import OptimizedTransformer
+
+    cfg = _Cfg(args.config, args.layers)
+    model = OptimizedTransformer(cfg)
+    _init_model(model, SEED)
+    model = model.to(dev).eval()
+    x_cpu, mask_cpu = _synthetic_case(cfg, SEED, cfg.batch_size)
+    x = x_cpu.to(dev)
+    mask = mask_cpu.to(dev) if mask_cpu is not None else None
+    with torch.inference_mode():
+        ops = {name: fn for name, _b, _w, fn in _layer_ops(model, x, mask, kernels, cfg)}
+        if args.profile_kernel not in ops:
+            raise SystemExit(f"--profile-kernel must be one of {sorted(ops)}")
+        torch.cuda.synchronize(dev)
+        torch.cuda.nvtx.range_push("dotl_profile")
+        for _ in range(3):
+            ops[args.profile_kernel]()
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize(dev)
+    print(f"profiled {args.profile_kernel} x3 on {_describe(args.config)}")
+    return 0
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
+    ap.add_argument("--layers", type=int, default=1)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-graph", action="store_true", help="time the eager path (no CUDA graph)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--settle", type=float, default=1.0, help="seconds of untimed steps before timing")
+    ap.add_argument("--profile-kernel", default=None,
+                    help="run only this kernel of the layer 3x in an NVTX range (for ncu)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank)
+    if world != args.gpus:
+        print(f"[bench] note: --gpus {args.gpus} but WORLD_SIZE={world}; using {world}", file=sys.stderr)
+    return run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

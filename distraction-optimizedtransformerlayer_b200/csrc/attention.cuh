@@ -1,31 +1,39 @@
 // Flash attention forward on the 5th-generation tensor cores.
 //
 // Replaces the reference's wmma flash-attention kernel
-// (csrc/attention_wmma.cuh:874-1770) and its launcher
-// (attention_dispatch.cuh:332-519). Same contract: softmax(q k^T * scale +
-// masks) v per (batch, head), fp16 operands, fp32 softmax and accumulation in
-// the exp2 domain, causal and key-padding masks combinable, fully masked rows
-// written as 0, output in [B,H,S,hd] (layout 0) or [B,S,H*hd] (layout 1).
+// (csrc/attention_wmma.cuh:874-1770), its split-KV combine (:1783-1826) and its
+// launcher (attention_dispatch.cuh:332-519). Same contract: softmax(q k^T *
+// scale + masks) v per (batch, head), fp16 operands, fp32 softmax and
+// accumulation in the exp2 domain, causal and key masks combinable, fully
+// masked rows written as 0, output [B,H,S,hd] (layout 0) or [B,S,H*hd]
+// (layout 1).
 //
-// Design (sm_100a), one CTA per SM, persistent over work items
-// (head, 128-row query tile), largest causal tiles first:
-//   warp 0      TMA producer: the Q tile once per item, then K and V tiles
-//               (128 keys each) into a STAGES-deep ring, 128B/64B swizzled;
-//   warp 1      MMA issuer: S(j) = Q K(j)^T into one of two TMEM S buffers
-//               (M=128, N=128, K=hd), then PV(j) = P(j) V(j) into one of two
-//               TMEM partial-O buffers (M=128, N=hd, K=128 keys);
-//   warps 2-5   softmax: each thread owns one query row, reads its 128 scores
-//               from TMEM, applies scale, causal / segment / key masks,
-//               online max and sum in the exp2 domain, writes P(j) as fp16
-//               into swizzled smem for the PV MMA, and folds PV(j-1) into its
-//               register-resident O with the running correction factor.
-// The score matrix never leaves TMEM/SMEM. Key tiles past the causal
-// diagonal or past a query tile's segment are never loaded.
+// Design (sm_100a): one CTA per SM, persistent over work items (stream, 128-row
+// query tile), largest causal tiles first. Ten warps:
+//   warp 0      producer: publishes each item's key-tile count (after scanning
+//               a per-key mask for its last valid key), loads the Q tile and
+//               the K/V tiles (128 keys each) into a STAGES-deep ring by TMA;
+//   warp 1      MMA issuer: S(j) = Q K(j)^T into the TMEM S region of the
+//               softmax warpgroup that owns tile j (even tiles: group 0, odd:
+//               group 1), then O_g += P(j) V(j) with P read from TMEM (the
+//               tcgen05 "TS" form), O_g accumulating in TMEM;
+//   warps 2-5   softmax group 0, warps 6-9 softmax group 1: each thread owns
+//               one query row, loads its 128 scores from TMEM in one pass,
+//               masks (only on boundary tiles), takes the row max, rescales
+//               its O row in TMEM only when the max grew by more than 2^8
+//               (the stale max is exact: numerator and denominator share it),
+//               writes P = exp2(s*c - m*c) as fp16 over its S columns, and
+//               keeps the row sum. Group 1 hands (max, sum) to group 0, which
+//               merges the two partial outputs and stores the row.
+// Splitting one query tile's keys between two groups lets their softmax
+// phases interleave on each SM sub-partition while the tensor core runs the
+// other group's MMAs, and keeps 128-row tiles (the most CTAs) for small
+// problems. The score matrix never leaves TMEM.
 //
-// "Packed" mode runs the query/key tiles over the flat token axis
-// (b * S + s), so short sequences (S < 128) share one 128-row tile; a row's
-// keys are confined to its own sequence by an interval test. It needs
-// batch stride == S * sequence stride, which the fused QKV buffer has.
+// "Packed" mode runs the tiles over the flat token axis (b * S + s), so short
+// sequences share one 128-row tile; a row's keys are confined to its own
+// sequence by an interval test. It needs batch stride == S * sequence stride,
+// which the fused QKV buffer has.
 
 #pragma once
 
@@ -33,14 +41,15 @@
 
 namespace dotl {
 
-constexpr int kAttnThreads = 192;
-constexpr int kAttnTile = 128;   // query rows per tile and keys per key tile
+constexpr int kAttnThreads = 320;
+constexpr int kAttnTile = 128;          // query rows per tile and keys per key tile
+constexpr float kRescaleLog2 = 8.0f;    // lazy-rescale threshold, in log2 units
 
 struct AttnParams {
     int B, H, S;
     int packed;          // tiles over the flat token axis
     int rows_total;      // packed: B*S; else S
-    int num_q_tiles;     // per (head[, batch]) stream
+    int num_q_tiles;     // per stream
     int num_streams;     // packed: H; else B*H
     int causal;
     float scale_log2;    // scale * log2(e)
@@ -70,24 +79,28 @@ struct AttnSmem {
     static constexpr uint32_t kBlkBytes = kAttnTile * kRowBytes;
     static constexpr uint32_t kTileBytes = kNumBlk * kBlkBytes; // one Q/K/V tile
     static constexpr uint32_t kSwz = kRowBytes == 128 ? kSwizzle128 : kSwizzle64;
-    static constexpr uint32_t kPBytes = kAttnTile * kAttnTile * 2;
     static constexpr uint32_t kOffQ = 0;
     static constexpr uint32_t kOffK = kOffQ + kTileBytes;
     static constexpr uint32_t kOffV = kOffK + STAGES * kTileBytes;
-    static constexpr uint32_t kOffP = kOffV + STAGES * kTileBytes;
-    static constexpr uint32_t kOffBar = kOffP + 2 * kPBytes;
+    static constexpr uint32_t kOffComb = kOffV + STAGES * kTileBytes;   // 128 x (max, sum) of group 1
+    static constexpr uint32_t kOffInfo = kOffComb + kAttnTile * 8;      // 2 item slots
+    static constexpr uint32_t kOffBar = kOffInfo + 16;
     // q_full, q_empty, k_full[ST], v_full[ST], kv_empty[ST], s_full[2],
-    // s_empty[2], p_full[2], o_full[2], o_empty[2], drain
-    static constexpr uint32_t kNumBars = 2 + 3 * STAGES + 10 + 1;
+    // p_full[2], o_done[2], o_free, comb_full, comb_empty, info_full[2],
+    // info_empty[2], drain
+    static constexpr uint32_t kNumBars = 2 + 3 * STAGES + 6 + 3 + 4 + 1;
     static constexpr uint32_t kOffSlot = kOffBar + kNumBars * 8;
     static constexpr uint32_t kOffAbort = kOffSlot + 4;
     static constexpr uint32_t kBytes = kOffAbort + 4;
     static constexpr uint32_t kAlloc = kBytes + 1024;
-    static constexpr uint32_t kTmemCols = 512;    // S[2] at 0/128, O[2] at 256/256+HD
+    static constexpr uint32_t kTmemCols = 512;
+    // TMEM columns: S/P of group g at 128 g, O of group g at 256 + HD g.
+    static constexpr uint32_t kColS = 0;
+    static constexpr uint32_t kColO = 256;
 };
 
-// Item -> (stream, query tile) with the query-tile index descending in the
-// slowest position: under causal masking the longest tiles go first.
+// Item -> (stream, query tile), query-tile index descending in the slowest
+// position: under causal masking the longest tiles go first.
 __device__ __forceinline__ void attn_item(const AttnParams& p, int item, int& stream, int& qt) {
     const int tile_rank = item / p.num_streams;
     stream = item - tile_rank * p.num_streams;
@@ -107,6 +120,19 @@ __device__ __forceinline__ void attn_key_range(const AttnParams& p, int qt, int&
     }
 }
 
+// One past the last key of sequence b the per-key mask allows (0 if none).
+// Warp-collective; scans backwards 32 keys at a time.
+__device__ __forceinline__ int attn_last_valid_key(const AttnParams& p, int b, int lane) {
+    const uint8_t* base = p.mask + static_cast<int64_t>(b) * p.ms0;
+    for (int hi = p.S; hi > 0; hi -= 32) {
+        const int k = hi - 1 - lane;
+        const bool v = k >= 0 && base[static_cast<int64_t>(k) * p.ms3] != 0;
+        const uint32_t bits = __ballot_sync(0xffffffffu, v);
+        if (bits) return hi - (__ffs(bits) - 1);
+    }
+    return 0;
+}
+
 template <int HD, int STAGES>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
@@ -121,14 +147,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     auto k_full = [&](int s) { return bar0 + 8u * (2 + s); };
     auto v_full = [&](int s) { return bar0 + 8u * (2 + STAGES + s); };
     auto kv_empty = [&](int s) { return bar0 + 8u * (2 + 2 * STAGES + s); };
-    auto s_full = [&](int b) { return bar0 + 8u * (2 + 3 * STAGES + b); };
-    auto s_empty = [&](int b) { return bar0 + 8u * (4 + 3 * STAGES + b); };
-    auto p_full = [&](int b) { return bar0 + 8u * (6 + 3 * STAGES + b); };
-    auto o_full = [&](int b) { return bar0 + 8u * (8 + 3 * STAGES + b); };
-    auto o_empty = [&](int b) { return bar0 + 8u * (10 + 3 * STAGES + b); };
-    const uint32_t drain_bar = bar0 + 8u * (12 + 3 * STAGES);
+    auto s_full = [&](int g) { return bar0 + 8u * (2 + 3 * STAGES + g); };
+    auto p_full = [&](int g) { return bar0 + 8u * (4 + 3 * STAGES + g); };
+    auto o_done = [&](int g) { return bar0 + 8u * (6 + 3 * STAGES + g); };
+    const uint32_t o_free = bar0 + 8u * (8 + 3 * STAGES);
+    const uint32_t comb_full = bar0 + 8u * (9 + 3 * STAGES);
+    const uint32_t comb_empty = bar0 + 8u * (10 + 3 * STAGES);
+    auto info_full = [&](int s) { return bar0 + 8u * (11 + 3 * STAGES + s); };
+    auto info_empty = [&](int s) { return bar0 + 8u * (13 + 3 * STAGES + s); };
+    const uint32_t drain_bar = bar0 + 8u * (15 + 3 * STAGES);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffAbort);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffSlot);
+    volatile int* info = reinterpret_cast<volatile int*>(smem + L::kOffInfo);
+    float2* comb = reinterpret_cast<float2*>(smem + L::kOffComb);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -141,13 +172,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             mbar_init(v_full(s), 1);
             mbar_init(kv_empty(s), 1);
         }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(s_full(b), 1);
-            mbar_init(s_empty(b), 128);
-            mbar_init(p_full(b), 128);
-            mbar_init(o_full(b), 1);
-            mbar_init(o_empty(b), 128);
+        for (int g = 0; g < 2; ++g) {
+            mbar_init(s_full(g), 1);
+            mbar_init(p_full(g), 128);
+            mbar_init(o_done(g), 1);
+            mbar_init(info_full(g), 1);
+            mbar_init(info_empty(g), 1 + 8);
         }
+        mbar_init(o_free, 128);
+        mbar_init(comb_full, 128);
+        mbar_init(comb_empty, 128);
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
         fence_barrier_init();
@@ -164,11 +198,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const int num_items = p.num_streams * p.num_q_tiles;
+    const bool scan_mask = p.mask_kind == 1 && !p.packed;
 
-    if (warp == 0 && lane == 0) {
-        // ---------------------------------------------------- TMA producer --
-        uint32_t tcount = 0;     // key tiles issued, across items
-        uint32_t icount = 0;     // items issued
+    if (warp == 0) {
+        // ------------------------------------------------------- producer --
+        uint32_t tcount = 0, qcount = 0, icount = 0;
         int k_issued_phase[STAGES];
         for (int s = 0; s < STAGES; ++s) k_issued_phase[s] = -1;
         int q_issued = -1;
@@ -178,34 +212,51 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             attn_key_range(p, qt, k_lo, k_hi);
             const int h = p.packed ? stream : stream % p.H;
             const int bq = p.packed ? 0 : stream / p.H;
-            if (!mbar_wait(q_empty, (icount & 1u) ^ 1u, abort_flag)) goto producer_done;
-            mbar_arrive_expect_tx(q_full, L::kTileBytes);
+            if (scan_mask) k_hi = min(k_hi, attn_last_valid_key(p, bq, lane));
+            const int n_kt = k_hi > k_lo ? (k_hi - k_lo + kAttnTile - 1) / kAttnTile : 0;
+            bool ok = true;
+            if (lane == 0) {
+                const int slot = static_cast<int>(icount & 1u);
+                ok = mbar_wait(info_empty(slot), ((icount >> 1) & 1u) ^ 1u, abort_flag);
+                if (ok) {
+                    info[slot] = n_kt;
+                    mbar_arrive(info_full(slot));
+                }
+                if (ok && n_kt > 0) {
+                    ok = mbar_wait(q_empty, (qcount & 1u) ^ 1u, abort_flag);
+                    if (ok) {
+                        mbar_arrive_expect_tx(q_full, L::kTileBytes);
 #pragma unroll
-            for (int cb = 0; cb < L::kNumBlk; ++cb)
-                attn_tma(sbase + L::kOffQ + cb * L::kBlkBytes, &tmap_q, q_full, cb * L::kBlkCols,
-                         qt * kAttnTile, h, bq, p.head_inner & 1);
-            q_issued = static_cast<int>(icount & 1u);
-            const int n_kt = (k_hi - k_lo + kAttnTile - 1) / kAttnTile;
-            for (int j = 0; j < n_kt; ++j, ++tcount) {
-                const int st = static_cast<int>(tcount % STAGES);
-                const uint32_t ph = (tcount / STAGES) & 1u;
-                const int kc0 = k_lo + j * kAttnTile;
-                if (!mbar_wait(kv_empty(st), ph ^ 1u, abort_flag)) goto producer_done;
-                mbar_arrive_expect_tx(k_full(st), L::kTileBytes);
+                        for (int cb = 0; cb < L::kNumBlk; ++cb)
+                            attn_tma(sbase + L::kOffQ + cb * L::kBlkBytes, &tmap_q, q_full,
+                                     cb * L::kBlkCols, qt * kAttnTile, h, bq, p.head_inner & 1);
+                        q_issued = static_cast<int>(qcount & 1u);
+                    }
+                }
+                for (int j = 0; ok && j < n_kt; ++j, ++tcount) {
+                    const int st = static_cast<int>(tcount % STAGES);
+                    const uint32_t ph = (tcount / STAGES) & 1u;
+                    const int kc0 = k_lo + j * kAttnTile;
+                    ok = mbar_wait(kv_empty(st), ph ^ 1u, abort_flag);
+                    if (!ok) break;
+                    mbar_arrive_expect_tx(k_full(st), L::kTileBytes);
 #pragma unroll
-                for (int cb = 0; cb < L::kNumBlk; ++cb)
-                    attn_tma(sbase + L::kOffK + st * L::kTileBytes + cb * L::kBlkBytes, &tmap_k,
-                             k_full(st), cb * L::kBlkCols, kc0, h, bq, p.head_inner & 2);
-                mbar_arrive_expect_tx(v_full(st), L::kTileBytes);
+                    for (int cb = 0; cb < L::kNumBlk; ++cb)
+                        attn_tma(sbase + L::kOffK + st * L::kTileBytes + cb * L::kBlkBytes, &tmap_k,
+                                 k_full(st), cb * L::kBlkCols, kc0, h, bq, p.head_inner & 2);
+                    mbar_arrive_expect_tx(v_full(st), L::kTileBytes);
 #pragma unroll
-                for (int cb = 0; cb < L::kNumBlk; ++cb)
-                    attn_tma(sbase + L::kOffV + st * L::kTileBytes + cb * L::kBlkBytes, &tmap_v,
-                             v_full(st), cb * L::kBlkCols, kc0, h, bq, p.head_inner & 4);
-                k_issued_phase[st] = static_cast<int>(ph);
+                    for (int cb = 0; cb < L::kNumBlk; ++cb)
+                        attn_tma(sbase + L::kOffV + st * L::kTileBytes + cb * L::kBlkBytes, &tmap_v,
+                                 v_full(st), cb * L::kBlkCols, kc0, h, bq, p.head_inner & 4);
+                    k_issued_phase[st] = static_cast<int>(ph);
+                }
             }
+            if (n_kt > 0) ++qcount;
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (!ok) break;
         }
-    producer_done:
-        if (*abort_flag) {
+        if (lane == 0 && *abort_flag) {
             if (q_issued >= 0) mbar_wait_drain(q_full, static_cast<uint32_t>(q_issued));
             for (int s = 0; s < STAGES; ++s) {
                 if (k_issued_phase[s] >= 0) {
@@ -215,86 +266,94 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             }
         }
     } else if (warp == 1 && lane == 0) {
-        // ------------------------------------------------------ MMA issuer --
+        // ---------------------------------------------------- MMA issuer --
         constexpr uint32_t idesc_s = idesc_f16_f32(kAttnTile, kAttnTile, false, false);
         constexpr uint32_t idesc_o = idesc_f16_f32(kAttnTile, HD, false, true);
         constexpr int kStepsPerBlk = L::kBlkCols / 16;
-        uint32_t tcount = 0;
-        uint32_t icount = 0;
+        uint32_t tcount = 0, qcount = 0, icount = 0;
+        uint32_t gcount[2] = {0, 0};
         for (int item = blockIdx.x; item < num_items; item += gridDim.x, ++icount) {
-            int stream, qt, k_lo, k_hi;
-            attn_item(p, item, stream, qt);
-            attn_key_range(p, qt, k_lo, k_hi);
-            const int n_kt = (k_hi - k_lo + kAttnTile - 1) / kAttnTile;
-            if (!mbar_wait(q_full, icount & 1u, abort_flag)) goto mma_done;
+            const int slot = static_cast<int>(icount & 1u);
+            if (!mbar_wait(info_full(slot), (icount >> 1) & 1u, abort_flag)) break;
+            const int n_kt = info[slot];
+            mbar_arrive(info_empty(slot));
+            if (n_kt == 0) continue;
+            if (!mbar_wait(q_full, qcount & 1u, abort_flag)) break;
             tc_fence_after();
-            // S(j) = Q K(j)^T for global tile index t
-            auto issue_s = [&](uint32_t t) -> bool {
+            // S(j) = Q K(j)^T into group (j & 1)'s S region.
+            auto issue_s = [&](int j) -> bool {
+                const uint32_t t = tcount + j;
                 const int st = static_cast<int>(t % STAGES);
-                const int sb = static_cast<int>(t & 1u);
                 if (!mbar_wait(k_full(st), (t / STAGES) & 1u, abort_flag)) return false;
-                if (!mbar_wait(s_empty(sb), ((t >> 1) & 1u) ^ 1u, abort_flag)) return false;
                 tc_fence_after();
-                const uint32_t d = tmem_base + static_cast<uint32_t>(sb * kAttnTile);
+                const uint32_t d = tmem_base + L::kColS + static_cast<uint32_t>((j & 1) * kAttnTile);
                 const uint32_t qa = sbase + L::kOffQ;
                 const uint32_t ka = sbase + L::kOffK + st * L::kTileBytes;
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; ++kk) {
                     const uint32_t off = (kk / kStepsPerBlk) * L::kBlkBytes + (kk % kStepsPerBlk) * 32;
-                    const uint64_t ad = smem_desc(qa + off, 16, 8 * L::kRowBytes, L::kSwz);
-                    const uint64_t bd = smem_desc(ka + off, 16, 8 * L::kRowBytes, L::kSwz);
-                    mma_f16_ss(d, ad, bd, idesc_s, kk != 0 ? 1u : 0u);
+                    mma_f16_ss(d, smem_desc(qa + off, 16, 8 * L::kRowBytes, L::kSwz),
+                               smem_desc(ka + off, 16, 8 * L::kRowBytes, L::kSwz), idesc_s, kk != 0 ? 1u : 0u);
                 }
-                tc_commit(s_full(sb));
+                tc_commit(s_full(j & 1));
+                if (j == n_kt - 1) tc_commit(q_empty);   // Q is no longer read
                 return true;
             };
-            if (!issue_s(tcount)) goto mma_done;
-            if (n_kt == 1) tc_commit(q_empty);
-            for (int j = 0; j < n_kt; ++j) {
+            bool ok = issue_s(0);
+            if (ok && n_kt > 1) ok = issue_s(1);
+            for (int j = 0; ok && j < n_kt; ++j) {
+                const int g = j & 1;
                 const uint32_t t = tcount + j;
-                if (j + 1 < n_kt) {
-                    if (!issue_s(t + 1)) goto mma_done;
-                    if (j + 2 == n_kt) tc_commit(q_empty);   // Q is no longer read
-                }
                 const int st = static_cast<int>(t % STAGES);
-                const int b = static_cast<int>(t & 1u);
-                const uint32_t use = (t >> 1) & 1u;
-                if (!mbar_wait(p_full(b), use, abort_flag)) goto mma_done;
-                if (!mbar_wait(v_full(st), (t / STAGES) & 1u, abort_flag)) goto mma_done;
-                if (!mbar_wait(o_empty(b), use ^ 1u, abort_flag)) goto mma_done;
+                // the previous item's epilogue has read both O accumulators
+                if (j == 0 && !mbar_wait(o_free, (qcount & 1u) ^ 1u, abort_flag)) { ok = false; break; }
+                if (!mbar_wait(p_full(g), gcount[g] & 1u, abort_flag)) { ok = false; break; }
+                if (!mbar_wait(v_full(st), (t / STAGES) & 1u, abort_flag)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t d = tmem_base + 2u * kAttnTile + static_cast<uint32_t>(b * HD);
-                const uint32_t pa = sbase + L::kOffP + b * L::kPBytes;
+                const uint32_t d = tmem_base + L::kColO + static_cast<uint32_t>(g * HD);
+                const uint32_t pa = tmem_base + L::kColS + static_cast<uint32_t>(g * kAttnTile);
                 const uint32_t va = sbase + L::kOffV + st * L::kTileBytes;
 #pragma unroll
-                for (int kk = 0; kk < kAttnTile / 16; ++kk) {
-                    const uint64_t ad = smem_desc(pa + (kk / 4) * (kAttnTile * 128) + (kk % 4) * 32, 16,
-                                                  1024, kSwizzle128);
-                    const uint64_t bd = smem_desc(va + kk * 16 * L::kRowBytes, L::kBlkBytes,
-                                                  8 * L::kRowBytes, L::kSwz);
-                    mma_f16_ss(d, ad, bd, idesc_o, kk != 0 ? 1u : 0u);
-                }
-                tc_commit(o_full(b));
+                for (int kk = 0; kk < kAttnTile / 16; ++kk)
+                    mma_f16_ts(d, pa + kk * 8, smem_desc(va + kk * 16 * L::kRowBytes, L::kBlkBytes,
+                                                         8 * L::kRowBytes, L::kSwz),
+                               idesc_o, (j >= 2 || kk != 0) ? 1u : 0u);
+                tc_commit(o_done(g));
                 tc_commit(kv_empty(st));
+                ++gcount[g];
+                if (j + 2 < n_kt && !issue_s(j + 2)) { ok = false; break; }
             }
+            if (!ok) break;
             tcount += n_kt;
+            ++qcount;
         }
-    mma_done:
         tc_commit(drain_bar);
         mbar_wait_drain(drain_bar, 0);
     } else if (warp >= 2) {
-        // --------------------------------------------- softmax + epilogue --
+        // ------------------------------------------ softmax warpgroups --
+        const int grp = (warp - 2) >> 2;               // 0: even key tiles, 1: odd
         const int quarter = warp & 3;
-        const int row = quarter * 32 + lane;           // query row within the tile
+        const int row = quarter * 32 + lane;            // query row within the tile
         const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-        uint32_t tcount = 0;
-        for (int item = blockIdx.x; item < num_items; item += gridDim.x) {
+        const uint32_t t_s = tmem_base + lane_off + L::kColS + static_cast<uint32_t>(grp * kAttnTile);
+        const uint32_t t_o0 = tmem_base + lane_off + L::kColO;
+        const uint32_t t_o = t_o0 + static_cast<uint32_t>(grp * HD);
+        const float c = p.scale_log2;
+        uint32_t gtiles = 0, icount = 0, ocount = 0, ccount = 0;
+        bool alive = true;
+        for (int item = blockIdx.x; item < num_items && alive; item += gridDim.x, ++icount) {
+            const int slot = static_cast<int>(icount & 1u);
+            bool ok = mbar_wait(info_full(slot), (icount >> 1) & 1u, abort_flag);
+            if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
+            const int n_kt = info[slot];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(info_empty(slot));
+
             int stream, qt, k_lo, k_hi;
             attn_item(p, item, stream, qt);
             attn_key_range(p, qt, k_lo, k_hi);
-            const int n_kt = (k_hi - k_lo + kAttnTile - 1) / kAttnTile;
             const int h = p.packed ? stream : stream % p.H;
-            const int rq = qt * kAttnTile + row;       // map row coordinate
+            const int rq = qt * kAttnTile + row;
             const bool q_ok = rq < p.rows_total;
             int b, s, klo_r, khi_r;
             if (p.packed) {
@@ -316,152 +375,219 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             if (p.mask_kind == 2 && q_ok)
                 mrow = p.mask + b * p.ms0 + h * p.ms1 + static_cast<int64_t>(s) * p.ms2;
 
-            float o[HD];
-#pragma unroll
-            for (int i = 0; i < HD; ++i) o[i] = 0.0f;
-            float m_run = -INFINITY, l_run = 0.0f, alpha_prev = 1.0f;
-
-            // Folds PV(t) into o with the correction factor of its step.
-            auto accumulate = [&](uint32_t t, float alpha) -> bool {
-                const int ob = static_cast<int>(t & 1u);
-                bool ok = mbar_wait(o_full(ob), (t >> 1) & 1u, abort_flag);
-                ok = __all_sync(0xffffffffu, ok);
-                if (!ok) return false;
-                tc_fence_after();
-                const uint32_t ta = tmem_base + lane_off + 2u * kAttnTile + static_cast<uint32_t>(ob * HD);
-#pragma unroll
-                for (int c = 0; c < HD; c += 32) {
-                    uint32_t r[32];
-                    tmem_ld_32x32b_x32(ta + c, r);
-                    tmem_ld_wait(r);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) o[c + i] = fmaf(o[c + i], alpha, __uint_as_float(r[i]));
-                }
-                tc_fence_before();
-                mbar_arrive(o_empty(ob));
-                return true;
-            };
-
-            bool alive = true;
-            for (int j = 0; j < n_kt && alive; ++j) {
-                const uint32_t t = tcount + j;
-                const int sb = static_cast<int>(t & 1u);
+            float m_used = -INFINITY, l_run = 0.0f;
+            int mine = 0;
+            for (int j = grp; j < n_kt; j += 2, ++mine, ++gtiles) {
                 const int kc0 = k_lo + j * kAttnTile;
-                // Per-key mask bits for this tile, identical for every row:
-                // bits[q] bit i  <->  key kc0 + 4 i + q.
-                uint32_t kbits[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
+                // Allowed keys of this row in this tile as a 128-bit mask:
+                // bit i of allow[w] <-> key column 32 w + i.
+                uint32_t allow[4];
+#pragma unroll
+                for (int w = 0; w < 4; ++w) {
+                    // the row's key interval [klo_r, khi_r] clipped to this word
+                    const int a = max(klo_r - kc0 - 32 * w, 0);
+                    const int z = min(khi_r - kc0 - 32 * w, 31);
+                    uint32_t bits = 0u;
+                    if (a <= z) bits = (z == 31 ? 0xffffffffu : ((1u << (z + 1)) - 1u)) & ~((1u << a) - 1u);
+                    allow[w] = bits;
+                }
                 if (p.mask_kind == 1) {
 #pragma unroll
-                    for (int q4 = 0; q4 < 4; ++q4) {
-                        const int kc = kc0 + 4 * lane + q4;
+                    for (int w = 0; w < 4; ++w) {
+                        const int kc = kc0 + 32 * w + lane;
                         bool allowed = false;
                         if (kc < p.rows_total) {
-                            int bk = b, sk = kc;
+                            int bk, sk;
                             if (p.packed) {
                                 bk = kc / p.S;
                                 sk = kc - bk * p.S;
                             } else {
                                 bk = stream / p.H;
+                                sk = kc;
                             }
                             allowed = p.mask[bk * p.ms0 + static_cast<int64_t>(sk) * p.ms3] != 0;
                         }
-                        kbits[q4] = __ballot_sync(0xffffffffu, allowed);
+                        allow[w] &= __ballot_sync(0xffffffffu, allowed);
+                    }
+                } else if (p.mask_kind == 2) {
+#pragma unroll 1
+                    for (int i = 0; i < kAttnTile; ++i) {
+                        const int kc = kc0 + i;
+                        if (((allow[i >> 5] >> (i & 31)) & 1u) && mrow[static_cast<int64_t>(kc - klo_r) * p.ms3] == 0)
+                            allow[i >> 5] &= ~(1u << (i & 31));
                     }
                 }
-                const bool interior = p.mask_kind == 0 && kc0 >= klo_r && kc0 + kAttnTile - 1 <= khi_r;
+                const bool interior = (allow[0] & allow[1] & allow[2] & allow[3]) == 0xffffffffu;
 
-                bool ok = mbar_wait(s_full(sb), (t >> 1) & 1u, abort_flag);
-                ok = __all_sync(0xffffffffu, ok);
-                if (!ok) { alive = false; break; }
+                ok = mbar_wait(s_full(grp), gtiles & 1u, abort_flag);
+                if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
                 tc_fence_after();
-                const uint32_t ts = tmem_base + lane_off + static_cast<uint32_t>(sb * kAttnTile);
-
-                auto allowed_at = [&](int c) -> bool {
-                    if (interior) return true;
-                    const int kc = kc0 + c;
-                    bool a = kc >= klo_r && kc <= khi_r;
-                    if (p.mask_kind == 1) a = a && ((kbits[c & 3] >> (c >> 2)) & 1u);
-                    if (p.mask_kind == 2) a = a && mrow[static_cast<int64_t>(kc - klo_r) * p.ms3] != 0;
-                    return a;
-                };
-
-                // pass 1: row max of the allowed raw scores
-                float mx = -INFINITY;
+                // pass 1: row max over two 64-column halves, eight independent chains
+                float mx8[8];
 #pragma unroll
-                for (int c0 = 0; c0 < kAttnTile; c0 += 32) {
-                    uint32_t r[32];
-                    tmem_ld_32x32b_x32(ts + c0, r);
-                    tmem_ld_wait(r);
+                for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
 #pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (allowed_at(c0 + i)) mx = fmaxf(mx, __uint_as_float(r[i]));
-                }
-                const float m_new = fmaxf(m_run, mx);
-                const float m_scaled = (m_new == -INFINITY) ? 0.0f : m_new * p.scale_log2;
-                const float alpha = (m_run == -INFINITY) ? 0.0f : fast_exp2(m_run * p.scale_log2 - m_scaled);
-
-                // pass 2: p = exp2(s*c - m*c), row sum, P as fp16 into swizzled smem
-                uint8_t* prow = smem + L::kOffP + sb * L::kPBytes + (row >> 3) * 1024 + (row & 7) * 128;
-                float rsum = 0.0f;
+                for (int hf = 0; hf < 2; ++hf) {
+                    uint32_t sa[32], sb[32];
+                    tmem_ld_32x32b_x32(t_s + hf * 64, sa);
+                    tmem_ld_32x32b_x32(t_s + hf * 64 + 32, sb);
+                    tmem_ld_wait(sa);
+                    tmem_ld_wait(sb);
+                    if (interior) {
 #pragma unroll
-                for (int c0 = 0; c0 < kAttnTile; c0 += 32) {
-                    uint32_t r[32];
-                    tmem_ld_32x32b_x32(ts + c0, r);
-                    tmem_ld_wait(r);
-                    uint32_t packed[16];
+                        for (int i = 0; i < 32; ++i) {
+                            mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sa[i]));
+                            mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sb[i]));
+                        }
+                    } else {
+                        const uint32_t wa = allow[2 * hf], wb = allow[2 * hf + 1];
 #pragma unroll
-                    for (int i = 0; i < 32; i += 2) {
-                        const float p0 = allowed_at(c0 + i)
-                                             ? fast_exp2(fmaf(__uint_as_float(r[i]), p.scale_log2, -m_scaled))
-                                             : 0.0f;
-                        const float p1 = allowed_at(c0 + i + 1)
-                                             ? fast_exp2(fmaf(__uint_as_float(r[i + 1]), p.scale_log2, -m_scaled))
-                                             : 0.0f;
-                        rsum += p0 + p1;
-                        packed[i / 2] = pack_half2(p0, p1);
-                    }
-                    // keys [c0, c0+32): block c0/64, 16-byte chunks (c0%64)/8 .. +3
-                    uint8_t* blk = prow + (c0 / 64) * (kAttnTile * 128);
-#pragma unroll
-                    for (int q4 = 0; q4 < 4; ++q4) {
-                        const int chunk = ((c0 % 64) / 8 + q4) ^ (row & 7);
-                        *reinterpret_cast<uint4*>(blk + chunk * 16) =
-                            make_uint4(packed[4 * q4], packed[4 * q4 + 1], packed[4 * q4 + 2], packed[4 * q4 + 3]);
+                        for (int i = 0; i < 32; ++i) {
+                            const float va = ((wa >> i) & 1u) ? __uint_as_float(sa[i]) : -INFINITY;
+                            const float vb = ((wb >> i) & 1u) ? __uint_as_float(sb[i]) : -INFINITY;
+                            mx8[i & 7] = fmaxf(mx8[i & 7], fmaxf(va, vb));
+                        }
                     }
                 }
-                l_run = l_run * alpha + rsum;
-                m_run = m_new;
+                const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+                const float m_new = fmaxf(m_used, mx);
+                // lazy rescale: only when the max grew by more than 2^kRescaleLog2
+                float alpha = 1.0f;
+                bool rescale = false;
+                if (m_used == -INFINITY) {
+                    m_used = m_new;          // no O yet (or O is all zero): nothing to scale
+                } else if ((m_new - m_used) * c > kRescaleLog2) {
+                    alpha = fast_exp2((m_used - m_new) * c);
+                    rescale = true;
+                }
+                if (__any_sync(0xffffffffu, rescale)) {
+                    // O holds the previous tiles of this group: wait for the last PV
+                    ok = mbar_wait(o_done(grp), (gtiles - 1) & 1u, abort_flag);
+                    if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
+                    tc_fence_after();
+#pragma unroll 1
+                    for (int cc = 0; cc < HD; cc += 32) {
+                        uint32_t orr[32];
+                        tmem_ld_32x32b_x32(t_o + cc, orr);
+                        tmem_ld_wait(orr);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) orr[i] = __float_as_uint(__uint_as_float(orr[i]) * alpha);
+                        tmem_st_32x32b_x32(t_o + cc, orr);
+                    }
+                    tmem_st_wait();
+                    if (rescale) {
+                        l_run *= alpha;
+                        m_used = m_new;
+                    }
+                }
+                const float mc = (m_used == -INFINITY) ? 0.0f : m_used * c;
+                // pass 2: P = exp2(s c - m c) as fp16 over the S columns already
+                // read (keys 64 hf.. go to columns 32 hf..), row sum in fp32
+                float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                    uint32_t sa[32], sb[32], pk[32];
+                    tmem_ld_32x32b_x32(t_s + hf * 64, sa);
+                    tmem_ld_32x32b_x32(t_s + hf * 64 + 32, sb);
+                    tmem_ld_wait(sa);
+                    tmem_ld_wait(sb);
+                    const uint32_t wa = interior ? 0xffffffffu : allow[2 * hf];
+                    const uint32_t wb = interior ? 0xffffffffu : allow[2 * hf + 1];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        float p0 = fast_exp2(fmaf(__uint_as_float(sa[2 * i]), c, -mc));
+                        float p1 = fast_exp2(fmaf(__uint_as_float(sa[2 * i + 1]), c, -mc));
+                        float p2 = fast_exp2(fmaf(__uint_as_float(sb[2 * i]), c, -mc));
+                        float p3 = fast_exp2(fmaf(__uint_as_float(sb[2 * i + 1]), c, -mc));
+                        p0 = ((wa >> (2 * i)) & 1u) ? p0 : 0.0f;
+                        p1 = ((wa >> (2 * i + 1)) & 1u) ? p1 : 0.0f;
+                        p2 = ((wb >> (2 * i)) & 1u) ? p2 : 0.0f;
+                        p3 = ((wb >> (2 * i + 1)) & 1u) ? p3 : 0.0f;
+                        sum8[i & 7] += p0 + p1;
+                        sum8[(i + 4) & 7] += p2 + p3;
+                        pk[i] = pack_half2(p0, p1);
+                        pk[16 + i] = pack_half2(p2, p3);
+                    }
+                    tmem_st_32x32b_x32(t_s + hf * 32, pk);
+                }
+                l_run += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+                tmem_st_wait();
                 tc_fence_before();
-                mbar_arrive(s_empty(sb));
-                fence_proxy_async_smem();     // P stores -> visible to the tensor core
-                mbar_arrive(p_full(sb));
-
-                if (j > 0 && !accumulate(t - 1, alpha_prev)) { alive = false; break; }
-                alpha_prev = alpha;
+                mbar_arrive(p_full(grp));
             }
-            if (alive && !accumulate(tcount + n_kt - 1, alpha_prev)) alive = false;
             if (!alive) break;
-            tcount += n_kt;
-
-            if (q_ok) {
-                const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
-                int64_t off;
-                if (p.out_layout == 1)
-                    off = ((static_cast<int64_t>(b) * p.S + s) * p.H + h) * HD;
-                else
-                    off = ((static_cast<int64_t>(b) * p.H + h) * p.S + s) * HD;
-                __half* op = reinterpret_cast<__half*>(p.out) + off;
+            if (n_kt == 0) {
+                if (grp == 0 && q_ok) {
+                    int64_t off = (p.out_layout == 1) ? ((static_cast<int64_t>(b) * p.S + s) * p.H + h) * HD
+                                                      : ((static_cast<int64_t>(b) * p.H + h) * p.S + s) * HD;
+                    __half* op = reinterpret_cast<__half*>(p.out) + off;
 #pragma unroll
-                for (int i = 0; i < HD; i += 8) {
-                    uint4 v;
-                    v.x = pack_half2(o[i] * inv, o[i + 1] * inv);
-                    v.y = pack_half2(o[i + 2] * inv, o[i + 3] * inv);
-                    v.z = pack_half2(o[i + 4] * inv, o[i + 5] * inv);
-                    v.w = pack_half2(o[i + 6] * inv, o[i + 7] * inv);
-                    *reinterpret_cast<uint4*>(op + i) = v;
+                    for (int i = 0; i < HD; i += 8) *reinterpret_cast<uint4*>(op + i) = make_uint4(0, 0, 0, 0);
+                }
+                continue;
+            }
+            // With a single key tile group 1 had no work in this item.
+            const bool two = n_kt >= 2;
+            if (grp == 1 && !two) continue;
+            // the last PV of this group has landed in O
+            ok = mbar_wait(o_done(grp), (gtiles - 1) & 1u, abort_flag);
+            if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
+            tc_fence_after();
+            if (grp == 1) {
+                ok = mbar_wait(comb_empty, (ccount & 1u) ^ 1u, abort_flag);
+                if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
+                comb[row] = make_float2(m_used, l_run);
+                mbar_arrive(comb_full);
+                ++ccount;
+                continue;
+            }
+            float a0 = 1.0f, a1 = 0.0f, l_tot = l_run;
+            if (two) {
+                ok = mbar_wait(comb_full, ccount & 1u, abort_flag);
+                if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
+                const float2 other = comb[row];
+                mbar_arrive(comb_empty);
+                ++ccount;
+                const float m = fmaxf(m_used, other.x);
+                a0 = (m_used == -INFINITY) ? 0.0f : fast_exp2((m_used - m) * c);
+                a1 = (other.x == -INFINITY) ? 0.0f : fast_exp2((other.x - m) * c);
+                l_tot = l_run * a0 + other.y * a1;
+            }
+            const float inv = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;
+            a0 *= inv;
+            a1 *= inv;
+            int64_t off = (p.out_layout == 1) ? ((static_cast<int64_t>(b) * p.S + s) * p.H + h) * HD
+                                              : ((static_cast<int64_t>(b) * p.H + h) * p.S + s) * HD;
+            __half* op = reinterpret_cast<__half*>(p.out) + off;
+#pragma unroll 1
+            for (int cc = 0; cc < HD; cc += 32) {
+                uint32_t o0[32], o1[32];
+                tmem_ld_32x32b_x32(t_o0 + cc, o0);
+                if (two) tmem_ld_32x32b_x32(t_o0 + HD + cc, o1);
+                tmem_ld_wait(o0);
+                if (two) tmem_ld_wait(o1);
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    o0[i] = __float_as_uint(two ? fmaf(__uint_as_float(o0[i]), a0, __uint_as_float(o1[i]) * a1)
+                                                : __uint_as_float(o0[i]) * a0);
+                if (q_ok) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 8) {
+                        uint4 w;
+                        w.x = pack_half2(__uint_as_float(o0[i]), __uint_as_float(o0[i + 1]));
+                        w.y = pack_half2(__uint_as_float(o0[i + 2]), __uint_as_float(o0[i + 3]));
+                        w.z = pack_half2(__uint_as_float(o0[i + 4]), __uint_as_float(o0[i + 5]));
+                        w.w = pack_half2(__uint_as_float(o0[i + 6]), __uint_as_float(o0[i + 7]));
+                        *reinterpret_cast<uint4*>(op + cc + i) = w;
+                    }
                 }
             }
+            tc_fence_before();
+            mbar_arrive(o_free);
+            ++ocount;
         }
+        (void)ocount;
     }
 
     // ------------------------------------------------------------ teardown --
