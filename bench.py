@@ -99,6 +99,27 @@ def _init_model(model, seed):
                 p.copy_((torch.rand(p.shape, generator=g) * 2 - 1) * 0.02)
 
 
+def shard_rows(batch, world, rank, strong):
+    """Batch rows [lo, hi) this rank runs. Weak scaling: every rank runs the
+    config's whole batch (a global batch of batch * world). Strong scaling:
+    the config's batch is split evenly across ranks (rows never interact)."""
+    if not strong:
+        return 0, batch
+    if batch % world != 0:
+        raise ValueError(f"--strong needs the batch ({batch}) divisible by the {world} ranks")
+    per = batch // world
+    return rank * per, (rank + 1) * per
+
+
+def max_over_ranks(values, dist, device):
+    """Elementwise max of a list of floats over all ranks (the slowest rank's
+    time is the job's time)."""
+    t = torch.tensor(values, dtype=torch.float64, device=device)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t.tolist()]
+
+
 def _peaks():
     path = os.path.join(REPO, "MEASURED_PEAKS.json")
     try:
@@ -367,11 +388,17 @@ def run_ours(args, rank, world, local_rank):
     model = OptimizedTransformer(cfg)
     _init_model(model, SEED)
     model = model.to(dev).eval()
-    x_cpu, mask_cpu = _synthetic_case(cfg, SEED + 17 * rank, cfg.batch_size)
+    lo, hi = shard_rows(cfg.batch_size, world, rank, args.strong)
+    if args.strong:
+        x_all, mask_all = _synthetic_case(cfg, SEED, cfg.batch_size)
+        x_cpu = x_all[lo:hi].contiguous()
+        mask_cpu = mask_all[lo:hi].contiguous() if mask_all is not None else None
+    else:
+        x_cpu, mask_cpu = _synthetic_case(cfg, SEED + 17 * rank, cfg.batch_size)
     x = x_cpu.to(dev)
     mask = mask_cpu.to(dev) if mask_cpu is not None else None
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
-    tokens_per_rank = cfg.batch_size * cfg.seq_len
+    tokens_per_rank = (hi - lo) * cfg.seq_len
     stream = torch.cuda.current_stream(dev)
 
     def barrier():
@@ -430,10 +457,7 @@ def run_ours(args, rank, world, local_rank):
     h2d = x_cpu.numel() * 4 + (mask_cpu.numel() if mask_cpu is not None else 0)
     d2h = x_cpu.numel() * 4
 
-    times = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=dev)
-    if dist is not None:
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    total_ms, e2e_ms = float(times[0]), float(times[1])
+    total_ms, e2e_ms = max_over_ranks([total_ms, e2e_ms], dist, dev)
 
     breakdown = None
     if rank == 0:
@@ -457,10 +481,10 @@ def run_ours(args, rank, world, local_rank):
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
-            "data": "synthetic",
-            "config": {"workload": _describe(args.config), "batch_per_gpu": cfg.batch_size,
-                       "global_batch": cfg.batch_size * world, "seq_len": cfg.seq_len,
+            "higher_is_better": True, "scaling": "strong" if args.strong else "weak",
+            "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": _describe(args.config), "batch_per_gpu": hi - lo,
+                       "global_batch": (hi - lo) * world, "seq_len": cfg.seq_len,
                        "layers": cfg.num_layers, "parallelism": f"dp{world}",
                        "l2": "flushed between steps (256 MiB write); inputs smaller than L2",
                        "cuda_graph": oconfig.CUDA_GRAPH != "off",
@@ -524,6 +548,8 @@ def main() -> int:
     ap.add_argument("--layers", type=int, default=1)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-graph", action="store_true", help="time the eager path (no CUDA graph)")
+    ap.add_argument("--strong", action="store_true",
+                    help="split the config's batch across ranks (strong scaling) instead of a full batch per rank")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--settle", type=float, default=1.0, help="seconds of untimed steps before timing")
     ap.add_argument("--profile-kernel", default=None,

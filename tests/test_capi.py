@@ -1,0 +1,112 @@
+"""libdotl's C ABI on the host (no GPU): it loads, exports every symbol that
+include/dotl.h declares, and rejects bad arguments with a status code and a
+message before anything reaches a device."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import PKG, REPO
+
+HEADER = os.path.join(REPO, "include", "dotl.h")
+LIB = os.path.join(PKG, "lib", "libdotl.so")
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not os.path.exists(LIB):
+        import kernel_ext
+
+        kernel_ext.build()
+    import dotl_ops
+
+    return dotl_ops.load(LIB)
+
+
+def _declared():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"\b(dotl_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_entry_points():
+    names = _declared()
+    for n in ("dotl_linear", "dotl_attention", "dotl_layernorm", "dotl_identity_f32",
+              "dotl_last_error", "dotl_device_error"):
+        assert n in names
+
+
+def test_every_declared_symbol_is_exported(lib):
+    missing = [n for n in _declared() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_abi_version(lib):
+    assert lib.dotl_abi_version() == 1
+
+
+def _err(lib):
+    return lib.dotl_last_error().decode()
+
+
+def test_linear_rejects_unaligned_k(lib):
+    rc = lib.dotl_linear(16, 4, 7, 7, 16, 16, 7, 16, 0, None, 0, None, 0, 16, 0, 16, 0, None)
+    assert rc == 2 and "multiples of 8" in _err(lib)
+
+
+def test_linear_rejects_bad_modes(lib):
+    assert lib.dotl_linear(16, 4, 8, 8, 16, 16, 8, 16, 2, None, 0, None, 0, 16, 0, 16, 0, None) == 1
+    assert "act must be" in _err(lib)
+    assert lib.dotl_linear(16, 4, 8, 8, 16, 16, 8, 16, 0, None, 0, None, 9, 16, 0, 16, 0, None) == 1
+    assert "residual mode" in _err(lib)
+    assert lib.dotl_linear(16, 4, 8, 8, 16, 16, 8, 16, 0, None, 0, None, 0, 16, 5, 16, 0, None) == 1
+    assert "out dtype" in _err(lib)
+    # masked residual needs the row mask
+    assert lib.dotl_linear(16, 4, 8, 8, 16, 16, 8, 16, 0, 16, 16, None, 3, 16, 0, 16, 0, None) == 1
+    assert "row_valid" in _err(lib)
+
+
+def test_linear_empty_m_is_ok(lib):
+    assert lib.dotl_linear(None, 0, 8, 8, None, 16, 8, None, 0, None, 0, None, 0, None, 0, 16, 0, None) == 0
+
+
+def test_attention_rejects_head_dim(lib):
+    st = (ctypes.c_int64 * 3)(0, 0, 0)
+    rc = lib.dotl_attention(16, 16, 16, 1, 1, 8, 48, st, st, st, None, 0, None, 0, 0.1, 16, 0, None)
+    assert rc == 2 and "head_dim" in _err(lib)
+
+
+def test_attention_rejects_layout_and_mask(lib):
+    st = (ctypes.c_int64 * 3)(0, 0, 0)
+    assert lib.dotl_attention(16, 16, 16, 1, 1, 8, 64, st, st, st, None, 0, None, 0, 0.1, 16, 2, None) == 1
+    assert "out_layout" in _err(lib)
+    assert lib.dotl_attention(16, 16, 16, 1, 1, 8, 64, st, st, st, None, 1, None, 0, 0.1, 16, 0, None) == 1
+    assert "needs mask" in _err(lib)
+
+
+def test_attention_rejects_unaligned_strides(lib):
+    st = (ctypes.c_int64 * 3)(64 * 8, 64, 12)
+    rc = lib.dotl_attention(16, 16, 16, 1, 1, 8, 64, st, st, st, None, 0, None, 0, 0.1, 16, 0, None)
+    assert rc == 2 and "multiples of 8" in _err(lib)
+
+
+def test_layernorm_rejects(lib):
+    assert lib.dotl_layernorm(16, None, 16, 16, None, 16, 0, None, 4, 4096, 1e-5, None) == 2
+    assert "2048" in _err(lib)
+    assert lib.dotl_layernorm(16, 16, 16, 16, None, 16, 0, None, 4, 64, 1e-5, None) == 1
+    assert "x_new" in _err(lib)
+    assert lib.dotl_layernorm(16, None, 16, 16, None, 16, 7, None, 4, 64, 1e-5, None) == 1
+
+
+def test_identity_rejects_negative(lib):
+    assert lib.dotl_identity_f32(None, None, -1, None) == 1
+    assert "negative" in _err(lib)
+    assert lib.dotl_identity_f32(None, None, 0, None) == 0
+
+
+def test_build_flags_target_sm100a():
+    import kernel_ext
+
+    cmd = " ".join(kernel_ext.build_command())
+    assert "arch=compute_100a,code=sm_100a" in cmd and "-lineinfo" in cmd

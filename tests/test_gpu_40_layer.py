@@ -92,13 +92,3 @@ def test_batch_rows_independent(kernels):
         full = model(x, mask)
         one = model(x[1:2].contiguous(), mask[1:2].contiguous())
     assert torch.equal(full[1:2], one)
-
-
-def test_missing_library_raises(monkeypatch):
-    """The product path fails loudly without libdotl (no CPU or torch fallback)."""
-    import kernel_ext
-    from optimized import kernels as okernels
-
-    monkeypatch.setattr(kernel_ext, "get_kernels", lambda verbose=False: None)
-    with pytest.raises(RuntimeError, match="no fallback"):
-        okernels._custom_kernels()

@@ -1,0 +1,69 @@
+"""The multi-rank host plumbing of bench.py on CPU ranks (gloo, world size 2).
+
+The GPU job shards batch rows across ranks with no data-path collective and
+takes the slowest rank's time. Here each CPU rank runs the oracle on its shard
+(the stand-in for its GPU's forward), the max-over-ranks reduction is checked,
+and the gathered shards must equal the unsharded forward: rows never interact.
+"""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import layer as O
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, result_path):
+    import sys
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path.insert(0, os.path.dirname(here))
+    import bench
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cfg = O.TransformerConfig(4, 24, 32, 2, 64, 1, True)
+        params = O.init_params(cfg, 3)
+        x, mask = O.generate_random_case(cfg, 4, 0.5, 1.0)
+        lo, hi = bench.shard_rows(cfg.batch_size, world, rank, strong=True)
+        sub = O.TransformerConfig(hi - lo, 24, 32, 2, 64, 1, True)
+        out = O.baseline_forward(params, sub, x[lo:hi], mask[lo:hi])
+        gathered = [torch.empty_like(out) for _ in range(world)]
+        dist.all_gather(gathered, out)
+        slowest = bench.max_over_ranks([1.0 + rank, 5.0 - rank], dist, torch.device("cpu"))
+        if rank == 0:
+            full = O.baseline_forward(params, cfg, x, mask)
+            torch.save({"full": full, "sharded": torch.cat(gathered), "max": slowest}, result_path)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_ranks_shard_and_reduce(tmp_path):
+    world = 2
+    path = str(tmp_path / "r.pt")
+    mp.start_processes(_worker, args=(world, _free_port(), path), nprocs=world,
+                       start_method="spawn", join=True)
+    r = torch.load(path)
+    assert torch.equal(r["full"], r["sharded"])
+    assert r["max"] == [2.0, 5.0]
+
+
+def test_shard_rows_arithmetic():
+    import bench
+
+    assert bench.shard_rows(8, 4, 2, strong=True) == (4, 6)
+    assert bench.shard_rows(8, 4, 3, strong=False) == (0, 8)
+    with pytest.raises(ValueError, match="divisible"):
+        bench.shard_rows(4, 8, 0, strong=True)
