@@ -16,7 +16,8 @@ write between steps to flush the 126 MB L2 (the inputs are smaller than L2).
 `value` = tokens processed by all ranks / max over ranks of the summed step
 time. `e2e` repeats the steps with the input copied in from pinned host memory
 and the output copied back inside the timed region. `roofline` is the
-dominant kernel of the layer, timed alone with CUDA events. `cpu_baseline` is
+dominant kernel of the layer, timed alone with CUDA events around CUDA-graph
+replays of 20 back-to-back launches (best of 5). `cpu_baseline` is
 the reference's CPU layer (the oracle port of BaselineTransformer) on this
 host's cores, rank 0 at N=1 only.
 
@@ -332,24 +333,35 @@ def _layer_ops(model, x, mask, kernels, cfg):
 
 
 def _op_breakdown(model, x, mask, reps, kernels, cfg):
-    """Each kernel of one layer forward timed alone (CUDA events on the
-    launching stream, back to back, steady state), with its algorithmic work."""
+    """Each kernel of one layer forward timed alone: `reps` back-to-back
+    launches captured in a CUDA graph (no host launch cost in the timing),
+    replayed between CUDA events on the launching stream, best of 5."""
     ops = _layer_ops(model, x, mask, kernels, cfg)
-    stream = torch.cuda.current_stream()
     out = []
     for name, bound, work, fn in ops:
-        for _ in range(3):
-            fn()
-        ev0 = torch.cuda.Event(enable_timing=True)
-        ev1 = torch.cuda.Event(enable_timing=True)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                fn()
+        torch.cuda.current_stream().wait_stream(side)
         torch.cuda.synchronize()
-        ev0.record(stream)
-        for _ in range(reps):
-            fn()
-        ev1.record(stream)
-        torch.cuda.synchronize()
-        ms = ev0.elapsed_time(ev1) / reps
-        out.append({"kernel": name, "bound": bound, "work": work, "ms": ms})
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            for _ in range(reps):
+                fn()
+        stream = torch.cuda.current_stream()
+        best = float("inf")
+        for _ in range(5):
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev0.record(stream)
+            graph.replay()
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            best = min(best, ev0.elapsed_time(ev1) / reps)
+        graph.reset()
+        out.append({"kernel": name, "bound": bound, "work": work, "ms": best})
     return out
 
 
@@ -462,7 +474,7 @@ def run_ours(args, rank, world, local_rank):
     breakdown = None
     if rank == 0:
         with torch.inference_mode():
-            breakdown = _op_breakdown(model, x, mask, max(20, min(args.steps, 200)), kernels, cfg)
+            breakdown = _op_breakdown(model, x, mask, 20, kernels, cfg)
     word = kernels.device_error(clear=True)
     if word:
         raise RuntimeError(f"device error word {word:#x} after the timed run")

@@ -41,7 +41,7 @@
 
 namespace dotl {
 
-constexpr int kAttnThreads = 320;
+constexpr int kAttnThreads = 384;   // softmax warpgroups 0-1, producer/MMA warpgroup 2
 constexpr int kAttnTile = 128;          // query rows per tile and keys per key tile
 constexpr float kRescaleLog2 = 8.0f;    // lazy-rescale threshold, in log2 units
 
@@ -84,11 +84,11 @@ struct AttnSmem {
     static constexpr uint32_t kOffV = kOffK + STAGES * kTileBytes;
     static constexpr uint32_t kOffComb = kOffV + STAGES * kTileBytes;   // 128 x (max, sum) of group 1
     static constexpr uint32_t kOffInfo = kOffComb + kAttnTile * 8;      // 2 item slots
-    static constexpr uint32_t kOffBar = kOffInfo + 16;
+    static constexpr uint32_t kOffBar = kOffInfo + 16;   // 2 slots x {n_kt, hole}
     // q_full, q_empty, k_full[ST], v_full[ST], kv_empty[ST], s_full[2],
-    // p_full[2], o_done[2], o_free, comb_full, comb_empty, info_full[2],
+    // p_full[2], o_done[2], o_free[2], comb_full, comb_empty, info_full[2],
     // info_empty[2], drain
-    static constexpr uint32_t kNumBars = 2 + 3 * STAGES + 6 + 3 + 4 + 1;
+    static constexpr uint32_t kNumBars = 2 + 3 * STAGES + 8 + 2 + 4 + 1;
     static constexpr uint32_t kOffSlot = kOffBar + kNumBars * 8;
     static constexpr uint32_t kOffAbort = kOffSlot + 4;
     static constexpr uint32_t kBytes = kOffAbort + 4;
@@ -120,17 +120,35 @@ __device__ __forceinline__ void attn_key_range(const AttnParams& p, int qt, int&
     }
 }
 
-// One past the last key of sequence b the per-key mask allows (0 if none).
-// Warp-collective; scans backwards 32 keys at a time.
-__device__ __forceinline__ int attn_last_valid_key(const AttnParams& p, int b, int lane) {
+// Scans sequence b's per-key mask once: `end` = one past its last allowed key
+// (0 if none), `hole` = its first masked key (S if none). Keys below `hole`
+// are all allowed, so tiles there need no per-key mask reads. Warp-collective.
+__device__ __forceinline__ void attn_scan_keys(const AttnParams& p, int b, int lane, int& end, int& hole) {
     const uint8_t* base = p.mask + static_cast<int64_t>(b) * p.ms0;
-    for (int hi = p.S; hi > 0; hi -= 32) {
-        const int k = hi - 1 - lane;
-        const bool v = k >= 0 && base[static_cast<int64_t>(k) * p.ms3] != 0;
-        const uint32_t bits = __ballot_sync(0xffffffffu, v);
-        if (bits) return hi - (__ffs(bits) - 1);
+    int first_zero = p.S, last_one = -1;
+    const bool vec = p.ms3 == 1 && (reinterpret_cast<uintptr_t>(base) & 15u) == 0 && (p.S & 15) == 0;
+    if (vec) {
+        for (int k0 = 16 * lane; k0 < p.S; k0 += 512) {
+            const uint4 v = *reinterpret_cast<const uint4*>(base + k0);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+#pragma unroll
+                for (int byte = 0; byte < 4; ++byte) {
+                    const int k = k0 + 4 * q + byte;
+                    if ((w[q] >> (8 * byte)) & 0xffu) last_one = max(last_one, k);
+                    else first_zero = min(first_zero, k);
+                }
+            }
+        }
+    } else {
+        for (int k = lane; k < p.S; k += 32) {
+            if (base[static_cast<int64_t>(k) * p.ms3]) last_one = max(last_one, k);
+            else first_zero = min(first_zero, k);
+        }
     }
-    return 0;
+    end = __reduce_max_sync(0xffffffffu, last_one) + 1;
+    hole = __reduce_min_sync(0xffffffffu, first_zero);
 }
 
 template <int HD, int STAGES>
@@ -150,15 +168,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     auto s_full = [&](int g) { return bar0 + 8u * (2 + 3 * STAGES + g); };
     auto p_full = [&](int g) { return bar0 + 8u * (4 + 3 * STAGES + g); };
     auto o_done = [&](int g) { return bar0 + 8u * (6 + 3 * STAGES + g); };
-    const uint32_t o_free = bar0 + 8u * (8 + 3 * STAGES);
-    const uint32_t comb_full = bar0 + 8u * (9 + 3 * STAGES);
-    const uint32_t comb_empty = bar0 + 8u * (10 + 3 * STAGES);
-    auto info_full = [&](int s) { return bar0 + 8u * (11 + 3 * STAGES + s); };
-    auto info_empty = [&](int s) { return bar0 + 8u * (13 + 3 * STAGES + s); };
-    const uint32_t drain_bar = bar0 + 8u * (15 + 3 * STAGES);
+    auto o_free = [&](int g) { return bar0 + 8u * (8 + 3 * STAGES + g); };
+    const uint32_t comb_full = bar0 + 8u * (10 + 3 * STAGES);
+    const uint32_t comb_empty = bar0 + 8u * (11 + 3 * STAGES);
+    auto info_full = [&](int s) { return bar0 + 8u * (12 + 3 * STAGES + s); };
+    auto info_empty = [&](int s) { return bar0 + 8u * (14 + 3 * STAGES + s); };
+    const uint32_t drain_bar = bar0 + 8u * (16 + 3 * STAGES);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffAbort);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffSlot);
-    volatile int* info = reinterpret_cast<volatile int*>(smem + L::kOffInfo);
+    volatile int* info = reinterpret_cast<volatile int*>(smem + L::kOffInfo);   // {n_kt, hole} x 2
     float2* comb = reinterpret_cast<float2*>(smem + L::kOffComb);
 
     const int warp = threadIdx.x >> 5;
@@ -176,10 +194,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             mbar_init(s_full(g), 1);
             mbar_init(p_full(g), 128);
             mbar_init(o_done(g), 1);
+            mbar_init(o_free(g), 128);
             mbar_init(info_full(g), 1);
             mbar_init(info_empty(g), 1 + 8);
         }
-        mbar_init(o_free, 128);
         mbar_init(comb_full, 128);
         mbar_init(comb_empty, 128);
         mbar_init(drain_bar, 1);
@@ -189,7 +207,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tma_prefetch_map(&tmap_k);
         tma_prefetch_map(&tmap_v);
     }
-    if (warp == 1) {
+    pdl_wait();
+    pdl_launch_dependents();
+    if (warp == 9) {
         tmem_alloc(smem_u32(tmem_slot), L::kTmemCols);
         tmem_relinquish();
     }
@@ -200,138 +220,161 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int num_items = p.num_streams * p.num_q_tiles;
     const bool scan_mask = p.mask_kind == 1 && !p.packed;
 
-    if (warp == 0) {
-        // ------------------------------------------------------- producer --
-        uint32_t tcount = 0, qcount = 0, icount = 0;
-        int k_issued_phase[STAGES];
-        for (int s = 0; s < STAGES; ++s) k_issued_phase[s] = -1;
-        int q_issued = -1;
-        for (int item = blockIdx.x; item < num_items; item += gridDim.x, ++icount) {
-            int stream, qt, k_lo, k_hi;
-            attn_item(p, item, stream, qt);
-            attn_key_range(p, qt, k_lo, k_hi);
-            const int h = p.packed ? stream : stream % p.H;
-            const int bq = p.packed ? 0 : stream / p.H;
-            if (scan_mask) k_hi = min(k_hi, attn_last_valid_key(p, bq, lane));
-            const int n_kt = k_hi > k_lo ? (k_hi - k_lo + kAttnTile - 1) / kAttnTile : 0;
-            bool ok = true;
-            if (lane == 0) {
-                const int slot = static_cast<int>(icount & 1u);
-                ok = mbar_wait(info_empty(slot), ((icount >> 1) & 1u) ^ 1u, abort_flag);
-                if (ok) {
-                    info[slot] = n_kt;
-                    mbar_arrive(info_full(slot));
+    // Which group takes an item's first key tile. Items with several tiles
+    // alternate tiles between the groups (group 0 merges and writes); items
+    // with a single tile alternate whole items between the groups.
+    auto first_group = [](int n_kt, uint32_t& singles) -> int {
+        if (n_kt != 1) return 0;
+        return static_cast<int>(singles++ & 1u);
+    };
+
+    if (warp >= 8) {
+        regs_dec<104>();
+        if (warp == 8) {
+            // --------------------------------------------------- producer --
+            uint32_t tcount = 0, qcount = 0, icount = 0;
+            int k_issued_phase[STAGES];
+            for (int s = 0; s < STAGES; ++s) k_issued_phase[s] = -1;
+            int q_issued = -1;
+            for (int item = blockIdx.x; item < num_items; item += gridDim.x, ++icount) {
+                int stream, qt, k_lo, k_hi;
+                attn_item(p, item, stream, qt);
+                attn_key_range(p, qt, k_lo, k_hi);
+                const int h = p.packed ? stream : stream % p.H;
+                const int bq = p.packed ? 0 : stream / p.H;
+                int hole = 0;
+                if (scan_mask) {
+                    int end;
+                    attn_scan_keys(p, bq, lane, end, hole);
+                    k_hi = min(k_hi, end);
                 }
-                if (ok && n_kt > 0) {
-                    ok = mbar_wait(q_empty, (qcount & 1u) ^ 1u, abort_flag);
+                const int n_kt = k_hi > k_lo ? (k_hi - k_lo + kAttnTile - 1) / kAttnTile : 0;
+                bool ok = true;
+                if (lane == 0) {
+                    const int slot = static_cast<int>(icount & 1u);
+                    ok = mbar_wait(info_empty(slot), ((icount >> 1) & 1u) ^ 1u, abort_flag);
                     if (ok) {
-                        mbar_arrive_expect_tx(q_full, L::kTileBytes);
+                        info[2 * slot] = n_kt;
+                        info[2 * slot + 1] = hole;
+                        mbar_arrive(info_full(slot));
+                    }
+                    if (ok && n_kt > 0) {
+                        ok = mbar_wait(q_empty, (qcount & 1u) ^ 1u, abort_flag);
+                        if (ok) {
+                            mbar_arrive_expect_tx(q_full, L::kTileBytes);
+#pragma unroll
+                            for (int cb = 0; cb < L::kNumBlk; ++cb)
+                                attn_tma(sbase + L::kOffQ + cb * L::kBlkBytes, &tmap_q, q_full,
+                                         cb * L::kBlkCols, qt * kAttnTile, h, bq, p.head_inner & 1);
+                            q_issued = static_cast<int>(qcount & 1u);
+                        }
+                    }
+                    for (int j = 0; ok && j < n_kt; ++j, ++tcount) {
+                        const int st = static_cast<int>(tcount % STAGES);
+                        const uint32_t ph = (tcount / STAGES) & 1u;
+                        const int kc0 = k_lo + j * kAttnTile;
+                        ok = mbar_wait(kv_empty(st), ph ^ 1u, abort_flag);
+                        if (!ok) break;
+                        mbar_arrive_expect_tx(k_full(st), L::kTileBytes);
 #pragma unroll
                         for (int cb = 0; cb < L::kNumBlk; ++cb)
-                            attn_tma(sbase + L::kOffQ + cb * L::kBlkBytes, &tmap_q, q_full,
-                                     cb * L::kBlkCols, qt * kAttnTile, h, bq, p.head_inner & 1);
-                        q_issued = static_cast<int>(qcount & 1u);
+                            attn_tma(sbase + L::kOffK + st * L::kTileBytes + cb * L::kBlkBytes, &tmap_k,
+                                     k_full(st), cb * L::kBlkCols, kc0, h, bq, p.head_inner & 2);
+                        mbar_arrive_expect_tx(v_full(st), L::kTileBytes);
+#pragma unroll
+                        for (int cb = 0; cb < L::kNumBlk; ++cb)
+                            attn_tma(sbase + L::kOffV + st * L::kTileBytes + cb * L::kBlkBytes, &tmap_v,
+                                     v_full(st), cb * L::kBlkCols, kc0, h, bq, p.head_inner & 4);
+                        k_issued_phase[st] = static_cast<int>(ph);
                     }
                 }
-                for (int j = 0; ok && j < n_kt; ++j, ++tcount) {
-                    const int st = static_cast<int>(tcount % STAGES);
-                    const uint32_t ph = (tcount / STAGES) & 1u;
-                    const int kc0 = k_lo + j * kAttnTile;
-                    ok = mbar_wait(kv_empty(st), ph ^ 1u, abort_flag);
-                    if (!ok) break;
-                    mbar_arrive_expect_tx(k_full(st), L::kTileBytes);
-#pragma unroll
-                    for (int cb = 0; cb < L::kNumBlk; ++cb)
-                        attn_tma(sbase + L::kOffK + st * L::kTileBytes + cb * L::kBlkBytes, &tmap_k,
-                                 k_full(st), cb * L::kBlkCols, kc0, h, bq, p.head_inner & 2);
-                    mbar_arrive_expect_tx(v_full(st), L::kTileBytes);
-#pragma unroll
-                    for (int cb = 0; cb < L::kNumBlk; ++cb)
-                        attn_tma(sbase + L::kOffV + st * L::kTileBytes + cb * L::kBlkBytes, &tmap_v,
-                                 v_full(st), cb * L::kBlkCols, kc0, h, bq, p.head_inner & 4);
-                    k_issued_phase[st] = static_cast<int>(ph);
+                if (n_kt > 0) ++qcount;
+                ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+                if (!ok) break;
+            }
+            if (lane == 0 && *abort_flag) {
+                if (q_issued >= 0) mbar_wait_drain(q_full, static_cast<uint32_t>(q_issued));
+                for (int s = 0; s < STAGES; ++s) {
+                    if (k_issued_phase[s] >= 0) {
+                        mbar_wait_drain(k_full(s), static_cast<uint32_t>(k_issued_phase[s]));
+                        mbar_wait_drain(v_full(s), static_cast<uint32_t>(k_issued_phase[s]));
+                    }
                 }
             }
-            if (n_kt > 0) ++qcount;
-            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-            if (!ok) break;
-        }
-        if (lane == 0 && *abort_flag) {
-            if (q_issued >= 0) mbar_wait_drain(q_full, static_cast<uint32_t>(q_issued));
-            for (int s = 0; s < STAGES; ++s) {
-                if (k_issued_phase[s] >= 0) {
-                    mbar_wait_drain(k_full(s), static_cast<uint32_t>(k_issued_phase[s]));
-                    mbar_wait_drain(v_full(s), static_cast<uint32_t>(k_issued_phase[s]));
-                }
-            }
-        }
-    } else if (warp == 1 && lane == 0) {
-        // ---------------------------------------------------- MMA issuer --
-        constexpr uint32_t idesc_s = idesc_f16_f32(kAttnTile, kAttnTile, false, false);
-        constexpr uint32_t idesc_o = idesc_f16_f32(kAttnTile, HD, false, true);
-        constexpr int kStepsPerBlk = L::kBlkCols / 16;
-        uint32_t tcount = 0, qcount = 0, icount = 0;
-        uint32_t gcount[2] = {0, 0};
-        for (int item = blockIdx.x; item < num_items; item += gridDim.x, ++icount) {
-            const int slot = static_cast<int>(icount & 1u);
-            if (!mbar_wait(info_full(slot), (icount >> 1) & 1u, abort_flag)) break;
-            const int n_kt = info[slot];
-            mbar_arrive(info_empty(slot));
-            if (n_kt == 0) continue;
-            if (!mbar_wait(q_full, qcount & 1u, abort_flag)) break;
-            tc_fence_after();
-            // S(j) = Q K(j)^T into group (j & 1)'s S region.
-            auto issue_s = [&](int j) -> bool {
-                const uint32_t t = tcount + j;
-                const int st = static_cast<int>(t % STAGES);
-                if (!mbar_wait(k_full(st), (t / STAGES) & 1u, abort_flag)) return false;
+        } else if (warp == 9 && lane == 0) {
+            // ------------------------------------------------- MMA issuer --
+            constexpr uint32_t idesc_s = idesc_f16_f32(kAttnTile, kAttnTile, false, false);
+            constexpr uint32_t idesc_o = idesc_f16_f32(kAttnTile, HD, false, true);
+            constexpr int kStepsPerBlk = L::kBlkCols / 16;
+            uint32_t tcount = 0, qcount = 0, icount = 0, singles = 0;
+            uint32_t gcount[2] = {0, 0}, pcount[2] = {0, 0};
+            for (int item = blockIdx.x; item < num_items; item += gridDim.x, ++icount) {
+                const int slot = static_cast<int>(icount & 1u);
+                if (!mbar_wait(info_full(slot), (icount >> 1) & 1u, abort_flag)) break;
+                const int n_kt = info[2 * slot];
+                mbar_arrive(info_empty(slot));
+                if (n_kt == 0) continue;
+                const int g0 = first_group(n_kt, singles);
+                if (!mbar_wait(q_full, qcount & 1u, abort_flag)) break;
                 tc_fence_after();
-                const uint32_t d = tmem_base + L::kColS + static_cast<uint32_t>((j & 1) * kAttnTile);
-                const uint32_t qa = sbase + L::kOffQ;
-                const uint32_t ka = sbase + L::kOffK + st * L::kTileBytes;
+                // S(j) = Q K(j)^T into the S region of tile j's group.
+                auto issue_s = [&](int j) -> bool {
+                    const uint32_t t = tcount + j;
+                    const int st = static_cast<int>(t % STAGES);
+                    const int g = (g0 + j) & 1;
+                    if (!mbar_wait(k_full(st), (t / STAGES) & 1u, abort_flag)) return false;
+                    tc_fence_after();
+                    const uint32_t d = tmem_base + L::kColS + static_cast<uint32_t>(g * kAttnTile);
+                    const uint32_t qa = sbase + L::kOffQ;
+                    const uint32_t ka = sbase + L::kOffK + st * L::kTileBytes;
 #pragma unroll
-                for (int kk = 0; kk < HD / 16; ++kk) {
-                    const uint32_t off = (kk / kStepsPerBlk) * L::kBlkBytes + (kk % kStepsPerBlk) * 32;
-                    mma_f16_ss(d, smem_desc(qa + off, 16, 8 * L::kRowBytes, L::kSwz),
-                               smem_desc(ka + off, 16, 8 * L::kRowBytes, L::kSwz), idesc_s, kk != 0 ? 1u : 0u);
+                    for (int kk = 0; kk < HD / 16; ++kk) {
+                        const uint32_t off = (kk / kStepsPerBlk) * L::kBlkBytes + (kk % kStepsPerBlk) * 32;
+                        mma_f16_ss(d, smem_desc(qa + off, 16, 8 * L::kRowBytes, L::kSwz),
+                                   smem_desc(ka + off, 16, 8 * L::kRowBytes, L::kSwz), idesc_s,
+                                   kk != 0 ? 1u : 0u);
+                    }
+                    tc_commit(s_full(g));
+                    if (j == n_kt - 1) tc_commit(q_empty);   // Q is no longer read
+                    return true;
+                };
+                bool ok = issue_s(0);
+                if (ok && n_kt > 1) ok = issue_s(1);
+                for (int j = 0; ok && j < n_kt; ++j) {
+                    const int g = (g0 + j) & 1;
+                    const uint32_t t = tcount + j;
+                    const int st = static_cast<int>(t % STAGES);
+                    // the group's previous item has read its O accumulator
+                    if (j < 2 && !mbar_wait(o_free(g), (pcount[g] & 1u) ^ 1u, abort_flag)) { ok = false; break; }
+                    if (!mbar_wait(p_full(g), gcount[g] & 1u, abort_flag)) { ok = false; break; }
+                    if (!mbar_wait(v_full(st), (t / STAGES) & 1u, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t d = tmem_base + L::kColO + static_cast<uint32_t>(g * HD);
+                    const uint32_t pa = tmem_base + L::kColS + static_cast<uint32_t>(g * kAttnTile);
+                    const uint32_t va = sbase + L::kOffV + st * L::kTileBytes;
+#pragma unroll
+                    for (int kk = 0; kk < kAttnTile / 16; ++kk)
+                        mma_f16_ts(d, pa + kk * 8,
+                                   smem_desc(va + kk * 16 * L::kRowBytes, L::kBlkBytes, 8 * L::kRowBytes, L::kSwz),
+                                   idesc_o, (j >= 2 || kk != 0) ? 1u : 0u);
+                    tc_commit(o_done(g));
+                    tc_commit(kv_empty(st));
+                    ++gcount[g];
+                    if (j + 2 < n_kt && !issue_s(j + 2)) { ok = false; break; }
                 }
-                tc_commit(s_full(j & 1));
-                if (j == n_kt - 1) tc_commit(q_empty);   // Q is no longer read
-                return true;
-            };
-            bool ok = issue_s(0);
-            if (ok && n_kt > 1) ok = issue_s(1);
-            for (int j = 0; ok && j < n_kt; ++j) {
-                const int g = j & 1;
-                const uint32_t t = tcount + j;
-                const int st = static_cast<int>(t % STAGES);
-                // the previous item's epilogue has read both O accumulators
-                if (j == 0 && !mbar_wait(o_free, (qcount & 1u) ^ 1u, abort_flag)) { ok = false; break; }
-                if (!mbar_wait(p_full(g), gcount[g] & 1u, abort_flag)) { ok = false; break; }
-                if (!mbar_wait(v_full(st), (t / STAGES) & 1u, abort_flag)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t d = tmem_base + L::kColO + static_cast<uint32_t>(g * HD);
-                const uint32_t pa = tmem_base + L::kColS + static_cast<uint32_t>(g * kAttnTile);
-                const uint32_t va = sbase + L::kOffV + st * L::kTileBytes;
-#pragma unroll
-                for (int kk = 0; kk < kAttnTile / 16; ++kk)
-                    mma_f16_ts(d, pa + kk * 8, smem_desc(va + kk * 16 * L::kRowBytes, L::kBlkBytes,
-                                                         8 * L::kRowBytes, L::kSwz),
-                               idesc_o, (j >= 2 || kk != 0) ? 1u : 0u);
-                tc_commit(o_done(g));
-                tc_commit(kv_empty(st));
-                ++gcount[g];
-                if (j + 2 < n_kt && !issue_s(j + 2)) { ok = false; break; }
+                if (!ok) break;
+                ++pcount[g0];
+                if (n_kt > 1) ++pcount[g0 ^ 1];
+                tcount += n_kt;
+                ++qcount;
             }
-            if (!ok) break;
-            tcount += n_kt;
-            ++qcount;
+            tc_commit(drain_bar);
+            mbar_wait_drain(drain_bar, 0);
         }
-        tc_commit(drain_bar);
-        mbar_wait_drain(drain_bar, 0);
-    } else if (warp >= 2) {
-        // ------------------------------------------ softmax warpgroups --
-        const int grp = (warp - 2) >> 2;               // 0: even key tiles, 1: odd
+    } else {
+        // -------------------------------------------- softmax warpgroups --
+        regs_inc<192>();
+        const int grp = warp >> 2;                     // warpgroup 0 or 1
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;            // query row within the tile
         const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
@@ -339,15 +382,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t t_o0 = tmem_base + lane_off + L::kColO;
         const uint32_t t_o = t_o0 + static_cast<uint32_t>(grp * HD);
         const float c = p.scale_log2;
-        uint32_t gtiles = 0, icount = 0, ocount = 0, ccount = 0;
+        uint32_t gtiles = 0, icount = 0, ccount = 0, singles = 0;
         bool alive = true;
         for (int item = blockIdx.x; item < num_items && alive; item += gridDim.x, ++icount) {
             const int slot = static_cast<int>(icount & 1u);
             bool ok = mbar_wait(info_full(slot), (icount >> 1) & 1u, abort_flag);
             if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
-            const int n_kt = info[slot];
+            const int n_kt = info[2 * slot];
+            const int hole = info[2 * slot + 1];
             __syncwarp();
             if (lane == 0) mbar_arrive(info_empty(slot));
+            const int g0 = n_kt > 0 ? first_group(n_kt, singles) : 0;
 
             int stream, qt, k_lo, k_hi;
             attn_item(p, item, stream, qt);
@@ -371,27 +416,37 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 klo_r = 1;
                 khi_r = 0;
             }
-            const uint8_t* mrow = nullptr;
-            if (p.mask_kind == 2 && q_ok)
-                mrow = p.mask + b * p.ms0 + h * p.ms1 + static_cast<int64_t>(s) * p.ms2;
+            auto out_row = [&]() -> __half* {
+                const int64_t off = (p.out_layout == 1) ? ((static_cast<int64_t>(b) * p.S + s) * p.H + h) * HD
+                                                        : ((static_cast<int64_t>(b) * p.H + h) * p.S + s) * HD;
+                return reinterpret_cast<__half*>(p.out) + off;
+            };
+            if (n_kt == 0) {
+                if (grp == 0 && q_ok) {
+                    __half* op = out_row();
+#pragma unroll
+                    for (int i = 0; i < HD; i += 8) *reinterpret_cast<uint4*>(op + i) = make_uint4(0, 0, 0, 0);
+                }
+                continue;
+            }
+            const bool two = n_kt >= 2;
+            if (!two && grp != g0) continue;           // the other group owns this single-tile item
 
             float m_used = -INFINITY, l_run = 0.0f;
-            int mine = 0;
-            for (int j = grp; j < n_kt; j += 2, ++mine, ++gtiles) {
+            for (int j = (grp - g0) & 1; j < n_kt; j += 2, ++gtiles) {
                 const int kc0 = k_lo + j * kAttnTile;
                 // Allowed keys of this row in this tile as a 128-bit mask:
                 // bit i of allow[w] <-> key column 32 w + i.
                 uint32_t allow[4];
 #pragma unroll
                 for (int w = 0; w < 4; ++w) {
-                    // the row's key interval [klo_r, khi_r] clipped to this word
-                    const int a = max(klo_r - kc0 - 32 * w, 0);
-                    const int z = min(khi_r - kc0 - 32 * w, 31);
+                    const int lo = max(klo_r - kc0 - 32 * w, 0);
+                    const int hi = min(khi_r - kc0 - 32 * w, 31);
                     uint32_t bits = 0u;
-                    if (a <= z) bits = (z == 31 ? 0xffffffffu : ((1u << (z + 1)) - 1u)) & ~((1u << a) - 1u);
+                    if (lo <= hi) bits = (hi == 31 ? 0xffffffffu : ((1u << (hi + 1)) - 1u)) & ~((1u << lo) - 1u);
                     allow[w] = bits;
                 }
-                if (p.mask_kind == 1) {
+                if (p.mask_kind == 1 && kc0 + kAttnTile > hole) {
 #pragma unroll
                     for (int w = 0; w < 4; ++w) {
                         const int kc = kc0 + 32 * w + lane;
@@ -409,7 +464,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                         }
                         allow[w] &= __ballot_sync(0xffffffffu, allowed);
                     }
-                } else if (p.mask_kind == 2) {
+                } else if (p.mask_kind == 2 && q_ok) {
+                    const uint8_t* mrow = p.mask + b * p.ms0 + h * p.ms1 + static_cast<int64_t>(s) * p.ms2;
 #pragma unroll 1
                     for (int i = 0; i < kAttnTile; ++i) {
                         const int kc = kc0 + i;
@@ -422,31 +478,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 ok = mbar_wait(s_full(grp), gtiles & 1u, abort_flag);
                 if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
                 tc_fence_after();
-                // pass 1: row max over two 64-column halves, eight independent chains
+                // pass 1: row max, 32 columns at a time, eight independent chains
                 float mx8[8];
 #pragma unroll
                 for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
 #pragma unroll
-                for (int hf = 0; hf < 2; ++hf) {
-                    uint32_t sa[32], sb[32];
-                    tmem_ld_32x32b_x32(t_s + hf * 64, sa);
-                    tmem_ld_32x32b_x32(t_s + hf * 64 + 32, sb);
-                    tmem_ld_wait(sa);
-                    tmem_ld_wait(sb);
+                for (int q4 = 0; q4 < 4; ++q4) {
+                    uint32_t sr[32];
+                    tmem_ld_32x32b_x32(t_s + q4 * 32, sr);
+                    tmem_ld_wait(sr);
                     if (interior) {
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sa[i]));
-                            mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sb[i]));
-                        }
+                        for (int i = 0; i < 32; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sr[i]));
                     } else {
-                        const uint32_t wa = allow[2 * hf], wb = allow[2 * hf + 1];
+                        const uint32_t wq = allow[q4];
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            const float va = ((wa >> i) & 1u) ? __uint_as_float(sa[i]) : -INFINITY;
-                            const float vb = ((wb >> i) & 1u) ? __uint_as_float(sb[i]) : -INFINITY;
-                            mx8[i & 7] = fmaxf(mx8[i & 7], fmaxf(va, vb));
-                        }
+                        for (int i = 0; i < 32; ++i)
+                            mx8[i & 7] = fmaxf(mx8[i & 7], ((wq >> i) & 1u) ? __uint_as_float(sr[i]) : -INFINITY);
                     }
                 }
                 const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
@@ -482,34 +530,26 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     }
                 }
                 const float mc = (m_used == -INFINITY) ? 0.0f : m_used * c;
-                // pass 2: P = exp2(s c - m c) as fp16 over the S columns already
-                // read (keys 64 hf.. go to columns 32 hf..), row sum in fp32
+                // pass 2: P = exp2(s c - m c) as fp16, 32 keys at a time, written
+                // over S columns already read (keys 32 q.. go to columns 16 q..);
+                // the row sum stays fp32.
                 float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                for (int hf = 0; hf < 2; ++hf) {
-                    uint32_t sa[32], sb[32], pk[32];
-                    tmem_ld_32x32b_x32(t_s + hf * 64, sa);
-                    tmem_ld_32x32b_x32(t_s + hf * 64 + 32, sb);
-                    tmem_ld_wait(sa);
-                    tmem_ld_wait(sb);
-                    const uint32_t wa = interior ? 0xffffffffu : allow[2 * hf];
-                    const uint32_t wb = interior ? 0xffffffffu : allow[2 * hf + 1];
+                for (int q4 = 0; q4 < 4; ++q4) {
+                    uint32_t sr[32], pk[16];
+                    tmem_ld_32x32b_x32(t_s + q4 * 32, sr);
+                    tmem_ld_wait(sr);
+                    const uint32_t wq = interior ? 0xffffffffu : allow[q4];
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
-                        float p0 = fast_exp2(fmaf(__uint_as_float(sa[2 * i]), c, -mc));
-                        float p1 = fast_exp2(fmaf(__uint_as_float(sa[2 * i + 1]), c, -mc));
-                        float p2 = fast_exp2(fmaf(__uint_as_float(sb[2 * i]), c, -mc));
-                        float p3 = fast_exp2(fmaf(__uint_as_float(sb[2 * i + 1]), c, -mc));
-                        p0 = ((wa >> (2 * i)) & 1u) ? p0 : 0.0f;
-                        p1 = ((wa >> (2 * i + 1)) & 1u) ? p1 : 0.0f;
-                        p2 = ((wb >> (2 * i)) & 1u) ? p2 : 0.0f;
-                        p3 = ((wb >> (2 * i + 1)) & 1u) ? p3 : 0.0f;
+                        float p0 = fast_exp2(fmaf(__uint_as_float(sr[2 * i]), c, -mc));
+                        float p1 = fast_exp2(fmaf(__uint_as_float(sr[2 * i + 1]), c, -mc));
+                        p0 = ((wq >> (2 * i)) & 1u) ? p0 : 0.0f;
+                        p1 = ((wq >> (2 * i + 1)) & 1u) ? p1 : 0.0f;
                         sum8[i & 7] += p0 + p1;
-                        sum8[(i + 4) & 7] += p2 + p3;
                         pk[i] = pack_half2(p0, p1);
-                        pk[16 + i] = pack_half2(p2, p3);
                     }
-                    tmem_st_32x32b_x32(t_s + hf * 32, pk);
+                    tmem_st_32x32b_x16(t_s + q4 * 16, pk);
                 }
                 l_run += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
                 tmem_st_wait();
@@ -517,24 +557,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 mbar_arrive(p_full(grp));
             }
             if (!alive) break;
-            if (n_kt == 0) {
-                if (grp == 0 && q_ok) {
-                    int64_t off = (p.out_layout == 1) ? ((static_cast<int64_t>(b) * p.S + s) * p.H + h) * HD
-                                                      : ((static_cast<int64_t>(b) * p.H + h) * p.S + s) * HD;
-                    __half* op = reinterpret_cast<__half*>(p.out) + off;
-#pragma unroll
-                    for (int i = 0; i < HD; i += 8) *reinterpret_cast<uint4*>(op + i) = make_uint4(0, 0, 0, 0);
-                }
-                continue;
-            }
-            // With a single key tile group 1 had no work in this item.
-            const bool two = n_kt >= 2;
-            if (grp == 1 && !two) continue;
             // the last PV of this group has landed in O
             ok = mbar_wait(o_done(grp), (gtiles - 1) & 1u, abort_flag);
             if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
             tc_fence_after();
-            if (grp == 1) {
+            if (two && grp == 1) {
+                // hand (max, sum) to group 0, which merges both accumulators
                 ok = mbar_wait(comb_empty, (ccount & 1u) ^ 1u, abort_flag);
                 if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
                 comb[row] = make_float2(m_used, l_run);
@@ -557,44 +585,39 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             const float inv = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;
             a0 *= inv;
             a1 *= inv;
-            int64_t off = (p.out_layout == 1) ? ((static_cast<int64_t>(b) * p.S + s) * p.H + h) * HD
-                                              : ((static_cast<int64_t>(b) * p.H + h) * p.S + s) * HD;
-            __half* op = reinterpret_cast<__half*>(p.out) + off;
+            __half* op = out_row();
 #pragma unroll 1
-            for (int cc = 0; cc < HD; cc += 32) {
-                uint32_t o0[32], o1[32];
-                tmem_ld_32x32b_x32(t_o0 + cc, o0);
-                if (two) tmem_ld_32x32b_x32(t_o0 + HD + cc, o1);
-                tmem_ld_wait(o0);
-                if (two) tmem_ld_wait(o1);
+            for (int cc = 0; cc < HD; cc += 16) {
+                uint32_t o0[16], o1[16];
+                tmem_ld_32x32b_x16(t_o + cc, o0);
+                if (two) tmem_ld_32x32b_x16(t_o0 + HD + cc, o1);
+                tmem_ld_wait16(o0);
+                if (two) tmem_ld_wait16(o1);
+                uint32_t w[8];
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    o0[i] = __float_as_uint(two ? fmaf(__uint_as_float(o0[i]), a0, __uint_as_float(o1[i]) * a1)
-                                                : __uint_as_float(o0[i]) * a0);
+                for (int i = 0; i < 8; ++i) {
+                    const float v0 = two ? fmaf(__uint_as_float(o0[2 * i]), a0, __uint_as_float(o1[2 * i]) * a1)
+                                         : __uint_as_float(o0[2 * i]) * a0;
+                    const float v1 = two ? fmaf(__uint_as_float(o0[2 * i + 1]), a0, __uint_as_float(o1[2 * i + 1]) * a1)
+                                         : __uint_as_float(o0[2 * i + 1]) * a0;
+                    w[i] = pack_half2(v0, v1);
+                }
                 if (q_ok) {
-#pragma unroll
-                    for (int i = 0; i < 32; i += 8) {
-                        uint4 w;
-                        w.x = pack_half2(__uint_as_float(o0[i]), __uint_as_float(o0[i + 1]));
-                        w.y = pack_half2(__uint_as_float(o0[i + 2]), __uint_as_float(o0[i + 3]));
-                        w.z = pack_half2(__uint_as_float(o0[i + 4]), __uint_as_float(o0[i + 5]));
-                        w.w = pack_half2(__uint_as_float(o0[i + 6]), __uint_as_float(o0[i + 7]));
-                        *reinterpret_cast<uint4*>(op + cc + i) = w;
-                    }
+                    *reinterpret_cast<uint4*>(op + cc) = make_uint4(w[0], w[1], w[2], w[3]);
+                    *reinterpret_cast<uint4*>(op + cc + 8) = make_uint4(w[4], w[5], w[6], w[7]);
                 }
             }
             tc_fence_before();
-            mbar_arrive(o_free);
-            ++ocount;
+            mbar_arrive(o_free(grp));
+            if (two) mbar_arrive(o_free(1));
         }
-        (void)ocount;
     }
 
     // ------------------------------------------------------------ teardown --
     __syncwarp();
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == 9) {
         tc_fence_after();
         tmem_dealloc(tmem_base, L::kTmemCols);
     }

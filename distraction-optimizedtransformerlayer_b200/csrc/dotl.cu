@@ -16,6 +16,8 @@
 #include <cstdio>
 #include <mutex>
 #include <string>
+#include <algorithm>
+#include <utility>
 
 namespace {
 
@@ -71,6 +73,25 @@ int ensure_smem(Kernel kernel, uint32_t bytes, int dev, bool* done_flags) {
     return DOTL_OK;
 }
 
+// Launches with programmatic stream serialization, so the kernel's prologue
+// can overlap the previous kernel's tail (each kernel starts with
+// griddepcontrol.wait before it touches its inputs).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // ------------------------------------------------------------ tensor maps --
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -112,16 +133,39 @@ int encode_f16_map(CUtensorMap* map, const void* base, int rank, const cuuint64_
 // ------------------------------------------------------------------ GEMM --
 
 template <int BN, int STAGES, bool OUT_F16>
-int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const dotl::GemmParams& p, int dev,
-                cudaStream_t stream) {
+int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const dotl::GemmParams& p,
+                int dev, cudaStream_t stream) {
     using L = dotl::GemmSmem<BN, STAGES>;
     auto kernel = dotl::gemm_tc_kernel<BN, STAGES, OUT_F16>;
     static bool done[kMaxDevices] = {false};
     if (int rc = ensure_smem(kernel, L::kAlloc, dev, done)) return rc;
     const int tiles = p.num_m_tiles * p.num_n_tiles;
     const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
-    kernel<<<grid, dotl::kGemmThreads, L::kAlloc, stream>>>(ta, tw, p);
+    const cudaError_t e = launch_pdl(kernel, dim3(grid), dim3(dotl::kGemmThreads), L::kAlloc, stream, ta, tw, to, p);
+    if (e != cudaSuccess) return fail(DOTL_ECUDA, "dotl_linear: launch failed: %s", cudaGetErrorString(e));
     return check_launch("dotl_linear");
+}
+
+// N tile for an [M,N,K] problem, from a cost model in SM cycles: waves of
+// persistent tiles, each a fixed start-up plus K/64 steps that cost the larger
+// of the MMA time (128 x BN x 64 at 8192 FLOP/clk) and the time to stream the
+// A and W stage from L2 (about 120 bytes/clk per SM).
+int pick_tile_n(int64_t M, int64_t N, int64_t K, int sms) {
+    const int64_t mt = (M + dotl::kGemmBM - 1) / dotl::kGemmBM;
+    const int64_t nkb = (K + dotl::kGemmBK - 1) / dotl::kGemmBK;
+    int best = 128;
+    double best_cost = 1e300;
+    for (int bn : {256, 128, 64}) {
+        const int64_t tiles = mt * ((N + bn - 1) / bn);
+        const int64_t waves = (tiles + sms - 1) / sms;
+        const double step = std::max(2.0 * bn, (16384.0 + 128.0 * bn) / 120.0);
+        const double cost = static_cast<double>(waves) * (3000.0 + static_cast<double>(nkb) * step);
+        if (cost < best_cost * 0.97) {
+            best_cost = cost;
+            best = bn;
+        }
+    }
+    return best;
 }
 
 // ------------------------------------------------------------- attention --
@@ -135,7 +179,8 @@ int launch_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap&
     if (int rc = ensure_smem(kernel, L::kAlloc, dev, done)) return rc;
     const int items = p.num_streams * p.num_q_tiles;
     const int grid = items < sm_count(dev) ? items : sm_count(dev);
-    kernel<<<grid, dotl::kAttnThreads, L::kAlloc, stream>>>(tq, tk, tv, p);
+    const cudaError_t e = launch_pdl(kernel, dim3(grid), dim3(dotl::kAttnThreads), L::kAlloc, stream, tq, tk, tv, p);
+    if (e != cudaSuccess) return fail(DOTL_ECUDA, "dotl_attention: launch failed: %s", cudaGetErrorString(e));
     return check_launch("dotl_attention");
 }
 
@@ -223,14 +268,15 @@ int dotl_layernorm(const float* x, const float* sub, const float* weight, const 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int Di = static_cast<int>(D);
 
+    cudaError_t le = cudaSuccess;
 #define DOTL_LN(EPL, VEC)                                                                                      \
     do {                                                                                                       \
         if (normed_dtype == DOTL_F16)                                                                          \
-            dotl::ln_rows_kernel<EPL, VEC, __half><<<grid, block, 0, s>>>(                                     \
-                x, sub, weight, bias, x_new, static_cast<__half*>(normed), row_valid, rows, Di, eps);          \
+            le = launch_pdl(dotl::ln_rows_kernel<EPL, VEC, __half>, grid, block, 0, s, x, sub, weight, bias,  \
+                            x_new, static_cast<__half*>(normed), row_valid, rows, Di, eps);                    \
         else                                                                                                   \
-            dotl::ln_rows_kernel<EPL, VEC, float><<<grid, block, 0, s>>>(                                      \
-                x, sub, weight, bias, x_new, static_cast<float*>(normed), row_valid, rows, Di, eps);           \
+            le = launch_pdl(dotl::ln_rows_kernel<EPL, VEC, float>, grid, block, 0, s, x, sub, weight, bias,   \
+                            x_new, static_cast<float*>(normed), row_valid, rows, Di, eps);                     \
     } while (0)
 
     if (vec) {
@@ -249,6 +295,7 @@ int dotl_layernorm(const float* x, const float* sub, const float* weight, const 
         else DOTL_LN(64, false);
     }
 #undef DOTL_LN
+    if (le != cudaSuccess) return fail(DOTL_ECUDA, "%s: launch failed: %s", who, cudaGetErrorString(le));
     return check_launch(who);
 }
 
@@ -277,16 +324,14 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
     if ((resid_mode == DOTL_RESID_ADD_MASKSUB || resid_mode == DOTL_RESID_ADD_MASKALL) && row_valid == nullptr)
         return fail(DOTL_EINVAL, "%s: masked residual mode needs row_valid", who);
     if (!aligned16(bias)) return fail(DOTL_EUNSUPPORTED, "%s: bias must be 16-byte aligned", who);
+    if (resid_mode != DOTL_RESID_NONE && out_dtype != DOTL_F32)
+        return fail(DOTL_EUNSUPPORTED, "%s: residual epilogues write the fp32 residual stream (out dtype DOTL_F32)", who);
 
     int dev;
     if (int rc = current_device(&dev)) return rc;
     int bn = tile_n;
-    if (bn == 0) {
-        // 256-wide tiles halve the A re-reads; take them when they still fill the SMs.
-        const int64_t mt = (M + dotl::kGemmBM - 1) / dotl::kGemmBM;
-        bn = (N >= 256 && mt * ((N + 255) / 256) >= sm_count(dev)) ? 256 : 128;
-    }
-    if (bn != 128 && bn != 256) return fail(DOTL_EINVAL, "%s: tile_n must be 0, 128 or 256", who);
+    if (bn == 0) bn = pick_tile_n(M, N, K, sm_count(dev));
+    if (bn != 64 && bn != 128 && bn != 256) return fail(DOTL_EINVAL, "%s: tile_n must be 0, 64, 128 or 256", who);
 
     CUtensorMap ta, tw;
     const cuuint64_t adims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
@@ -295,6 +340,21 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
     const cuuint64_t wdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
     const cuuint64_t wstr[1] = {static_cast<cuuint64_t>(ldw) * 2};
     if (int rc = encode_f16_map(&tw, w, 2, wdims, wstr, dotl::kGemmBK, static_cast<uint32_t>(bn), who)) return rc;
+    // output: 32 x 32 boxes (128 B fp32 rows with 128B swizzle, 64 B fp16 rows with 64B swizzle)
+    CUtensorMap to;
+    {
+        EncodeTiledFn fn = encode_fn();
+        if (fn == nullptr) return fail(DOTL_ECUDA, "%s: cuTensorMapEncodeTiled is unavailable from the driver", who);
+        const cuuint64_t odims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M)};
+        const cuuint64_t ostr[1] = {static_cast<cuuint64_t>(ldo) * (out_dtype == DOTL_F16 ? 2 : 4)};
+        const cuuint32_t obox[2] = {32u, 32u};
+        const cuuint32_t oes[2] = {1, 1};
+        const CUresult r = fn(&to, out_dtype == DOTL_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                              2, out, odims, ostr, obox, oes, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              out_dtype == DOTL_F16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return fail(DOTL_ECUDA, "%s: cuTensorMapEncodeTiled (out) failed (CUresult %d)", who, (int)r);
+    }
 
     dotl::GemmParams p;
     p.M = static_cast<int>(M);
@@ -312,10 +372,13 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
     p.ldo = ldo;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (bn == 256)
-        return out_dtype == DOTL_F16 ? launch_gemm<256, 4, true>(ta, tw, p, dev, s)
-                                     : launch_gemm<256, 4, false>(ta, tw, p, dev, s);
-    return out_dtype == DOTL_F16 ? launch_gemm<128, 6, true>(ta, tw, p, dev, s)
-                                 : launch_gemm<128, 6, false>(ta, tw, p, dev, s);
+        return out_dtype == DOTL_F16 ? launch_gemm<256, 4, true>(ta, tw, to, p, dev, s)
+                                     : launch_gemm<256, 4, false>(ta, tw, to, p, dev, s);
+    if (bn == 64)
+        return out_dtype == DOTL_F16 ? launch_gemm<64, 7, true>(ta, tw, to, p, dev, s)
+                                     : launch_gemm<64, 7, false>(ta, tw, to, p, dev, s);
+    return out_dtype == DOTL_F16 ? launch_gemm<128, 5, true>(ta, tw, to, p, dev, s)
+                                 : launch_gemm<128, 5, false>(ta, tw, to, p, dev, s);
 }
 
 int dotl_attention(const void* q, const void* k, const void* v, int B, int H, int S, int head_dim,

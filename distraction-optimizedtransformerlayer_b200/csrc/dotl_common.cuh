@@ -105,6 +105,25 @@ __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity) {
     return true;
 }
 
+// ---------------------------------------------- programmatic dependent launch --
+// Kernels are launched with programmatic stream serialization: the next kernel
+// in the stream may start its prologue while this one drains. pdl_wait() blocks
+// until every kernel this one depends on has completed and its writes are
+// visible; it must precede the first read of a predecessor's output (and every
+// TMEM allocation, so a waiting CTA never holds tensor memory).
+// pdl_launch_dependents() lets the next kernel begin launching; its own
+// pdl_wait() still waits for this kernel's completion.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Per-warpgroup register budget (all four warps of a warpgroup execute it).
+template <int N>
+__device__ __forceinline__ void regs_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N)); }
+template <int N>
+__device__ __forceinline__ void regs_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N)); }
+
 // --------------------------------------------------------------------- TMA --
 
 __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
@@ -128,6 +147,23 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
         "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
         : "memory");
 }
+
+// Shared -> global tensor store (bulk-group completion); clips at the tensor
+// bounds. The smem source must not be rewritten before bulk_wait_read().
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(c0), "r"(c1), "r"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// At most N committed bulk groups of this thread still reading shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Every committed bulk group of this thread complete (writes performed).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // ----------------------------------------------------------------- tcgen05 --
 
@@ -238,9 +274,39 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
         : "memory");
 }
 
+// 32 lanes x 16 consecutive 32-bit TMEM columns from registers (warp-collective).
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
 // Completes every outstanding tcgen05.st of this thread.
 __device__ __forceinline__ void tmem_st_wait() {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit TMEM columns (warp-collective).
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld_wait16(uint32_t (&r)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                   "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                   "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+                 :
+                 : "memory");
 }
 
 // Completes every outstanding tcgen05.ld of this thread. The registers are
@@ -259,9 +325,36 @@ __device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
 
 // -------------------------------------------------------------- arithmetic --
 
-// Exact (erf) GELU, the form F.gelu(approximate="none") computes.
+// Exact (erf) GELU, the form F.gelu(approximate="none") computes, using
+// CUDA's erff.
 __device__ __forceinline__ float gelu_erf(float v) {
     return 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
+}
+
+// erf(x) for x >= 0 by Abramowitz & Stegun, Handbook of Mathematical
+// Functions, formula 7.1.28 (Hastings): erf(x) = 1 - (1 + a1 x + ... + a6 x^6)^-16,
+// absolute error <= 3e-7. Horner, four squarings and one fast reciprocal: no
+// exponential, no branches.
+__device__ __forceinline__ float erf_as7128(float x) {
+    float t = fmaf(x, 0.0000430638f, 0.0002765672f);
+    t = fmaf(t, x, 0.0001520143f);
+    t = fmaf(t, x, 0.0092705272f);
+    t = fmaf(t, x, 0.0422820123f);
+    t = fmaf(t, x, 0.0705230784f);
+    t = fmaf(t, x, 1.0f);
+    t = t * t;
+    t = t * t;
+    t = t * t;
+    t = t * t;
+    return 1.0f - __fdividef(1.0f, t);
+}
+
+// GELU(v) = v * Phi(v) = 0.5 v (1 + erf(v / sqrt 2)) with erf from A&S 7.1.28;
+// agrees with gelu_erf to ~3e-7 * |v| (tests/test_gpu_20_linear.py checks it
+// against erff on the device).
+__device__ __forceinline__ float gelu_fast(float v) {
+    const float e = erf_as7128(fabsf(v) * 0.70710678118654752440f);
+    return 0.5f * v * (1.0f + copysignf(e, v));
 }
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {

@@ -10,9 +10,10 @@
 //     the same A row-block and the weight matrix stays L2 resident;
 //   * warp-specialised: warp 0 issues TMA loads into a STAGES-deep ring of
 //     128B-swizzled smem tiles, warp 1 issues tcgen05.mma (M=128, N=BN, K=16)
-//     into one of two TMEM accumulators, warps 2-5 drain the other
-//     accumulator through tcgen05.ld and run the fused epilogue, so the
-//     epilogue of tile i overlaps the main loop of tile i+1;
+//     into one of two TMEM accumulators, warps 2-9 drain the other
+//     accumulator through tcgen05.ld, run the fused epilogue and TMA-store
+//     the result through swizzled smem, so the epilogue of tile i overlaps
+//     the main loop of tile i+1;
 //   * epilogues: bias, bias+GELU (fp16 out, the FFN hidden), bias + residual
 //     with an optional padded-row mask (fp32 out, the residual stream).
 //
@@ -27,7 +28,7 @@ namespace dotl {
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;                  // one 128-byte swizzle atom of fp16
-constexpr int kGemmThreads = 192;            // 6 warps
+constexpr int kGemmThreads = 320;            // producer, MMA, 8 epilogue warps
 constexpr uint32_t kGemmATileBytes = kGemmBM * kGemmBK * 2;
 
 enum GemmResidMode : int {
@@ -56,7 +57,10 @@ struct GemmSmem {
     static constexpr uint32_t kStageBytes = kGemmATileBytes + kBTileBytes;
     static constexpr uint32_t kOffA = 0;
     static constexpr uint32_t kOffB = STAGES * kGemmATileBytes;
-    static constexpr uint32_t kOffBar = kOffB + STAGES * kBTileBytes;
+    // per epilogue warp: one 32-row x 128-byte staging buffer for TMA stores
+    static constexpr uint32_t kOffStage = kOffB + STAGES * kBTileBytes;
+    static constexpr uint32_t kStageBufBytes = 32 * 128;
+    static constexpr uint32_t kOffBar = kOffStage + 8 * kStageBufBytes;
     // full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], drain
     static constexpr uint32_t kNumBars = 2 * STAGES + 5;
     static constexpr uint32_t kOffSlot = kOffBar + kNumBars * 8;
@@ -68,8 +72,8 @@ struct GemmSmem {
 
 template <int BN, int STAGES, bool OUT_F16>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                   const __grid_constant__ CUtensorMap tmap_w, const GemmParams p) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
+                   const __grid_constant__ CUtensorMap tmap_out, const GemmParams p) {
     using L = GemmSmem<BN, STAGES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -94,14 +98,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(accf_bar(b), 1);
-            mbar_init(acce_bar(b), 128);
+            mbar_init(acce_bar(b), 256);
         }
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
         fence_barrier_init();
         tma_prefetch_map(&tmap_a);
         tma_prefetch_map(&tmap_w);
+        tma_prefetch_map(&tmap_out);
     }
+    pdl_wait();
+    pdl_launch_dependents();
     if (warp == 1) {
         tmem_alloc(smem_u32(tmem_slot), L::kTmemCols);
         tmem_relinquish();
@@ -183,8 +190,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         mbar_wait_drain(drain_bar, 0);
     } else if (warp >= 2) {
         // -------------------------------------------------------- epilogue --
-        const int quarter = warp & 3;             // TMEM lanes this warp may read
+        // Eight warps, two per TMEM lane quarter (the 32 rows a warp may
+        // read); the two split the tile's 32-column chunks alternately. Per
+        // chunk a warp reads the accumulator, applies bias / GELU / residual /
+        // row mask, writes the 32-row block into a swizzled smem buffer
+        // (128 B rows for fp32, 64 B for fp16; conflict-free) and one lane
+        // TMA-stores it, so every store is a full-line bulk copy.
+        constexpr int kCW = 32;
+        constexpr int kRowB = OUT_F16 ? 64 : 128;       // staged bytes per row
+        const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;
         const int row_in_tile = quarter * 32 + lane;
+        const uint32_t stage_addr = sbase + L::kOffStage + static_cast<uint32_t>(warp - 2) * L::kStageBufBytes;
+        uint8_t* srow = smem + L::kOffStage + (warp - 2) * L::kStageBufBytes + lane * kRowB;
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -201,79 +219,79 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
-            for (int c = 0; c < BN; c += 32) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(t_row + c, r);
-                tmem_ld_wait(r);
+            for (int c = half * kCW; c < BN; c += 2 * kCW) {
                 const int nc = n0 + c;
-                if (!row_ok || nc >= p.N) continue;
-                float v[32];
+                float v[kCW];
+                {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(t_row + c, r);
+                    tmem_ld_wait(r);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-                const bool full_chunk = (nc + 32 <= p.N);
-                if (full_chunk) {
-#pragma unroll
-                    for (int j = 0; j < 32; j += 4) {
-                        const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + nc + j));
-                        v[j] += bb.x; v[j + 1] += bb.y; v[j + 2] += bb.z; v[j + 3] += bb.w;
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (nc + j < p.N) v[j] += __ldg(p.bias + nc + j);
+                    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
                 }
-                if (p.act == 1) {
+                if (nc < p.N) {
+                    if (nc + kCW <= p.N) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
-                }
-                if (p.resid_mode != kResidNone) {
-                    const float* rp = p.resid + static_cast<int64_t>(row) * p.ldr + nc;
-                    const bool keep_sub = valid || p.resid_mode == kResidAdd;
-                    const bool keep_all = valid || p.resid_mode != kResidAddMaskAll;
-                    if (full_chunk) {
-#pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
-                            const float4 rr = *reinterpret_cast<const float4*>(rp + j);
-                            v[j] = keep_all ? rr.x + (keep_sub ? v[j] : 0.0f) : 0.0f;
-                            v[j + 1] = keep_all ? rr.y + (keep_sub ? v[j + 1] : 0.0f) : 0.0f;
-                            v[j + 2] = keep_all ? rr.z + (keep_sub ? v[j + 2] : 0.0f) : 0.0f;
-                            v[j + 3] = keep_all ? rr.w + (keep_sub ? v[j + 3] : 0.0f) : 0.0f;
+                        for (int j = 0; j < kCW; j += 4) {
+                            const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + nc + j));
+                            v[j] += bb.x; v[j + 1] += bb.y; v[j + 2] += bb.z; v[j + 3] += bb.w;
                         }
                     } else {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (nc + j < p.N)
-                                v[j] = keep_all ? rp[j] + (keep_sub ? v[j] : 0.0f) : 0.0f;
+                        for (int j = 0; j < kCW; ++j)
+                            if (nc + j < p.N) v[j] += __ldg(p.bias + nc + j);
+                    }
+                    if (p.act == 1) {
+#pragma unroll
+                        for (int j = 0; j < kCW; ++j) v[j] = gelu_fast(v[j]);
+                    }
+                    if (p.resid_mode != kResidNone && row_ok) {
+                        const float* rp = p.resid + static_cast<int64_t>(row) * p.ldr + nc;
+                        const bool keep_sub = valid || p.resid_mode == kResidAdd;
+                        const bool keep_all = valid || p.resid_mode != kResidAddMaskAll;
+                        if (nc + kCW <= p.N) {
+#pragma unroll
+                            for (int j = 0; j < kCW; j += 4) {
+                                const float4 rr = *reinterpret_cast<const float4*>(rp + j);
+                                v[j] = keep_all ? rr.x + (keep_sub ? v[j] : 0.0f) : 0.0f;
+                                v[j + 1] = keep_all ? rr.y + (keep_sub ? v[j + 1] : 0.0f) : 0.0f;
+                                v[j + 2] = keep_all ? rr.z + (keep_sub ? v[j + 2] : 0.0f) : 0.0f;
+                                v[j + 3] = keep_all ? rr.w + (keep_sub ? v[j + 3] : 0.0f) : 0.0f;
+                            }
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < kCW; ++j)
+                                if (nc + j < p.N) v[j] = keep_all ? rp[j] + (keep_sub ? v[j] : 0.0f) : 0.0f;
+                        }
                     }
                 }
+                // the previous store from this buffer has read it
+                if (lane == 0) bulk_wait_read<0>();
+                __syncwarp();
                 if constexpr (OUT_F16) {
-                    __half* op = reinterpret_cast<__half*>(p.out) + static_cast<int64_t>(row) * p.ldo + nc;
-                    if (full_chunk) {
+                    // 64 B rows, 64B swizzle: granule q of row r at q ^ ((r >> 1) & 3)
 #pragma unroll
-                        for (int j = 0; j < 32; j += 8) {
-                            uint4 h;
-                            h.x = pack_half2(v[j], v[j + 1]);
-                            h.y = pack_half2(v[j + 2], v[j + 3]);
-                            h.z = pack_half2(v[j + 4], v[j + 5]);
-                            h.w = pack_half2(v[j + 6], v[j + 7]);
-                            *reinterpret_cast<uint4*>(op + j) = h;
-                        }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (nc + j < p.N) op[j] = __float2half_rn(v[j]);
+                    for (int q = 0; q < 4; ++q) {
+                        uint4 w;
+                        w.x = pack_half2(v[8 * q], v[8 * q + 1]);
+                        w.y = pack_half2(v[8 * q + 2], v[8 * q + 3]);
+                        w.z = pack_half2(v[8 * q + 4], v[8 * q + 5]);
+                        w.w = pack_half2(v[8 * q + 6], v[8 * q + 7]);
+                        *reinterpret_cast<uint4*>(srow + ((q ^ ((lane >> 1) & 3)) << 4)) = w;
                     }
                 } else {
-                    float* op = reinterpret_cast<float*>(p.out) + static_cast<int64_t>(row) * p.ldo + nc;
-                    if (full_chunk) {
+                    // 128 B rows, 128B swizzle: granule q of row r at q ^ (r & 7)
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4)
-                            *reinterpret_cast<float4*>(op + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (nc + j < p.N) op[j] = v[j];
-                    }
+                    for (int q = 0; q < 8; ++q)
+                        *reinterpret_cast<uint4*>(srow + ((q ^ (lane & 7)) << 4)) =
+                            make_uint4(__float_as_uint(v[4 * q]), __float_as_uint(v[4 * q + 1]),
+                                       __float_as_uint(v[4 * q + 2]), __float_as_uint(v[4 * q + 3]));
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0 && nc < p.N) {
+                    tma_store_2d(&tmap_out, stage_addr, nc, m_blk * kGemmBM + quarter * 32);
+                    bulk_commit();
                 }
             }
             tc_fence_before();
@@ -283,6 +301,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 acc_phase ^= 1u;
             }
         }
+        if (lane == 0) bulk_wait_all();
     }
 
     // ------------------------------------------------------------ teardown --

@@ -47,6 +47,8 @@ __global__ void __launch_bounds__(kLnWarpsPerBlock * 32)
                    const float* __restrict__ w, const float* __restrict__ b,
                    float* __restrict__ x_new, NormT* __restrict__ normed,
                    const uint8_t* __restrict__ row_valid, int64_t rows, int D, float eps) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int lane = threadIdx.x & 31;
     const int64_t row = static_cast<int64_t>(blockIdx.x) * kLnWarpsPerBlock + (threadIdx.x >> 5);
     if (row >= rows) return;

@@ -109,3 +109,19 @@ def test_gemm_rejects(kernels):
     with pytest.raises(RuntimeError, match="x's last dimension must match"):
         kernels.linear_bias(torch.randn(4, 32, device="cuda"), torch.randn(8, 16, device="cuda"),
                             torch.randn(8, device="cuda"))
+
+
+def test_gelu_epilogue_matches_exact_erf(kernels):
+    """The epilogue's GELU (erf from Abramowitz & Stegun 7.1.28, |error| <= 3e-7)
+    against the exact erf GELU in float64, over every fp16 value in [-12, 12]."""
+    v = torch.arange(-12.0, 12.0, 2.0 ** -9, device="cuda").half().unique()
+    M = v.numel()
+    a = torch.zeros(M, 8, device="cuda", dtype=torch.float16)
+    a[:, 0] = v
+    w = torch.zeros(8, 8, device="cuda", dtype=torch.float16)
+    w[0, 0] = 1.0
+    b = torch.zeros(8, device="cuda")
+    out = kernels.linear_fp16(a, w, b, act=1)[:, 0].double()
+    ref = F.gelu(v.double(), approximate="none")
+    err = (out - ref).abs()
+    assert (err <= 1e-6 * (1.0 + v.double().abs())).all(), err.max().item()
