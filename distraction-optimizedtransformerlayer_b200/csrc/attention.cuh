@@ -482,16 +482,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 float mx8[8];
 #pragma unroll
                 for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
-#pragma unroll
+#pragma unroll 1
                 for (int q4 = 0; q4 < 4; ++q4) {
                     uint32_t sr[32];
                     tmem_ld_32x32b_x32(t_s + q4 * 32, sr);
                     tmem_ld_wait(sr);
                     if (interior) {
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sr[i]));
+                        for (int i = 0; i < 32; i += 2)
+                            mx8[(i >> 1) & 7] = fmax3(mx8[(i >> 1) & 7], __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
                     } else {
-                        const uint32_t wq = allow[q4];
+                        const uint32_t wq = q4 == 0 ? allow[0] : q4 == 1 ? allow[1] : q4 == 2 ? allow[2] : allow[3];
 #pragma unroll
                         for (int i = 0; i < 32; ++i)
                             mx8[i & 7] = fmaxf(mx8[i & 7], ((wq >> i) & 1u) ? __uint_as_float(sr[i]) : -INFINITY);
@@ -534,20 +535,30 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 // over S columns already read (keys 32 q.. go to columns 16 q..);
                 // the row sum stays fp32.
                 float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
+#pragma unroll 1
                 for (int q4 = 0; q4 < 4; ++q4) {
                     uint32_t sr[32], pk[16];
                     tmem_ld_32x32b_x32(t_s + q4 * 32, sr);
                     tmem_ld_wait(sr);
-                    const uint32_t wq = interior ? 0xffffffffu : allow[q4];
+                    if (interior) {
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        float p0 = fast_exp2(fmaf(__uint_as_float(sr[2 * i]), c, -mc));
-                        float p1 = fast_exp2(fmaf(__uint_as_float(sr[2 * i + 1]), c, -mc));
-                        p0 = ((wq >> (2 * i)) & 1u) ? p0 : 0.0f;
-                        p1 = ((wq >> (2 * i + 1)) & 1u) ? p1 : 0.0f;
-                        sum8[i & 7] += p0 + p1;
-                        pk[i] = pack_half2(p0, p1);
+                        for (int i = 0; i < 16; ++i) {
+                            const float p0 = fast_exp2(fmaf(__uint_as_float(sr[2 * i]), c, -mc));
+                            const float p1 = fast_exp2(fmaf(__uint_as_float(sr[2 * i + 1]), c, -mc));
+                            sum8[i & 7] += p0 + p1;
+                            pk[i] = pack_half2(p0, p1);
+                        }
+                    } else {
+                        const uint32_t wq = q4 == 0 ? allow[0] : q4 == 1 ? allow[1] : q4 == 2 ? allow[2] : allow[3];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            float p0 = fast_exp2(fmaf(__uint_as_float(sr[2 * i]), c, -mc));
+                            float p1 = fast_exp2(fmaf(__uint_as_float(sr[2 * i + 1]), c, -mc));
+                            p0 = ((wq >> (2 * i)) & 1u) ? p0 : 0.0f;
+                            p1 = ((wq >> (2 * i + 1)) & 1u) ? p1 : 0.0f;
+                            sum8[i & 7] += p0 + p1;
+                            pk[i] = pack_half2(p0, p1);
+                        }
                     }
                     tmem_st_32x32b_x16(t_s + q4 * 16, pk);
                 }
