@@ -365,6 +365,31 @@ def _op_breakdown(model, x, mask, reps, kernels, cfg):
     return out
 
 
+def _allreduce_roofline(dist, dev, numel, world, reps=20):
+    """One layer's all-reduce (an fp32 [T, d_model] partial sum) timed alone:
+    bus bandwidth 2 (P-1)/P * bytes / time against the measured 8-rank
+    NVLink all-reduce bus bandwidth of this pool (725 GB/s at 1 GiB)."""
+    buf = torch.ones(numel, dtype=torch.float32, device=dev)
+    for _ in range(3):
+        dist.all_reduce(buf)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(reps):
+        dist.all_reduce(buf)
+    ev1.record()
+    torch.cuda.synchronize(dev)
+    ms = ev0.elapsed_time(ev1) / reps
+    ms = max_over_ranks([ms], dist, dev)[0]
+    achieved = 2.0 * (world - 1) / world * numel * 4 / (ms / 1e3) / 1e9
+    return {"kernel": "nccl_allreduce_fp32_partials", "bound": "nvlink", "achieved": achieved,
+            "peak": 725.0, "unit": "GB/s", "frac": achieved / 725.0,
+            "peak_source": "measured 8-rank all-reduce bus bandwidth of this pool", "traffic": None,
+            "ms_per_allreduce": ms, "allreduces_per_step": 2}
+
+
 def _traffic_for(config_id, kernel):
     path = os.path.join(REPO, "profiles", "traffic.json")
     try:
@@ -399,8 +424,17 @@ def run_ours(args, rank, world, local_rank):
     cfg = _Cfg(args.config, args.layers)
     model = OptimizedTransformer(cfg)
     _init_model(model, SEED)
-    model = model.to(dev).eval()
-    lo, hi = shard_rows(cfg.batch_size, world, rank, args.strong)
+    if args.tp:
+        if world < 2:
+            raise SystemExit("--tp needs torchrun with at least 2 ranks")
+        from optimized.tensor_parallel import TensorParallelTransformer
+
+        state = {k: v.detach() for k, v in model.state_dict().items()}
+        model = TensorParallelTransformer(cfg, state, device=dev)
+        args.strong = True
+    else:
+        model = model.to(dev).eval()
+    lo, hi = (0, cfg.batch_size) if args.tp else shard_rows(cfg.batch_size, world, rank, args.strong)
     if args.strong:
         x_all, mask_all = _synthetic_case(cfg, SEED, cfg.batch_size)
         x_cpu = x_all[lo:hi].contiguous()
@@ -411,6 +445,7 @@ def run_ours(args, rank, world, local_rank):
     mask = mask_cpu.to(dev) if mask_cpu is not None else None
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
     tokens_per_rank = (hi - lo) * cfg.seq_len
+    job_tokens = cfg.batch_size * cfg.seq_len if args.tp else world * tokens_per_rank
     stream = torch.cuda.current_stream(dev)
 
     def barrier():
@@ -472,14 +507,34 @@ def run_ours(args, rank, world, local_rank):
     total_ms, e2e_ms = max_over_ranks([total_ms, e2e_ms], dist, dev)
 
     breakdown = None
-    if rank == 0:
+    allreduce = None
+    if args.tp:
+        allreduce = _allreduce_roofline(dist, dev, x.numel(), world)
+    elif rank == 0:
         with torch.inference_mode():
             breakdown = _op_breakdown(model, x, mask, 20, kernels, cfg)
     word = kernels.device_error(clear=True)
     if word:
         raise RuntimeError(f"device error word {word:#x} after the timed run")
 
-    if rank == 0:
+    if rank == 0 and args.tp:
+        line = {
+            "metric": METRIC, "value": job_tokens * args.steps / (total_ms / 1e3), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": _describe(args.config), "global_batch": cfg.batch_size,
+                       "seq_len": cfg.seq_len, "layers": cfg.num_layers, "parallelism": f"tp{world}",
+                       "l2": "flushed between steps (256 MiB write)", "cuda_graph": False,
+                       "arithmetic": "fp16 tensor-core operands, fp32 accumulate, fp32 partial sums all-reduced"},
+            "clocks": clocks,
+            "e2e": {"value": job_tokens * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": (1 + 7 * cfg.num_layers) * args.steps,
+            "roofline": allreduce,
+        }
+        print(json.dumps(line), flush=True)
+    elif rank == 0:
         hbm, tflops, _tsus, peak_kind = _peaks()
         dom = max(breakdown, key=lambda r: r["ms"])
         if dom["bound"] == "tensor":
@@ -489,7 +544,7 @@ def run_ours(args, rank, world, local_rank):
             achieved = dom["work"] / (dom["ms"] / 1e3) / 1e9
             peak, unit = hbm, "GB/s"
         launches_per_step = 1 + 7 * cfg.num_layers
-        value = world * tokens_per_rank * args.steps / (total_ms / 1e3)
+        value = job_tokens * args.steps / (total_ms / 1e3)
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
@@ -502,7 +557,7 @@ def run_ours(args, rank, world, local_rank):
                        "cuda_graph": oconfig.CUDA_GRAPH != "off",
                        "arithmetic": "fp16 tensor-core operands, fp32 accumulate, fp32 I/O and LN"},
             "clocks": clocks,
-            "e2e": {"value": world * tokens_per_rank * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
+            "e2e": {"value": job_tokens * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches_per_step * args.steps,
             "roofline": {"kernel": dom["kernel"], "bound": "tensor" if dom["bound"] == "tensor" else "hbm",
@@ -518,7 +573,8 @@ def run_ours(args, rank, world, local_rank):
             line["cpu_baseline"] = _cpu_layer_tokens_per_s(cfg, budget_s=10.0)
         print(json.dumps(line), flush=True)
     if dist is not None:
-        model.release_graphs()
+        if hasattr(model, "release_graphs"):
+            model.release_graphs()
         dist.barrier()
         dist.destroy_process_group()
     return 0
@@ -560,6 +616,9 @@ def main() -> int:
     ap.add_argument("--layers", type=int, default=1)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-graph", action="store_true", help="time the eager path (no CUDA graph)")
+    ap.add_argument("--tp", action="store_true",
+                    help="tensor parallel across all ranks (heads and FFN columns sharded, two NCCL "
+                         "all-reduces per layer); one global batch per step")
     ap.add_argument("--strong", action="store_true",
                     help="split the config's batch across ranks (strong scaling) instead of a full batch per rank")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -307,7 +307,7 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
     if (M > (int64_t)0x7fffffff - 256 || N > 0x7fffffff || K > 0x7fffffff)
         return fail(DOTL_EUNSUPPORTED, "%s: dimensions must fit in 31 bits", who);
     if (act != 0 && act != 1) return fail(DOTL_EINVAL, "%s: act must be 0 (none) or 1 (GELU)", who);
-    if (resid_mode < DOTL_RESID_NONE || resid_mode > DOTL_RESID_ADD_MASKALL)
+    if (resid_mode < DOTL_RESID_NONE || resid_mode > DOTL_MASK_ROWS)
         return fail(DOTL_EINVAL, "%s: unknown residual mode %d", who, resid_mode);
     if (out_dtype != DOTL_F32 && out_dtype != DOTL_F16) return fail(DOTL_EINVAL, "%s: out dtype must be DOTL_F32 or DOTL_F16", who);
     if (M == 0) return DOTL_OK;
@@ -317,14 +317,15 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
     if (!aligned16(a) || !aligned16(w)) return fail(DOTL_EUNSUPPORTED, "%s: a and w must be 16-byte aligned", who);
     if (N % 8 != 0) return fail(DOTL_EUNSUPPORTED, "%s: N=%lld must be a multiple of 8", who, (long long)N);
     if (ldo < N || !aligned16(out) || ldo % 8 != 0) return fail(DOTL_EUNSUPPORTED, "%s: out must be 16-byte aligned with ldo >= N, ldo %% 8 == 0", who);
-    if (resid_mode != DOTL_RESID_NONE) {
+    if (resid_mode != DOTL_RESID_NONE && resid_mode != DOTL_MASK_ROWS) {
         if (resid == nullptr) return fail(DOTL_EINVAL, "%s: residual mode %d needs resid", who, resid_mode);
         if (!aligned16(resid) || ldr % 4 != 0 || ldr < N) return fail(DOTL_EUNSUPPORTED, "%s: resid must be 16-byte aligned with ldr >= N, ldr %% 4 == 0", who);
     }
-    if ((resid_mode == DOTL_RESID_ADD_MASKSUB || resid_mode == DOTL_RESID_ADD_MASKALL) && row_valid == nullptr)
+    if ((resid_mode == DOTL_RESID_ADD_MASKSUB || resid_mode == DOTL_RESID_ADD_MASKALL || resid_mode == DOTL_MASK_ROWS) &&
+        row_valid == nullptr)
         return fail(DOTL_EINVAL, "%s: masked residual mode needs row_valid", who);
     if (!aligned16(bias)) return fail(DOTL_EUNSUPPORTED, "%s: bias must be 16-byte aligned", who);
-    if (resid_mode != DOTL_RESID_NONE && out_dtype != DOTL_F32)
+    if (resid_mode != DOTL_RESID_NONE && resid_mode != DOTL_MASK_ROWS && out_dtype != DOTL_F32)
         return fail(DOTL_EUNSUPPORTED, "%s: residual epilogues write the fp32 residual stream (out dtype DOTL_F32)", who);
 
     int dev;

@@ -36,6 +36,7 @@ enum GemmResidMode : int {
     kResidAdd = 1,        // out = resid + (acc + bias)
     kResidAddMaskSub = 2, // out = resid + (row valid ? acc + bias : 0)
     kResidAddMaskAll = 3, // out = row valid ? resid + acc + bias : 0
+    kMaskRows = 4,        // out = row valid ? acc + bias : 0 (no residual)
 };
 
 struct GemmParams {
@@ -245,7 +246,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
                         for (int j = 0; j < kCW; ++j) v[j] = gelu_fast(v[j]);
                     }
-                    if (p.resid_mode != kResidNone && row_ok) {
+                    if (p.resid_mode == kMaskRows && !valid) {
+#pragma unroll
+                        for (int j = 0; j < kCW; ++j) v[j] = 0.0f;
+                    }
+                    if (p.resid_mode != kResidNone && p.resid_mode != kMaskRows && row_ok) {
                         const float* rp = p.resid + static_cast<int64_t>(row) * p.ldr + nc;
                         const bool keep_sub = valid || p.resid_mode == kResidAdd;
                         const bool keep_all = valid || p.resid_mode != kResidAddMaskAll;

@@ -31,7 +31,7 @@ import torch
 _lib: Optional[ctypes.CDLL] = None
 
 F32, F16 = 0, 1
-RESID_NONE, RESID_ADD, RESID_ADD_MASKSUB, RESID_ADD_MASKALL = 0, 1, 2, 3
+RESID_NONE, RESID_ADD, RESID_ADD_MASKSUB, RESID_ADD_MASKALL, MASK_ROWS = 0, 1, 2, 3, 4
 MASK_NONE, MASK_KEY, MASK_FULL = 0, 1, 2
 
 _vp, _i64, _i32, _f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float

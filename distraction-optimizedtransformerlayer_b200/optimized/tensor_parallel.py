@@ -1,0 +1,162 @@
+"""Tensor parallelism across the GPUs of one box.
+
+The reference runs on one GPU and has no parallel code
+asks for the wide-head layer "8-way head-sharded tensor parallel with one NCCL
+all-reduce over NVLink after the out-proj and after FFN2". With P ranks (one
+process per GPU, torch.distributed over NCCL), rank r holds:
+
+    attention  q/k/v rows and out_proj columns of heads [r H/P, (r+1) H/P)
+    ffn_in     rows [r F/P, (r+1) F/P)        (column-parallel, GELU local)
+    ffn_out    columns [r F/P, (r+1) F/P)     (row-parallel)
+    biases of out_proj / ffn_out on rank 0 only (added once by the sum)
+    LayerNorm parameters on every rank (the norms run replicated)
+
+Per layer, on every rank (x replicated, fp32):
+
+    n1 = LN1(x) fp16; qkv_r = n1 Wqkv_r^T + b; ctx_r = attention(local heads)
+    part = mask(ctx_r Wo_r^T + [bo]) fp32   -> all_reduce(sum) over NVLink
+    x1, n2 = x + part, LN2(x + part)
+    h_r = GELU(n2 W1_r^T + b1_r); part = mask(h_r W2_r^T + [b2]) -> all_reduce
+    x2, out = x1 + part, next LN(x1 + part)
+
+The partial sums stay fp32 through the reduction. Padded rows are zeroed in
+the partials, so they add nothing; the residual stream keeps x there, which
+differs from the reference's zeroed rows only on padded rows, which no valid
+row attends to and the final LayerNorm writes as 0.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Dict, Optional
+
+import torch
+
+RESID_NONE, MASK_ROWS = 0, 4
+
+
+@dataclass(frozen=True)
+class TPShardPlan:
+    """Which slices of each weight rank `rank` of `world` holds."""
+
+    d_model: int
+    num_heads: int
+    ffn_dim: int
+    world: int
+    rank: int
+
+    def __post_init__(self):
+        if self.num_heads % self.world or self.ffn_dim % self.world:
+            raise ValueError(f"heads ({self.num_heads}) and ffn_dim ({self.ffn_dim}) must divide "
+                             f"by the tensor-parallel size {self.world}")
+        if not 0 <= self.rank < self.world:
+            raise ValueError(f"rank {self.rank} outside [0, {self.world})")
+        if (self.d_model // self.world) % 8 or (self.ffn_dim // self.world) % 8:
+            raise ValueError("each rank's slice of d_model and ffn_dim must be a multiple of 8")
+
+    @property
+    def head_dim(self) -> int:
+        return self.d_model // self.num_heads
+
+    @property
+    def local_heads(self) -> int:
+        return self.num_heads // self.world
+
+    @property
+    def d_slice(self) -> slice:
+        w = self.d_model // self.world
+        return slice(self.rank * w, (self.rank + 1) * w)
+
+    @property
+    def f_slice(self) -> slice:
+        w = self.ffn_dim // self.world
+        return slice(self.rank * w, (self.rank + 1) * w)
+
+    def shard(self, state: Dict[str, torch.Tensor], num_layers: int) -> Dict[str, torch.Tensor]:
+        """This rank's tensors from a full BaselineTransformer state_dict."""
+        ds, fs = self.d_slice, self.f_slice
+        out: Dict[str, torch.Tensor] = {}
+        for i in range(num_layers):
+            p = f"layers.{i}."
+            a = p + "attention."
+            out[p + "wqkv"] = torch.cat([state[a + f"{n}_proj.weight"][ds] for n in "qkv"], 0)
+            out[p + "bqkv"] = torch.cat([state[a + f"{n}_proj.bias"][ds] for n in "qkv"], 0)
+            out[p + "wo"] = state[a + "out_proj.weight"][:, ds]
+            bo = state[a + "out_proj.bias"]
+            out[p + "bo"] = bo if self.rank == 0 else torch.zeros_like(bo)
+            out[p + "w1"] = state[p + "ffn_in.weight"][fs]
+            out[p + "b1"] = state[p + "ffn_in.bias"][fs]
+            out[p + "w2"] = state[p + "ffn_out.weight"][:, fs]
+            b2 = state[p + "ffn_out.bias"]
+            out[p + "b2"] = b2 if self.rank == 0 else torch.zeros_like(b2)
+            for n in ("norm1", "norm2"):
+                out[p + n + ".weight"] = state[p + n + ".weight"]
+                out[p + n + ".bias"] = state[p + n + ".bias"]
+        out["final_norm.weight"] = state["final_norm.weight"]
+        out["final_norm.bias"] = state["final_norm.bias"]
+        return out
+
+
+class TensorParallelTransformer:
+    """The layer stack split over the ranks of a process group (one per GPU).
+
+    forward(x, valid_token_mask) takes the same replicated input on every rank
+    and returns the same [B, S, d_model] fp32 output on every rank. Every rank
+    must call it with the same shapes in the same order (it runs collectives).
+    """
+
+    def __init__(self, config, state_dict: Dict[str, torch.Tensor], group=None,
+                 device: Optional[torch.device] = None, eps: float = 1e-5) -> None:
+        import torch.distributed as dist
+
+        self.dist = dist
+        self.group = group
+        self.config = config
+        self.eps = eps
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        self.plan = TPShardPlan(config.d_model, config.num_heads, config.ffn_dim, world, rank)
+        dev = device or torch.device("cuda", torch.cuda.current_device())
+        self.device = dev
+        shards = self.plan.shard(state_dict, config.num_layers)
+        self.w: Dict[str, torch.Tensor] = {}
+        for k, t in shards.items():
+            half = k.split(".")[-1] in ("wqkv", "wo", "w1", "w2")
+            self.w[k] = t.detach().to(dev, torch.float16 if half else torch.float32).contiguous()
+
+    def _kernels(self):
+        from .kernels import _custom_kernels
+
+        return _custom_kernels()
+
+    def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        k = self._kernels()
+        cfg, plan, w = self.config, self.plan, self.w
+        B, S, d = x.shape
+        x = x.float().contiguous()
+        use_mask = valid_token_mask is not None and not bool(valid_token_mask.all())
+        mask = valid_token_mask.contiguous() if use_mask else None
+        rv = mask.reshape(-1) if use_mask else None
+        mode = MASK_ROWS if use_mask else RESID_NONE
+        hd, hl = plan.head_dim, plan.local_heads
+        normed = k.layernorm_rows(x, w["layers.0.norm1.weight"], w["layers.0.norm1.bias"], self.eps,
+                                  out_half=True)
+        for i in range(cfg.num_layers):
+            p = f"layers.{i}."
+            qkv = k.linear_fp16(normed, w[p + "wqkv"], w[p + "bqkv"], out_half=True)
+            q, kk, v = qkv.view(B, S, 3, hl, hd).permute(2, 0, 3, 1, 4).unbind(0)
+            ctx = k.attention_packed(q, kk, v, cfg.causal, hd ** -0.5, key_mask=mask)
+            part = k.linear_fp16(ctx, w[p + "wo"], w[p + "bo"], row_valid=rv, resid_mode=mode)
+            self.dist.all_reduce(part, group=self.group)
+            x1, n2 = k.layernorm_rows(x, w[p + "norm2.weight"], w[p + "norm2.bias"], self.eps, sub=part,
+                                      out_half=True)
+            h = k.linear_fp16(n2, w[p + "w1"], w[p + "b1"], act=1, out_half=True)
+            part2 = k.linear_fp16(h, w[p + "w2"], w[p + "b2"], row_valid=rv, resid_mode=mode)
+            self.dist.all_reduce(part2, group=self.group)
+            last = i == cfg.num_layers - 1
+            nn_ = "final_norm." if last else f"layers.{i + 1}.norm1."
+            x, normed = k.layernorm_rows(x1, w[nn_ + "weight"], w[nn_ + "bias"], self.eps, sub=part2,
+                                         out_half=not last, row_valid=rv if last else None)
+        return normed
+
+    __call__ = forward

@@ -44,6 +44,7 @@ extern "C" {
 #define DOTL_RESID_ADD 1         /* out = resid + (a w^T + bias) */
 #define DOTL_RESID_ADD_MASKSUB 2 /* out = resid + (valid ? a w^T + bias : 0) */
 #define DOTL_RESID_ADD_MASKALL 3 /* out = valid ? resid + a w^T + bias : 0 */
+#define DOTL_MASK_ROWS 4         /* out = valid ? act(a w^T + bias) : 0 (no residual) */
 
 /* dotl_attention mask kinds */
 #define DOTL_MASK_NONE 0
