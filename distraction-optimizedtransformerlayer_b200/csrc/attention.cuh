@@ -9,26 +9,29 @@
 // (layout 1).
 //
 // Design (sm_100a): one CTA per SM, persistent over work items (stream, 128-row
-// query tile), largest causal tiles first. Ten warps:
-//   warp 0      producer: publishes each item's key-tile count (after scanning
-//               a per-key mask for its last valid key), loads the Q tile and
-//               the K/V tiles (128 keys each) into a STAGES-deep ring by TMA;
-//   warp 1      MMA issuer: S(j) = Q K(j)^T into the TMEM S region of the
-//               softmax warpgroup that owns tile j (even tiles: group 0, odd:
-//               group 1), then O_g += P(j) V(j) with P read from TMEM (the
-//               tcgen05 "TS" form), O_g accumulating in TMEM;
-//   warps 2-5   softmax group 0, warps 6-9 softmax group 1: each thread owns
-//               one query row, loads its 128 scores from TMEM in one pass,
-//               masks (only on boundary tiles), takes the row max, rescales
-//               its O row in TMEM only when the max grew by more than 2^8
-//               (the stale max is exact: numerator and denominator share it),
-//               writes P = exp2(s*c - m*c) as fp16 over its S columns, and
-//               keeps the row sum. Group 1 hands (max, sum) to group 0, which
-//               merges the two partial outputs and stores the row.
-// Splitting one query tile's keys between two groups lets their softmax
-// phases interleave on each SM sub-partition while the tensor core runs the
-// other group's MMAs, and keeps 128-row tiles (the most CTAs) for small
-// problems. The score matrix never leaves TMEM.
+// query tile), largest causal tiles first. Twelve warps:
+//   warps 0-3   softmax group 0, warps 4-7 softmax group 1: each thread owns
+//               one query row of the tile, reads its 128 scores of a key tile
+//               from TMEM, masks (only on boundary tiles), takes the row max,
+//               rescales its O row in TMEM only when the max grew by more than
+//               2^8 (the stale max is exact: numerator and denominator share
+//               it), writes P = exp2(s*c - m*c) as fp16 over the S columns it
+//               has read, and keeps the row sum. The groups take alternate key
+//               tiles of an item; group 1 hands (max, sum) to the group that
+//               merges the two partial outputs and stores the row;
+//   warp 8      producer: publishes each item's key-tile count (after scanning
+//               a per-key mask for its last valid key) and loads by TMA the Q
+//               tile (two slots, so the next item's Q lands during this one)
+//               and the K and V tiles (128 keys each) into two rings;
+//   warp 9      MMA issuer: S(t) = Q K(t)^T into S/P buffer t mod NS, then
+//               O_g += P(t) V(t) with P read from TMEM (the tcgen05 "TS" form).
+// With NS = 3 S/P buffers (head_dim <= 64: 3 x 128 S columns plus two O
+// accumulators fit TMEM's 512 columns), S(t+3) is issued right after PV(t),
+// so a group's next scores are ready while it finishes the current tile;
+// head_dim 128 has room for two buffers. Splitting one query tile's keys
+// between two groups interleaves their softmax phases on each SM
+// sub-partition while the tensor core runs the other group's MMAs. The score
+// matrix never leaves TMEM.
 //
 // "Packed" mode runs the tiles over the flat token axis (b * S + s), so short
 // sequences share one 128-row tile; a row's keys are confined to its own
@@ -41,7 +44,7 @@
 
 namespace dotl {
 
-constexpr int kAttnThreads = 384;   // softmax warpgroups 0-1, producer/MMA warpgroup 2
+constexpr int kAttnThreads = 384;        // softmax warpgroups 0-1, producer/MMA warpgroup 2
 constexpr int kAttnTile = 128;          // query rows per tile and keys per key tile
 constexpr float kRescaleLog2 = 8.0f;    // lazy-rescale threshold, in log2 units
 
@@ -73,30 +76,37 @@ __device__ __forceinline__ void attn_tma(uint32_t dst, const CUtensorMap* map, u
 
 template <int HD, int STAGES>
 struct AttnSmem {
+    static constexpr int kNS = 3 * kAttnTile + 2 * HD <= 512 ? 3 : 2;   // S/P buffers in TMEM
     static constexpr int kBlkCols = HD < 64 ? HD : 64;          // fp16 columns per TMA box
     static constexpr int kRowBytes = kBlkCols * 2;              // 128 or 64
     static constexpr int kNumBlk = HD / kBlkCols;
     static constexpr uint32_t kBlkBytes = kAttnTile * kRowBytes;
     static constexpr uint32_t kTileBytes = kNumBlk * kBlkBytes; // one Q/K/V tile
     static constexpr uint32_t kSwz = kRowBytes == 128 ? kSwizzle128 : kSwizzle64;
-    static constexpr uint32_t kOffQ = 0;
-    static constexpr uint32_t kOffK = kOffQ + kTileBytes;
+    static constexpr uint32_t kOffQ = 0;                                  // 2 slots
+    static constexpr uint32_t kOffK = kOffQ + 2 * kTileBytes;
     static constexpr uint32_t kOffV = kOffK + STAGES * kTileBytes;
     static constexpr uint32_t kOffComb = kOffV + STAGES * kTileBytes;   // 128 x (max, sum) of group 1
     static constexpr uint32_t kOffInfo = kOffComb + kAttnTile * 8;      // 2 item slots
     static constexpr uint32_t kOffBar = kOffInfo + 16;   // 2 slots x {n_kt, hole}
-    // q_full, q_empty, k_full[ST], v_full[ST], kv_empty[ST], s_full[2],
-    // p_full[2], o_done[2], o_free[2], comb_full, comb_empty, info_full[2],
-    // info_empty[2], drain
-    static constexpr uint32_t kNumBars = 2 + 3 * STAGES + 8 + 2 + 4 + 1;
+    // mbarrier indices
+    static constexpr int kBarQFull = 0, kBarQEmpty = 2;                  // [2] each
+    static constexpr int kBarKFull = 4, kBarKEmpty = kBarKFull + STAGES; // [STAGES] each
+    static constexpr int kBarVFull = kBarKEmpty + STAGES, kBarVEmpty = kBarVFull + STAGES;
+    static constexpr int kBarSFull = kBarVEmpty + STAGES, kBarPFull = kBarSFull + kNS;   // [NS] each
+    static constexpr int kBarODone = kBarPFull + kNS, kBarOFree = kBarODone + 2;         // [2] each
+    static constexpr int kBarCombFull = kBarOFree + 2, kBarCombEmpty = kBarCombFull + 1;
+    static constexpr int kBarInfoFull = kBarCombEmpty + 1, kBarInfoEmpty = kBarInfoFull + 2;
+    static constexpr int kBarDrain = kBarInfoEmpty + 2;
+    static constexpr uint32_t kNumBars = kBarDrain + 1;
     static constexpr uint32_t kOffSlot = kOffBar + kNumBars * 8;
     static constexpr uint32_t kOffAbort = kOffSlot + 4;
     static constexpr uint32_t kBytes = kOffAbort + 4;
     static constexpr uint32_t kAlloc = kBytes + 1024;
     static constexpr uint32_t kTmemCols = 512;
-    // TMEM columns: S/P of group g at 128 g, O of group g at 256 + HD g.
+    // TMEM columns: S/P buffer i at 128 i, O of group g at 128 NS + HD g.
     static constexpr uint32_t kColS = 0;
-    static constexpr uint32_t kColO = 256;
+    static constexpr uint32_t kColO = kNS * kAttnTile;
 };
 
 // Item -> (stream, query tile), query-tile index descending in the slowest
@@ -161,19 +171,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                                                ~static_cast<uintptr_t>(1023));
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bar0 = sbase + L::kOffBar;
-    const uint32_t q_full = bar0, q_empty = bar0 + 8;
-    auto k_full = [&](int s) { return bar0 + 8u * (2 + s); };
-    auto v_full = [&](int s) { return bar0 + 8u * (2 + STAGES + s); };
-    auto kv_empty = [&](int s) { return bar0 + 8u * (2 + 2 * STAGES + s); };
-    auto s_full = [&](int g) { return bar0 + 8u * (2 + 3 * STAGES + g); };
-    auto p_full = [&](int g) { return bar0 + 8u * (4 + 3 * STAGES + g); };
-    auto o_done = [&](int g) { return bar0 + 8u * (6 + 3 * STAGES + g); };
-    auto o_free = [&](int g) { return bar0 + 8u * (8 + 3 * STAGES + g); };
-    const uint32_t comb_full = bar0 + 8u * (10 + 3 * STAGES);
-    const uint32_t comb_empty = bar0 + 8u * (11 + 3 * STAGES);
-    auto info_full = [&](int s) { return bar0 + 8u * (12 + 3 * STAGES + s); };
-    auto info_empty = [&](int s) { return bar0 + 8u * (14 + 3 * STAGES + s); };
-    const uint32_t drain_bar = bar0 + 8u * (16 + 3 * STAGES);
+    auto bar = [&](int i) { return bar0 + 8u * static_cast<uint32_t>(i); };
+    auto q_full = [&](int i) { return bar(L::kBarQFull + i); };
+    auto q_empty = [&](int i) { return bar(L::kBarQEmpty + i); };
+    auto k_full = [&](int s) { return bar(L::kBarKFull + s); };
+    auto k_empty = [&](int s) { return bar(L::kBarKEmpty + s); };
+    auto v_full = [&](int s) { return bar(L::kBarVFull + s); };
+    auto v_empty = [&](int s) { return bar(L::kBarVEmpty + s); };
+    auto s_full = [&](int i) { return bar(L::kBarSFull + i); };
+    auto p_full = [&](int i) { return bar(L::kBarPFull + i); };
+    auto o_done = [&](int g) { return bar(L::kBarODone + g); };
+    auto o_free = [&](int g) { return bar(L::kBarOFree + g); };
+    const uint32_t comb_full = bar(L::kBarCombFull);
+    const uint32_t comb_empty = bar(L::kBarCombEmpty);
+    auto info_full = [&](int s) { return bar(L::kBarInfoFull + s); };
+    auto info_empty = [&](int s) { return bar(L::kBarInfoEmpty + s); };
+    const uint32_t drain_bar = bar(L::kBarDrain);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffAbort);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffSlot);
     volatile int* info = reinterpret_cast<volatile int*>(smem + L::kOffInfo);   // {n_kt, hole} x 2
@@ -183,16 +196,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        mbar_init(q_full, 1);
-        mbar_init(q_empty, 1);
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(k_full(s), 1);
+            mbar_init(k_empty(s), 1);
             mbar_init(v_full(s), 1);
-            mbar_init(kv_empty(s), 1);
+            mbar_init(v_empty(s), 1);
+        }
+        for (int i = 0; i < L::kNS; ++i) {
+            mbar_init(s_full(i), 1);
+            mbar_init(p_full(i), 128);
         }
         for (int g = 0; g < 2; ++g) {
-            mbar_init(s_full(g), 1);
-            mbar_init(p_full(g), 128);
+            mbar_init(q_full(g), 1);
+            mbar_init(q_empty(g), 1);
             mbar_init(o_done(g), 1);
             mbar_init(o_free(g), 128);
             mbar_init(info_full(g), 1);
@@ -232,10 +248,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         regs_dec<104>();
         if (warp == 8) {
             // --------------------------------------------------- producer --
-            uint32_t tcount = 0, qcount = 0, icount = 0;
-            int k_issued_phase[STAGES];
-            for (int s = 0; s < STAGES; ++s) k_issued_phase[s] = -1;
-            int q_issued = -1;
+            // Loads follow the MMA issuer's order: K(0..NS-1), then V(j) and
+            // K(j+NS) for each j, so each ring runs independently.
+            uint32_t kcount = 0, vcount = 0, qcount = 0, icount = 0;
+            int k_issued_phase[STAGES], v_issued_phase[STAGES], q_issued_phase[2] = {-1, -1};
+            for (int s = 0; s < STAGES; ++s) k_issued_phase[s] = v_issued_phase[s] = -1;
             for (int item = blockIdx.x; item < num_items; item += gridDim.x, ++icount) {
                 int stream, qt, k_lo, k_hi;
                 attn_item(p, item, stream, qt);
@@ -259,33 +276,48 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                         mbar_arrive(info_full(slot));
                     }
                     if (ok && n_kt > 0) {
-                        ok = mbar_wait(q_empty, (qcount & 1u) ^ 1u, abort_flag);
+                        const int qs = static_cast<int>(qcount & 1u);
+                        const uint32_t qph = (qcount >> 1) & 1u;
+                        ok = mbar_wait(q_empty(qs), qph ^ 1u, abort_flag);
                         if (ok) {
-                            mbar_arrive_expect_tx(q_full, L::kTileBytes);
+                            mbar_arrive_expect_tx(q_full(qs), L::kTileBytes);
 #pragma unroll
                             for (int cb = 0; cb < L::kNumBlk; ++cb)
-                                attn_tma(sbase + L::kOffQ + cb * L::kBlkBytes, &tmap_q, q_full,
-                                         cb * L::kBlkCols, qt * kAttnTile, h, bq, p.head_inner & 1);
-                            q_issued = static_cast<int>(qcount & 1u);
+                                attn_tma(sbase + L::kOffQ + qs * L::kTileBytes + cb * L::kBlkBytes, &tmap_q,
+                                         q_full(qs), cb * L::kBlkCols, qt * kAttnTile, h, bq, p.head_inner & 1);
+                            q_issued_phase[qs] = static_cast<int>(qph);
                         }
                     }
-                    for (int j = 0; ok && j < n_kt; ++j, ++tcount) {
-                        const int st = static_cast<int>(tcount % STAGES);
-                        const uint32_t ph = (tcount / STAGES) & 1u;
-                        const int kc0 = k_lo + j * kAttnTile;
-                        ok = mbar_wait(kv_empty(st), ph ^ 1u, abort_flag);
-                        if (!ok) break;
+                    auto load_k = [&](int j) -> bool {
+                        const int st = static_cast<int>(kcount % STAGES);
+                        const uint32_t ph = (kcount / STAGES) & 1u;
+                        if (!mbar_wait(k_empty(st), ph ^ 1u, abort_flag)) return false;
                         mbar_arrive_expect_tx(k_full(st), L::kTileBytes);
 #pragma unroll
                         for (int cb = 0; cb < L::kNumBlk; ++cb)
                             attn_tma(sbase + L::kOffK + st * L::kTileBytes + cb * L::kBlkBytes, &tmap_k,
-                                     k_full(st), cb * L::kBlkCols, kc0, h, bq, p.head_inner & 2);
+                                     k_full(st), cb * L::kBlkCols, k_lo + j * kAttnTile, h, bq, p.head_inner & 2);
+                        k_issued_phase[st] = static_cast<int>(ph);
+                        ++kcount;
+                        return true;
+                    };
+                    auto load_v = [&](int j) -> bool {
+                        const int st = static_cast<int>(vcount % STAGES);
+                        const uint32_t ph = (vcount / STAGES) & 1u;
+                        if (!mbar_wait(v_empty(st), ph ^ 1u, abort_flag)) return false;
                         mbar_arrive_expect_tx(v_full(st), L::kTileBytes);
 #pragma unroll
                         for (int cb = 0; cb < L::kNumBlk; ++cb)
                             attn_tma(sbase + L::kOffV + st * L::kTileBytes + cb * L::kBlkBytes, &tmap_v,
-                                     v_full(st), cb * L::kBlkCols, kc0, h, bq, p.head_inner & 4);
-                        k_issued_phase[st] = static_cast<int>(ph);
+                                     v_full(st), cb * L::kBlkCols, k_lo + j * kAttnTile, h, bq, p.head_inner & 4);
+                        v_issued_phase[st] = static_cast<int>(ph);
+                        ++vcount;
+                        return true;
+                    };
+                    for (int j = 0; ok && j < min(n_kt, L::kNS); ++j) ok = load_k(j);
+                    for (int j = 0; ok && j < n_kt; ++j) {
+                        ok = load_v(j);
+                        if (ok && j + L::kNS < n_kt) ok = load_k(j + L::kNS);
                     }
                 }
                 if (n_kt > 0) ++qcount;
@@ -293,12 +325,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 if (!ok) break;
             }
             if (lane == 0 && *abort_flag) {
-                if (q_issued >= 0) mbar_wait_drain(q_full, static_cast<uint32_t>(q_issued));
+                // no TMA write may still be in flight when the CTA exits
+                for (int i = 0; i < 2; ++i)
+                    if (q_issued_phase[i] >= 0) mbar_wait_drain(q_full(i), static_cast<uint32_t>(q_issued_phase[i]));
                 for (int s = 0; s < STAGES; ++s) {
-                    if (k_issued_phase[s] >= 0) {
-                        mbar_wait_drain(k_full(s), static_cast<uint32_t>(k_issued_phase[s]));
-                        mbar_wait_drain(v_full(s), static_cast<uint32_t>(k_issued_phase[s]));
-                    }
+                    if (k_issued_phase[s] >= 0) mbar_wait_drain(k_full(s), static_cast<uint32_t>(k_issued_phase[s]));
+                    if (v_issued_phase[s] >= 0) mbar_wait_drain(v_full(s), static_cast<uint32_t>(v_issued_phase[s]));
                 }
             }
         } else if (warp == 9 && lane == 0) {
@@ -307,7 +339,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             constexpr uint32_t idesc_o = idesc_f16_f32(kAttnTile, HD, false, true);
             constexpr int kStepsPerBlk = L::kBlkCols / 16;
             uint32_t tcount = 0, qcount = 0, icount = 0, singles = 0;
-            uint32_t gcount[2] = {0, 0}, pcount[2] = {0, 0};
+            uint32_t pcount[2] = {0, 0};
             for (int item = blockIdx.x; item < num_items; item += gridDim.x, ++icount) {
                 const int slot = static_cast<int>(icount & 1u);
                 if (!mbar_wait(info_full(slot), (icount >> 1) & 1u, abort_flag)) break;
@@ -315,17 +347,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 mbar_arrive(info_empty(slot));
                 if (n_kt == 0) continue;
                 const int g0 = first_group(n_kt, singles);
-                if (!mbar_wait(q_full, qcount & 1u, abort_flag)) break;
+                const int qs = static_cast<int>(qcount & 1u);
+                if (!mbar_wait(q_full(qs), (qcount >> 1) & 1u, abort_flag)) break;
                 tc_fence_after();
-                // S(j) = Q K(j)^T into the S region of tile j's group.
+                // S(t) = Q K(t)^T into S/P buffer t mod NS (t counts this CTA's
+                // key tiles). The buffer's previous P was read by a PV issued
+                // earlier from this thread, and tcgen05 MMAs run in issue order.
                 auto issue_s = [&](int j) -> bool {
                     const uint32_t t = tcount + j;
                     const int st = static_cast<int>(t % STAGES);
-                    const int g = (g0 + j) & 1;
+                    const int sb = static_cast<int>(t % L::kNS);
                     if (!mbar_wait(k_full(st), (t / STAGES) & 1u, abort_flag)) return false;
                     tc_fence_after();
-                    const uint32_t d = tmem_base + L::kColS + static_cast<uint32_t>(g * kAttnTile);
-                    const uint32_t qa = sbase + L::kOffQ;
+                    const uint32_t d = tmem_base + L::kColS + static_cast<uint32_t>(sb * kAttnTile);
+                    const uint32_t qa = sbase + L::kOffQ + qs * L::kTileBytes;
                     const uint32_t ka = sbase + L::kOffK + st * L::kTileBytes;
 #pragma unroll
                     for (int kk = 0; kk < HD / 16; ++kk) {
@@ -334,23 +369,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                                    smem_desc(ka + off, 16, 8 * L::kRowBytes, L::kSwz), idesc_s,
                                    kk != 0 ? 1u : 0u);
                     }
-                    tc_commit(s_full(g));
-                    if (j == n_kt - 1) tc_commit(q_empty);   // Q is no longer read
+                    tc_commit(s_full(sb));
+                    tc_commit(k_empty(st));
+                    if (j == n_kt - 1) tc_commit(q_empty(qs));   // this Q slot is no longer read
                     return true;
                 };
-                bool ok = issue_s(0);
-                if (ok && n_kt > 1) ok = issue_s(1);
+                bool ok = true;
+                for (int j = 0; ok && j < min(n_kt, L::kNS); ++j) ok = issue_s(j);
                 for (int j = 0; ok && j < n_kt; ++j) {
                     const int g = (g0 + j) & 1;
                     const uint32_t t = tcount + j;
                     const int st = static_cast<int>(t % STAGES);
+                    const int sb = static_cast<int>(t % L::kNS);
                     // the group's previous item has read its O accumulator
                     if (j < 2 && !mbar_wait(o_free(g), (pcount[g] & 1u) ^ 1u, abort_flag)) { ok = false; break; }
-                    if (!mbar_wait(p_full(g), gcount[g] & 1u, abort_flag)) { ok = false; break; }
+                    if (!mbar_wait(p_full(sb), (t / L::kNS) & 1u, abort_flag)) { ok = false; break; }
                     if (!mbar_wait(v_full(st), (t / STAGES) & 1u, abort_flag)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t d = tmem_base + L::kColO + static_cast<uint32_t>(g * HD);
-                    const uint32_t pa = tmem_base + L::kColS + static_cast<uint32_t>(g * kAttnTile);
+                    const uint32_t pa = tmem_base + L::kColS + static_cast<uint32_t>(sb * kAttnTile);
                     const uint32_t va = sbase + L::kOffV + st * L::kTileBytes;
 #pragma unroll
                     for (int kk = 0; kk < kAttnTile / 16; ++kk)
@@ -358,9 +395,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                                    smem_desc(va + kk * 16 * L::kRowBytes, L::kBlkBytes, 8 * L::kRowBytes, L::kSwz),
                                    idesc_o, (j >= 2 || kk != 0) ? 1u : 0u);
                     tc_commit(o_done(g));
-                    tc_commit(kv_empty(st));
-                    ++gcount[g];
-                    if (j + 2 < n_kt && !issue_s(j + 2)) { ok = false; break; }
+                    tc_commit(v_empty(st));
+                    if (j + L::kNS < n_kt && !issue_s(j + L::kNS)) { ok = false; break; }
                 }
                 if (!ok) break;
                 ++pcount[g0];
@@ -378,11 +414,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;            // query row within the tile
         const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-        const uint32_t t_s = tmem_base + lane_off + L::kColS + static_cast<uint32_t>(grp * kAttnTile);
+        const uint32_t t_s0 = tmem_base + lane_off + L::kColS;
         const uint32_t t_o0 = tmem_base + lane_off + L::kColO;
         const uint32_t t_o = t_o0 + static_cast<uint32_t>(grp * HD);
         const float c = p.scale_log2;
-        uint32_t gtiles = 0, icount = 0, ccount = 0, singles = 0;
+        uint32_t gtiles = 0, icount = 0, ccount = 0, singles = 0, tbase = 0;
         bool alive = true;
         for (int item = blockIdx.x; item < num_items && alive; item += gridDim.x, ++icount) {
             const int slot = static_cast<int>(icount & 1u);
@@ -393,6 +429,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(info_empty(slot));
             const int g0 = n_kt > 0 ? first_group(n_kt, singles) : 0;
+            const uint32_t t_item = tbase;      // this CTA's index of the item's first key tile
+            tbase += static_cast<uint32_t>(n_kt);
 
             int stream, qt, k_lo, k_hi;
             attn_item(p, item, stream, qt);
@@ -416,6 +454,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 klo_r = 1;
                 khi_r = 0;
             }
+            // keys [kin_lo, kin_hi] are in range for every row of this warp
+            const int kin_lo = __reduce_max_sync(0xffffffffu, klo_r);
+            const int kin_hi = __reduce_min_sync(0xffffffffu, khi_r);
             auto out_row = [&]() -> __half* {
                 const int64_t off = (p.out_layout == 1) ? ((static_cast<int64_t>(b) * p.S + s) * p.H + h) * HD
                                                         : ((static_cast<int64_t>(b) * p.H + h) * p.S + s) * HD;
@@ -433,75 +474,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             if (!two && grp != g0) continue;           // the other group owns this single-tile item
 
             float m_used = -INFINITY, l_run = 0.0f;
-            for (int j = (grp - g0) & 1; j < n_kt; j += 2, ++gtiles) {
-                const int kc0 = k_lo + j * kAttnTile;
-                // Allowed keys of this row in this tile as a 128-bit mask:
-                // bit i of allow[w] <-> key column 32 w + i.
-                uint32_t allow[4];
-#pragma unroll
-                for (int w = 0; w < 4; ++w) {
-                    const int lo = max(klo_r - kc0 - 32 * w, 0);
-                    const int hi = min(khi_r - kc0 - 32 * w, 31);
-                    uint32_t bits = 0u;
-                    if (lo <= hi) bits = (hi == 31 ? 0xffffffffu : ((1u << (hi + 1)) - 1u)) & ~((1u << lo) - 1u);
-                    allow[w] = bits;
-                }
-                if (p.mask_kind == 1 && kc0 + kAttnTile > hole) {
-#pragma unroll
-                    for (int w = 0; w < 4; ++w) {
-                        const int kc = kc0 + 32 * w + lane;
-                        bool allowed = false;
-                        if (kc < p.rows_total) {
-                            int bk, sk;
-                            if (p.packed) {
-                                bk = kc / p.S;
-                                sk = kc - bk * p.S;
-                            } else {
-                                bk = stream / p.H;
-                                sk = kc;
-                            }
-                            allowed = p.mask[bk * p.ms0 + static_cast<int64_t>(sk) * p.ms3] != 0;
-                        }
-                        allow[w] &= __ballot_sync(0xffffffffu, allowed);
-                    }
-                } else if (p.mask_kind == 2 && q_ok) {
-                    const uint8_t* mrow = p.mask + b * p.ms0 + h * p.ms1 + static_cast<int64_t>(s) * p.ms2;
-#pragma unroll 1
-                    for (int i = 0; i < kAttnTile; ++i) {
-                        const int kc = kc0 + i;
-                        if (((allow[i >> 5] >> (i & 31)) & 1u) && mrow[static_cast<int64_t>(kc - klo_r) * p.ms3] == 0)
-                            allow[i >> 5] &= ~(1u << (i & 31));
-                    }
-                }
-                const bool interior = (allow[0] & allow[1] & allow[2] & allow[3]) == 0xffffffffu;
-
-                ok = mbar_wait(s_full(grp), gtiles & 1u, abort_flag);
-                if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
-                tc_fence_after();
-                // pass 1: row max, 32 columns at a time, eight independent chains
-                float mx8[8];
-#pragma unroll
-                for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
-#pragma unroll 1
-                for (int q4 = 0; q4 < 4; ++q4) {
-                    uint32_t sr[32];
-                    tmem_ld_32x32b_x32(t_s + q4 * 32, sr);
-                    tmem_ld_wait(sr);
-                    if (interior) {
-#pragma unroll
-                        for (int i = 0; i < 32; i += 2)
-                            mx8[(i >> 1) & 7] = fmax3(mx8[(i >> 1) & 7], __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
-                    } else {
-                        const uint32_t wq = q4 == 0 ? allow[0] : q4 == 1 ? allow[1] : q4 == 2 ? allow[2] : allow[3];
-#pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            mx8[i & 7] = fmaxf(mx8[i & 7], ((wq >> i) & 1u) ? __uint_as_float(sr[i]) : -INFINITY);
-                    }
-                }
-                const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+            // Folds this tile's row max into the running (lazily rescaled) max:
+            // rescales O in TMEM only when the max grew by more than
+            // 2^kRescaleLog2. Returns m_used * c, the exp2 offset for this tile.
+            auto softmax_rescale = [&](float mx) -> float {
                 const float m_new = fmaxf(m_used, mx);
-                // lazy rescale: only when the max grew by more than 2^kRescaleLog2
                 float alpha = 1.0f;
                 bool rescale = false;
                 if (m_used == -INFINITY) {
@@ -512,8 +489,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 }
                 if (__any_sync(0xffffffffu, rescale)) {
                     // O holds the previous tiles of this group: wait for the last PV
-                    ok = mbar_wait(o_done(grp), (gtiles - 1) & 1u, abort_flag);
-                    if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
+                    const bool ok2 = mbar_wait(o_done(grp), (gtiles - 1) & 1u, abort_flag);
+                    if (!__all_sync(0xffffffffu, ok2)) {
+                        alive = false;
+                        return 0.0f;
+                    }
                     tc_fence_after();
 #pragma unroll 1
                     for (int cc = 0; cc < HD; cc += 32) {
@@ -530,25 +510,130 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                         m_used = m_new;
                     }
                 }
-                const float mc = (m_used == -INFINITY) ? 0.0f : m_used * c;
-                // pass 2: P = exp2(s c - m c) as fp16, 32 keys at a time, written
-                // over S columns already read (keys 32 q.. go to columns 16 q..);
-                // the row sum stays fp32.
-                float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-                for (int q4 = 0; q4 < 4; ++q4) {
-                    uint32_t sr[32], pk[16];
-                    tmem_ld_32x32b_x32(t_s + q4 * 32, sr);
-                    tmem_ld_wait(sr);
-                    if (interior) {
+                return (m_used == -INFINITY) ? 0.0f : m_used * c;
+            };
+            for (int j = (grp - g0) & 1; j < n_kt; j += 2, ++gtiles) {
+                const int kc0 = k_lo + j * kAttnTile;
+                // Interior tile: every key allowed for every row of the warp
+                // (warp-uniform, so the branches below may hold .sync.aligned
+                // TMEM loads). Other tiles build per-row allow masks.
+                const bool interior = p.mask_kind != 2 && kc0 >= kin_lo && kc0 + (kAttnTile - 1) <= kin_hi &&
+                                      (p.mask_kind == 0 || kc0 + kAttnTile <= hole);
+                uint32_t allow[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
+                if (!interior) {
+                    // Allowed keys of this row in this tile as a 128-bit mask:
+                    // bit i of allow[w] <-> key column 32 w + i.
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            const float p0 = fast_exp2(fmaf(__uint_as_float(sr[2 * i]), c, -mc));
-                            const float p1 = fast_exp2(fmaf(__uint_as_float(sr[2 * i + 1]), c, -mc));
-                            sum8[i & 7] += p0 + p1;
-                            pk[i] = pack_half2(p0, p1);
+                    for (int w = 0; w < 4; ++w) {
+                        const int lo = max(klo_r - kc0 - 32 * w, 0);
+                        const int hi = min(khi_r - kc0 - 32 * w, 31);
+                        uint32_t bits = 0u;
+                        if (lo <= hi) bits = (hi == 31 ? 0xffffffffu : ((1u << (hi + 1)) - 1u)) & ~((1u << lo) - 1u);
+                        allow[w] = bits;
+                    }
+                    if (p.mask_kind == 1 && kc0 + kAttnTile > hole) {
+#pragma unroll
+                        for (int w = 0; w < 4; ++w) {
+                            const int kc = kc0 + 32 * w + lane;
+                            bool allowed = false;
+                            if (kc < p.rows_total) {
+                                int bk, sk;
+                                if (p.packed) {
+                                    bk = kc / p.S;
+                                    sk = kc - bk * p.S;
+                                } else {
+                                    bk = stream / p.H;
+                                    sk = kc;
+                                }
+                                allowed = p.mask[bk * p.ms0 + static_cast<int64_t>(sk) * p.ms3] != 0;
+                            }
+                            allow[w] &= __ballot_sync(0xffffffffu, allowed);
                         }
-                    } else {
+                    } else if (p.mask_kind == 2 && q_ok) {
+                        const uint8_t* mrow = p.mask + b * p.ms0 + h * p.ms1 + static_cast<int64_t>(s) * p.ms2;
+#pragma unroll 1
+                        for (int i = 0; i < kAttnTile; ++i) {
+                            const int kc = kc0 + i;
+                            if (((allow[i >> 5] >> (i & 31)) & 1u) && mrow[static_cast<int64_t>(kc - klo_r) * p.ms3] == 0)
+                                allow[i >> 5] &= ~(1u << (i & 31));
+                        }
+                    }
+                }
+                const uint32_t t = t_item + static_cast<uint32_t>(j);
+                const int sb = static_cast<int>(t % L::kNS);
+                const uint32_t t_s = t_s0 + static_cast<uint32_t>(sb * kAttnTile);
+                ok = mbar_wait(s_full(sb), (t / L::kNS) & 1u, abort_flag);
+                if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
+                tc_fence_after();
+                float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                if (interior) {
+                    // Every key allowed: 64 scores per TMEM read (two reads per
+                    // pass instead of four).
+                    float mx8[8];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
+#pragma unroll 1
+                    for (int h = 0; h < 2; ++h) {
+                        uint32_t sr[2][32];
+                        tmem_ld_32x32b_x32(t_s + h * 64, sr[0]);
+                        tmem_ld_32x32b_x32(t_s + h * 64 + 32, sr[1]);
+                        tmem_ld_wait(sr[0]);
+                        tmem_ld_wait(sr[1]);
+#pragma unroll
+                        for (int u = 0; u < 2; ++u)
+#pragma unroll
+                            for (int i = 0; i < 32; i += 2)
+                                mx8[(i >> 1) & 7] = fmax3(mx8[(i >> 1) & 7], __uint_as_float(sr[u][i]),
+                                                          __uint_as_float(sr[u][i + 1]));
+                    }
+                    const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                           fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+                    const float mc = softmax_rescale(mx);
+                    if (!alive) break;
+#pragma unroll 1
+                    for (int h = 0; h < 2; ++h) {
+                        uint32_t sr[2][32];
+                        tmem_ld_32x32b_x32(t_s + h * 64, sr[0]);
+                        tmem_ld_32x32b_x32(t_s + h * 64 + 32, sr[1]);
+                        tmem_ld_wait(sr[0]);
+                        tmem_ld_wait(sr[1]);
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            uint32_t pk[16];
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                const float p0 = fast_exp2(fmaf(__uint_as_float(sr[u][2 * i]), c, -mc));
+                                const float p1 = fast_exp2(fmaf(__uint_as_float(sr[u][2 * i + 1]), c, -mc));
+                                sum8[i & 7] += p0 + p1;
+                                pk[i] = pack_half2(p0, p1);
+                            }
+                            tmem_st_32x32b_x16(t_s + h * 32 + u * 16, pk);
+                        }
+                    }
+                } else {
+                    // Some keys masked: two passes of 32 columns (compact code).
+                    float mx8[8];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
+#pragma unroll 1
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        uint32_t sr[32];
+                        tmem_ld_32x32b_x32(t_s + q4 * 32, sr);
+                        tmem_ld_wait(sr);
+                        const uint32_t wq = q4 == 0 ? allow[0] : q4 == 1 ? allow[1] : q4 == 2 ? allow[2] : allow[3];
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            mx8[i & 7] = fmaxf(mx8[i & 7], ((wq >> i) & 1u) ? __uint_as_float(sr[i]) : -INFINITY);
+                    }
+                    const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                           fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+                    const float mc = softmax_rescale(mx);
+                    if (!alive) break;
+#pragma unroll 1
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        uint32_t sr[32], pk[16];
+                        tmem_ld_32x32b_x32(t_s + q4 * 32, sr);
+                        tmem_ld_wait(sr);
                         const uint32_t wq = q4 == 0 ? allow[0] : q4 == 1 ? allow[1] : q4 == 2 ? allow[2] : allow[3];
 #pragma unroll
                         for (int i = 0; i < 16; ++i) {
@@ -559,13 +644,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                             sum8[i & 7] += p0 + p1;
                             pk[i] = pack_half2(p0, p1);
                         }
+                        tmem_st_32x32b_x16(t_s + q4 * 16, pk);
                     }
-                    tmem_st_32x32b_x16(t_s + q4 * 16, pk);
                 }
                 l_run += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
                 tmem_st_wait();
                 tc_fence_before();
-                mbar_arrive(p_full(grp));
+                mbar_arrive(p_full(sb));
             }
             if (!alive) break;
             // the last PV of this group has landed in O
