@@ -151,21 +151,17 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap&
 // of the MMA time (128 x BN x 64 at 8192 FLOP/clk) and the time to stream the
 // A and W stage from L2 (about 120 bytes/clk per SM).
 int pick_tile_n(int64_t M, int64_t N, int64_t K, int sms) {
+    // The widest tile that still gives most SMs a tile: wide tiles read each
+    // operand byte into fewer CTAs (A is read once per N tile, W once per M
+    // tile), narrow ones only pay off when wide ones would leave SMs idle.
+    // Measured on B200 over the five BASELINE configs' GEMMs.
+    (void)K;
     const int64_t mt = (M + dotl::kGemmBM - 1) / dotl::kGemmBM;
-    const int64_t nkb = (K + dotl::kGemmBK - 1) / dotl::kGemmBK;
-    int best = 128;
-    double best_cost = 1e300;
-    for (int bn : {256, 128, 64}) {
+    for (int bn : {256, 128}) {
         const int64_t tiles = mt * ((N + bn - 1) / bn);
-        const int64_t waves = (tiles + sms - 1) / sms;
-        const double step = std::max(2.0 * bn, (16384.0 + 128.0 * bn) / 120.0);
-        const double cost = static_cast<double>(waves) * (3000.0 + static_cast<double>(nkb) * step);
-        if (cost < best_cost * 0.97) {
-            best_cost = cost;
-            best = bn;
-        }
+        if (tiles * 5 >= static_cast<int64_t>(sms) * 3) return bn;
     }
-    return best;
+    return 64;
 }
 
 // ------------------------------------------------------------- attention --

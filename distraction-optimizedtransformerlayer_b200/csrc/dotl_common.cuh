@@ -336,30 +336,31 @@ __device__ __forceinline__ float gelu_erf(float v) {
     return 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
 }
 
-// erf(x) for x >= 0 by Abramowitz & Stegun, Handbook of Mathematical
-// Functions, formula 7.1.28 (Hastings): erf(x) = 1 - (1 + a1 x + ... + a6 x^6)^-16,
-// absolute error <= 3e-7. Horner, four squarings and one fast reciprocal: no
-// exponential, no branches.
-__device__ __forceinline__ float erf_as7128(float x) {
-    float t = fmaf(x, 0.0000430638f, 0.0002765672f);
-    t = fmaf(t, x, 0.0001520143f);
-    t = fmaf(t, x, 0.0092705272f);
-    t = fmaf(t, x, 0.0422820123f);
-    t = fmaf(t, x, 0.0705230784f);
-    t = fmaf(t, x, 1.0f);
-    t = t * t;
-    t = t * t;
-    t = t * t;
-    t = t * t;
-    return 1.0f - __fdividef(1.0f, t);
-}
-
-// GELU(v) = v * Phi(v) = 0.5 v (1 + erf(v / sqrt 2)) with erf from A&S 7.1.28;
-// agrees with gelu_erf to ~3e-7 * |v| (tests/test_gpu_20_linear.py checks it
-// against erff on the device).
+// GELU(v) = 0.5 v (1 + erf(v / sqrt 2)) with erf from Abramowitz & Stegun,
+// Handbook of Mathematical Functions, formula 7.1.28 (Hastings):
+// erf(x) = 1 - R(x), R(x) = (1 + a1 x + ... + a6 x^6)^-16, |error| <= 3e-7.
+// With u = |v| and Q = R(u / sqrt 2) / 2, both sign cases collapse to
+//   GELU(v) = max(v, 0) - u Q
+// (v >= 0: v - v R/2; v < 0: v R/2). Q comes from one polynomial whose
+// coefficients absorb the 1/sqrt 2 argument scale (a_i 2^(-i/2)) and the 1/2
+// (a factor 2^(1/16) on every coefficient, since Q = (2^(1/16) P)^-16): six
+// FMAs, four squarings, one fast reciprocal, one max and one FMA. Agrees with
+// the float64 erf GELU to 7.1e-7 absolute over [-12, 12] (the GPU test checks
+// 1e-6 (1 + |v|)). For large u, P^16 overflows to +inf and Q to 0, giving
+// max(v, 0).
 __device__ __forceinline__ float gelu_fast(float v) {
-    const float e = erf_as7128(fabsf(v) * 0.70710678118654752440f);
-    return 0.5f * v * (1.0f + copysignf(e, v));
+    const float u = fabsf(v);
+    float t = fmaf(u, 5.6212997e-06f, 5.1055209e-05f);
+    t = fmaf(t, u, 3.9686137e-05f);
+    t = fmaf(t, u, 3.4227392e-03f);
+    t = fmaf(t, u, 2.2076998e-02f);
+    t = fmaf(t, u, 5.2075163e-02f);
+    t = fmaf(t, u, 1.0442738f);
+    t = t * t;
+    t = t * t;
+    t = t * t;
+    t = t * t;
+    return fmaf(-u, __fdividef(1.0f, t), fmaxf(v, 0.0f));
 }
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {

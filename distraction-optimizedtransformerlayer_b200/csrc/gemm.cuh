@@ -59,6 +59,7 @@ struct GemmSmem {
     static constexpr uint32_t kOffA = 0;
     static constexpr uint32_t kOffB = STAGES * kGemmATileBytes;
     // per epilogue warp: one 32-row x 128-byte staging buffer for TMA stores
+    // (an fp32 chunk, or two fp16 chunks of 64-byte rows used alternately)
     static constexpr uint32_t kOffStage = kOffB + STAGES * kBTileBytes;
     static constexpr uint32_t kStageBufBytes = 32 * 128;
     static constexpr uint32_t kOffBar = kOffStage + 8 * kStageBufBytes;
@@ -203,25 +204,47 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int half = (warp - 2) >> 2;
         const int row_in_tile = quarter * 32 + lane;
         const uint32_t stage_addr = sbase + L::kOffStage + static_cast<uint32_t>(warp - 2) * L::kStageBufBytes;
-        uint8_t* srow = smem + L::kOffStage + (warp - 2) * L::kStageBufBytes + lane * kRowB;
+        uint8_t* stage_ptr = smem + L::kOffStage + (warp - 2) * L::kStageBufBytes;
+        const bool has_resid = p.resid_mode != kResidNone && p.resid_mode != kMaskRows;
         int acc = 0;
         uint32_t acc_phase = 0;
+        uint32_t nstore = 0;                              // chunks this warp has staged
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
             const int m_blk = tile / p.num_n_tiles;
             const int n_blk = tile - m_blk * p.num_n_tiles;
-            bool ok = mbar_wait(accf_bar(acc), acc_phase, abort_flag);
-            ok = __all_sync(0xffffffffu, ok);
-            if (!ok) break;
-            tc_fence_after();
             const int row = m_blk * kGemmBM + row_in_tile;
             const int n0 = n_blk * BN;
             const bool row_ok = row < p.M;
             const bool valid = (p.row_valid == nullptr) || !row_ok || (p.row_valid[row] != 0);
+            // Global reads are issued ahead of the accumulator: the bias as
+            // one coalesced float per lane (column nc + lane, broadcast by
+            // shuffles), one chunk ahead; the residual row of a full chunk at
+            // the top of the chunk (for the first chunk while the main loop
+            // still runs).
+            float4 rr[kCW / 4];
+            auto load_bias = [&](int nc) -> float {
+                return nc + lane < p.N ? __ldg(p.bias + nc + lane) : 0.0f;
+            };
+            auto load_resid = [&](int nc) {
+                if (has_resid && row_ok && nc + kCW <= p.N) {
+                    const float4* rp = reinterpret_cast<const float4*>(p.resid + static_cast<int64_t>(row) * p.ldr + nc);
+#pragma unroll
+                    for (int j = 0; j < kCW / 4; ++j) rr[j] = rp[j];
+                }
+            };
+            float b_cur = load_bias(n0 + half * kCW);
+            load_resid(n0 + half * kCW);
+            bool ok = mbar_wait(accf_bar(acc), acc_phase, abort_flag);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            tc_fence_after();
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
             for (int c = half * kCW; c < BN; c += 2 * kCW) {
                 const int nc = n0 + c;
+                if (c != half * kCW) load_resid(nc);
+                const float b_next = c + 2 * kCW < BN ? load_bias(nc + 2 * kCW) : 0.0f;
                 float v[kCW];
                 {
                     uint32_t r[32];
@@ -231,17 +254,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
                 }
                 if (nc < p.N) {
-                    if (nc + kCW <= p.N) {
+                    const bool full = nc + kCW <= p.N;
 #pragma unroll
-                        for (int j = 0; j < kCW; j += 4) {
-                            const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + nc + j));
-                            v[j] += bb.x; v[j + 1] += bb.y; v[j + 2] += bb.z; v[j + 3] += bb.w;
-                        }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < kCW; ++j)
-                            if (nc + j < p.N) v[j] += __ldg(p.bias + nc + j);
-                    }
+                    for (int j = 0; j < kCW; ++j) v[j] += __shfl_sync(0xffffffffu, b_cur, j);
                     if (p.act == 1) {
 #pragma unroll
                         for (int j = 0; j < kCW; ++j) v[j] = gelu_fast(v[j]);
@@ -250,29 +265,34 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
                         for (int j = 0; j < kCW; ++j) v[j] = 0.0f;
                     }
-                    if (p.resid_mode != kResidNone && p.resid_mode != kMaskRows && row_ok) {
-                        const float* rp = p.resid + static_cast<int64_t>(row) * p.ldr + nc;
+                    if (has_resid && row_ok) {
                         const bool keep_sub = valid || p.resid_mode == kResidAdd;
                         const bool keep_all = valid || p.resid_mode != kResidAddMaskAll;
-                        if (nc + kCW <= p.N) {
+                        if (full) {
 #pragma unroll
                             for (int j = 0; j < kCW; j += 4) {
-                                const float4 rr = *reinterpret_cast<const float4*>(rp + j);
-                                v[j] = keep_all ? rr.x + (keep_sub ? v[j] : 0.0f) : 0.0f;
-                                v[j + 1] = keep_all ? rr.y + (keep_sub ? v[j + 1] : 0.0f) : 0.0f;
-                                v[j + 2] = keep_all ? rr.z + (keep_sub ? v[j + 2] : 0.0f) : 0.0f;
-                                v[j + 3] = keep_all ? rr.w + (keep_sub ? v[j + 3] : 0.0f) : 0.0f;
+                                v[j] = keep_all ? rr[j / 4].x + (keep_sub ? v[j] : 0.0f) : 0.0f;
+                                v[j + 1] = keep_all ? rr[j / 4].y + (keep_sub ? v[j + 1] : 0.0f) : 0.0f;
+                                v[j + 2] = keep_all ? rr[j / 4].z + (keep_sub ? v[j + 2] : 0.0f) : 0.0f;
+                                v[j + 3] = keep_all ? rr[j / 4].w + (keep_sub ? v[j + 3] : 0.0f) : 0.0f;
                             }
                         } else {
+                            const float* rp = p.resid + static_cast<int64_t>(row) * p.ldr + nc;
 #pragma unroll
                             for (int j = 0; j < kCW; ++j)
                                 if (nc + j < p.N) v[j] = keep_all ? rp[j] + (keep_sub ? v[j] : 0.0f) : 0.0f;
                         }
                     }
                 }
-                // the previous store from this buffer has read it
-                if (lane == 0) bulk_wait_read<0>();
+                // fp16 chunks alternate between the two halves of the buffer:
+                // wait until the store that last read this half is done
+                const uint32_t sb = OUT_F16 ? (nstore & 1u) * 2048u : 0u;
+                if (lane == 0) {
+                    if constexpr (OUT_F16) bulk_wait_read<1>();
+                    else bulk_wait_read<0>();
+                }
                 __syncwarp();
+                uint8_t* srow = stage_ptr + sb + lane * kRowB;
                 if constexpr (OUT_F16) {
                     // 64 B rows, 64B swizzle: granule q of row r at q ^ ((r >> 1) & 3)
 #pragma unroll
@@ -295,9 +315,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0 && nc < p.N) {
-                    tma_store_2d(&tmap_out, stage_addr, nc, m_blk * kGemmBM + quarter * 32);
+                    tma_store_2d(&tmap_out, stage_addr + sb, nc, m_blk * kGemmBM + quarter * 32);
                     bulk_commit();
                 }
+                ++nstore;
+                b_cur = b_next;
             }
             tc_fence_before();
             mbar_arrive(acce_bar(acc));

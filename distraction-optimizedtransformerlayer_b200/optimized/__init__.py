@@ -9,6 +9,10 @@ Same modules and reading order as the reference package:
     kernels.py   dispatch into libdotl through kernel_ext (no fallbacks)
     graphs.py    CUDA graph capture and replay
     util.py      small shared helpers
+    pipeline.py  HostPipeline: host-in/host-out batches with the copies
+                 overlapped (no upstream counterpart)
+    tensor_parallel.py  the layer split over the GPUs of one box (no
+                 upstream counterpart)
 
 A harness declares `class UserOptimizedTransformer(OptimizedTransformer,
 BaselineTransformer)` exactly as upstream. The directory holding this package
@@ -18,5 +22,6 @@ reference's project root did.
 
 from . import cli, config, graphs, kernels, layers, util
 from .model import OptimizedTransformer
+from .pipeline import HostPipeline
 
-__all__ = ["OptimizedTransformer", "cli", "config", "graphs", "kernels", "layers", "util"]
+__all__ = ["OptimizedTransformer", "HostPipeline", "cli", "config", "graphs", "kernels", "layers", "util"]

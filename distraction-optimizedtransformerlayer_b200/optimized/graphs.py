@@ -38,15 +38,20 @@ class _GraphRunner:
         self.pinned = pinned
         self.replays = 0
 
-    def replay(self, x: torch.Tensor, mask: Optional[torch.Tensor]) -> torch.Tensor:
-        """Copy the inputs in, replay, return a clone of the output (the next
-        replay overwrites static_out in place)."""
+    def replay(self, x: torch.Tensor, mask: Optional[torch.Tensor],
+               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Copy the inputs in, replay, return the output copied out of the
+        graph's buffer (the next replay overwrites static_out in place): into
+        `out` when given, else into a new tensor."""
         self.static_x.copy_(x)
         if self.needs_mask:
             self.static_mask.copy_(mask)
         self.graph.replay()
         self.replays += 1
-        return self.static_out.clone()
+        if out is None:
+            return self.static_out.clone()
+        out.copy_(self.static_out)
+        return out
 
     def release(self) -> None:
         try:

@@ -74,19 +74,37 @@ class OptimizedTransformer(nn.Module):
         # trailing LayerNorm, so `normed` is already the model's output.
         return normed if dtype == torch.float32 else normed.to(dtype)
 
-    def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
         config.validate()
-        mask_is_trivial = self._mask_is_trivial(valid_token_mask)
-        use_mask = valid_token_mask is not None and not mask_is_trivial
+        # A given mask always takes the masked kernels. On an all-valid mask
+        # they cost the same as the unmasked ones and give identical values,
+        # so unlike upstream (model.py:68-93) no device->host sync is spent on
+        # _mask_is_trivial to pick a path.
+        use_mask = valid_token_mask is not None
         key = _graph_key(x, use_mask)
         runner = self._graphs.get(key)
         if runner is None:
             runner = self._maybe_capture(key, x, valid_token_mask, use_mask)
         if runner is not None:
-            return runner.replay(x, valid_token_mask)
+            return runner.replay(x, valid_token_mask, out)
         if config.MICROBATCH_FALLBACK and x.is_cuda and x.shape[0] > 1:
-            return self._forward_chunk_on_oom(x, valid_token_mask, use_mask)
-        return self._forward_eager(x, valid_token_mask, use_mask)
+            y = self._forward_chunk_on_oom(x, valid_token_mask, use_mask)
+        else:
+            y = self._forward_eager(x, valid_token_mask, use_mask)
+        if out is None:
+            return y
+        out.copy_(y)
+        return out
+
+    def forward_into(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor],
+                     out: torch.Tensor) -> torch.Tensor:
+        """forward() writing its result into `out` (x's shape and dtype), so a
+        serving loop reuses its own output buffers instead of allocating one
+        per call. No upstream counterpart."""
+        if out.shape != x.shape or out.dtype != x.dtype or out.device != x.device:
+            raise ValueError("out must match x in shape, dtype and device")
+        return self.forward(x, valid_token_mask, out=out)
 
     def _rows_within_budget(self, x: torch.Tensor) -> int:
         rows = x.shape[0]

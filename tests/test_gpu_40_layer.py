@@ -92,3 +92,39 @@ def test_batch_rows_independent(kernels):
         full = model(x, mask)
         one = model(x[1:2].contiguous(), mask[1:2].contiguous())
     assert torch.equal(full[1:2], one)
+
+
+def test_all_valid_mask_matches_no_mask(kernels):
+    """A given all-valid mask takes the masked kernels; the output is the same
+    bits as with no mask (the reference instead skips the mask after a host
+    check)."""
+    cfg, _ = O.BASELINE_CONFIGS[2]
+    cfg = dataclasses.replace(cfg, batch_size=2)
+    model, _ = _model(cfg, 5)
+    x, mask = O.generate_random_case(cfg, 21, 0.0, 1.0)
+    assert bool(mask.all())
+    x, mask = x.cuda(), mask.cuda()
+    with torch.inference_mode():
+        a = model(x, mask)
+        b = model(x, None)
+    assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("cfg_id", [1, 2])
+def test_host_pipeline_matches_forward(kernels, cfg_id):
+    """HostPipeline (pinned host batches in and out, copies overlapped with
+    the neighbouring batches' forwards) returns exactly model(x, mask) per batch."""
+    from optimized import HostPipeline
+
+    cfg, pad = O.BASELINE_CONFIGS[cfg_id]
+    model, _ = _model(cfg, 3)
+    cases = [O.generate_random_case(cfg, 40 + i, pad, 1.0) for i in range(5)]
+    xs = [x.pin_memory() for x, _ in cases]
+    ms = [m.pin_memory() for _, m in cases]
+    outs = [torch.empty(x.shape, dtype=torch.float32).pin_memory() for x in xs]
+    pipe = HostPipeline(model, torch.device("cuda", 0))
+    with torch.inference_mode():
+        pipe.run(xs, ms, outs)
+        ref = [model(x.cuda(), m.cuda()).cpu() for x, m in zip(xs, ms)]
+    for o, r in zip(outs, ref):
+        assert torch.equal(o, r)
