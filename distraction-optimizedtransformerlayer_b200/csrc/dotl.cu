@@ -10,6 +10,7 @@
 #include "../../include/dotl.h"
 #include "attention.cuh"
 #include "gemm.cuh"
+#include "gemm_ln.cuh"
 #include "layernorm.cuh"
 
 #include <cstdarg>
@@ -146,10 +147,7 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap&
     return check_launch("dotl_linear");
 }
 
-// N tile for an [M,N,K] problem, from a cost model in SM cycles: waves of
-// persistent tiles, each a fixed start-up plus K/64 steps that cost the larger
-// of the MMA time (128 x BN x 64 at 8192 FLOP/clk) and the time to stream the
-// A and W stage from L2 (about 120 bytes/clk per SM).
+// N tile for an [M,N,K] problem.
 int pick_tile_n(int64_t M, int64_t N, int64_t K, int sms) {
     // The widest tile that still gives most SMs a tile: wide tiles read each
     // operand byte into fewer CTAs (A is read once per N tile, W once per M
@@ -162,6 +160,94 @@ int pick_tile_n(int64_t M, int64_t N, int64_t K, int sms) {
         if (tiles * 5 >= static_cast<int64_t>(sms) * 3) return bn;
     }
     return 64;
+}
+
+// A [rows, cols] fp32 or fp16 output written by 32 x 32 TMA store boxes (128 B
+// fp32 rows with 128B swizzle, 64 B fp16 rows with 64B swizzle).
+int encode_out_map(CUtensorMap* map, void* base, int64_t rows, int64_t cols, int64_t ld, int dtype, const char* who) {
+    EncodeTiledFn fn = encode_fn();
+    if (fn == nullptr) return fail(DOTL_ECUDA, "%s: cuTensorMapEncodeTiled is unavailable from the driver", who);
+    const cuuint64_t odims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t ostr[1] = {static_cast<cuuint64_t>(ld) * (dtype == DOTL_F16 ? 2 : 4)};
+    const cuuint32_t obox[2] = {32u, 32u};
+    const cuuint32_t oes[2] = {1, 1};
+    const CUresult r = fn(map, dtype == DOTL_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                          base, odims, ostr, obox, oes, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          dtype == DOTL_F16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(DOTL_ECUDA, "%s: cuTensorMapEncodeTiled (output) failed (CUresult %d)", who, (int)r);
+    return DOTL_OK;
+}
+
+// ------------------------------------------------- GEMM + LayerNorm epilogue --
+
+// Clusters of `cs` CTAs of this kernel that fit on the device at once.
+template <typename Kernel>
+int max_clusters(Kernel kernel, int cs, uint32_t smem, int* out) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(cs));
+    cfg.blockDim = dim3(dotl::kGemmThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(cs);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
+    if (e != cudaSuccess || n <= 0)
+        return fail(DOTL_ECUDA, "cudaOccupancyMaxActiveClusters(cluster %d) failed: %s", cs,
+                    e != cudaSuccess ? cudaGetErrorString(e) : "no cluster fits");
+    *out = n;
+    return DOTL_OK;
+}
+
+template <int BN, int STAGES, bool NORM_F16>
+int launch_gemm_ln(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tn,
+                   const dotl::GemmLnParams& p, int dev, cudaStream_t stream) {
+    using L = dotl::GemmLnSmem<BN, STAGES>;
+    auto kernel = dotl::gemm_ln_kernel<BN, STAGES, NORM_F16>;
+    static bool done[kMaxDevices] = {false};
+    static int fit[kMaxDevices][dotl::kLnMaxCluster + 1] = {};
+    if (int rc = ensure_smem(kernel, L::kAlloc, dev, done)) return rc;
+    int clusters = (dev >= 0 && dev < kMaxDevices) ? fit[dev][p.cs] : 0;
+    if (clusters == 0) {
+        if (int rc = max_clusters(kernel, p.cs, L::kAlloc, &clusters)) return rc;
+        if (dev >= 0 && dev < kMaxDevices) fit[dev][p.cs] = clusters;
+    }
+    if (clusters > p.num_m_tiles) clusters = p.num_m_tiles;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(clusters * p.cs));
+    cfg.blockDim = dim3(dotl::kGemmThreads);
+    cfg.dynamicSmemBytes = L::kAlloc;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = static_cast<unsigned>(p.cs);
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tw, tx, tn, p);
+    if (e != cudaSuccess) return fail(DOTL_ECUDA, "dotl_linear_ln: launch failed: %s", cudaGetErrorString(e));
+    return check_launch("dotl_linear_ln");
+}
+
+// N tile for the LayerNorm epilogue: N = cs * BN with cs <= 8; the widest
+// tile that still gives most SMs work, else the narrowest (most CTAs).
+int pick_tile_n_ln(int64_t M, int64_t N, int sms) {
+    const int64_t mt = (M + dotl::kGemmBM - 1) / dotl::kGemmBM;
+    int narrowest = 0;
+    for (int bn : {256, 128, 64}) {
+        if (N % bn != 0 || N / bn > dotl::kLnMaxCluster) continue;
+        if (mt * (N / bn) * 5 >= static_cast<int64_t>(sms) * 3) return bn;
+        narrowest = bn;
+    }
+    return narrowest;
 }
 
 // ------------------------------------------------------------- attention --
@@ -337,21 +423,8 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
     const cuuint64_t wdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
     const cuuint64_t wstr[1] = {static_cast<cuuint64_t>(ldw) * 2};
     if (int rc = encode_f16_map(&tw, w, 2, wdims, wstr, dotl::kGemmBK, static_cast<uint32_t>(bn), who)) return rc;
-    // output: 32 x 32 boxes (128 B fp32 rows with 128B swizzle, 64 B fp16 rows with 64B swizzle)
     CUtensorMap to;
-    {
-        EncodeTiledFn fn = encode_fn();
-        if (fn == nullptr) return fail(DOTL_ECUDA, "%s: cuTensorMapEncodeTiled is unavailable from the driver", who);
-        const cuuint64_t odims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M)};
-        const cuuint64_t ostr[1] = {static_cast<cuuint64_t>(ldo) * (out_dtype == DOTL_F16 ? 2 : 4)};
-        const cuuint32_t obox[2] = {32u, 32u};
-        const cuuint32_t oes[2] = {1, 1};
-        const CUresult r = fn(&to, out_dtype == DOTL_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
-                              2, out, odims, ostr, obox, oes, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                              out_dtype == DOTL_F16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
-                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-        if (r != CUDA_SUCCESS) return fail(DOTL_ECUDA, "%s: cuTensorMapEncodeTiled (out) failed (CUresult %d)", who, (int)r);
-    }
+    if (int rc = encode_out_map(&to, out, M, N, ldo, out_dtype, who)) return rc;
 
     dotl::GemmParams p;
     p.M = static_cast<int>(M);
@@ -376,6 +449,87 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
                                      : launch_gemm<64, 7, false>(ta, tw, to, p, dev, s);
     return out_dtype == DOTL_F16 ? launch_gemm<128, 5, true>(ta, tw, to, p, dev, s)
                                  : launch_gemm<128, 5, false>(ta, tw, to, p, dev, s);
+}
+
+int dotl_linear_ln(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,
+                   const float* bias, const float* resid, int64_t ldr, const uint8_t* row_valid, int resid_mode,
+                   float* out, int64_t ldo, const float* ln_weight, const float* ln_bias, float eps, void* normed,
+                   int normed_dtype, int64_t ldn, const uint8_t* normed_row_valid, int tile_n, void* stream) {
+    const char* who = "linear_add_layernorm";
+    if (M < 0 || N <= 0 || K <= 0) return fail(DOTL_EINVAL, "%s: bad shape M=%lld N=%lld K=%lld", who, (long long)M, (long long)N, (long long)K);
+    if (M > (int64_t)0x7fffffff - 256 || N > 0x7fffffff || K > 0x7fffffff)
+        return fail(DOTL_EUNSUPPORTED, "%s: dimensions must fit in 31 bits", who);
+    if (resid_mode != DOTL_RESID_NONE && resid_mode != DOTL_RESID_ADD && resid_mode != DOTL_RESID_ADD_MASKSUB &&
+        resid_mode != DOTL_RESID_ADD_MASKALL)
+        return fail(DOTL_EINVAL, "%s: residual mode %d is not one of NONE, ADD, ADD_MASKSUB, ADD_MASKALL", who, resid_mode);
+    if (normed_dtype != DOTL_F32 && normed_dtype != DOTL_F16) return fail(DOTL_EINVAL, "%s: normed dtype must be DOTL_F32 or DOTL_F16", who);
+    if (!(eps >= 0.0f)) return fail(DOTL_EINVAL, "%s: eps must be >= 0", who);
+    if (M == 0) return DOTL_OK;
+    if (a == nullptr || w == nullptr || bias == nullptr || ln_weight == nullptr || ln_bias == nullptr || normed == nullptr)
+        return fail(DOTL_EINVAL, "%s: NULL pointer", who);
+    if (K % 8 != 0 || lda % 8 != 0 || ldw % 8 != 0 || lda < K || ldw < K)
+        return fail(DOTL_EUNSUPPORTED, "%s: K, lda and ldw must be multiples of 8 (16-byte fp16 rows for TMA), got K=%lld lda=%lld ldw=%lld", who, (long long)K, (long long)lda, (long long)ldw);
+    if (!aligned16(a) || !aligned16(w)) return fail(DOTL_EUNSUPPORTED, "%s: a and w must be 16-byte aligned", who);
+    if (!aligned16(bias) || !aligned16(ln_weight) || !aligned16(ln_bias))
+        return fail(DOTL_EUNSUPPORTED, "%s: bias, ln_weight and ln_bias must be 16-byte aligned", who);
+    if (out != nullptr && (ldo < N || !aligned16(out) || ldo % 4 != 0))
+        return fail(DOTL_EUNSUPPORTED, "%s: out must be 16-byte aligned with ldo >= N, ldo %% 4 == 0", who);
+    if (ldn < N || !aligned16(normed) || ldn % 8 != 0)
+        return fail(DOTL_EUNSUPPORTED, "%s: normed must be 16-byte aligned with ldn >= N, ldn %% 8 == 0", who);
+    if (resid_mode != DOTL_RESID_NONE) {
+        if (resid == nullptr) return fail(DOTL_EINVAL, "%s: residual mode %d needs resid", who, resid_mode);
+        if (!aligned16(resid) || ldr % 4 != 0 || ldr < N) return fail(DOTL_EUNSUPPORTED, "%s: resid must be 16-byte aligned with ldr >= N, ldr %% 4 == 0", who);
+    }
+    if ((resid_mode == DOTL_RESID_ADD_MASKSUB || resid_mode == DOTL_RESID_ADD_MASKALL) && row_valid == nullptr)
+        return fail(DOTL_EINVAL, "%s: masked residual mode needs row_valid", who);
+
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    int bn = tile_n;
+    if (bn == 0) bn = pick_tile_n_ln(M, N, sm_count(dev));
+    if (bn != 64 && bn != 128 && bn != 256)
+        return fail(DOTL_EUNSUPPORTED, "%s: N=%lld must be 64, 128 or 256 times a cluster size of at most %d", who,
+                    (long long)N, dotl::kLnMaxCluster);
+    if (N % bn != 0 || N / bn > dotl::kLnMaxCluster)
+        return fail(DOTL_EUNSUPPORTED, "%s: N=%lld is not tile_n=%d times a cluster size of at most %d", who,
+                    (long long)N, bn, dotl::kLnMaxCluster);
+
+    CUtensorMap ta, tw, tx, tn;
+    const cuuint64_t adims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+    const cuuint64_t astr[1] = {static_cast<cuuint64_t>(lda) * 2};
+    if (int rc = encode_f16_map(&ta, a, 2, adims, astr, dotl::kGemmBK, dotl::kGemmBM, who)) return rc;
+    const cuuint64_t wdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
+    const cuuint64_t wstr[1] = {static_cast<cuuint64_t>(ldw) * 2};
+    if (int rc = encode_f16_map(&tw, w, 2, wdims, wstr, dotl::kGemmBK, static_cast<uint32_t>(bn), who)) return rc;
+    // with out == NULL the x map points at `normed` and is never used
+    if (int rc = encode_out_map(&tx, out != nullptr ? static_cast<void*>(out) : normed, M, N,
+                                out != nullptr ? ldo : ldn, out != nullptr ? DOTL_F32 : normed_dtype, who))
+        return rc;
+    if (int rc = encode_out_map(&tn, normed, M, N, ldn, normed_dtype, who)) return rc;
+
+    dotl::GemmLnParams p;
+    p.M = static_cast<int>(M);
+    p.N = static_cast<int>(N);
+    p.K = static_cast<int>(K);
+    p.num_m_tiles = static_cast<int>((M + dotl::kGemmBM - 1) / dotl::kGemmBM);
+    p.cs = static_cast<int>(N / bn);
+    p.bias = bias;
+    p.resid = resid;
+    p.ldr = ldr;
+    p.row_valid = row_valid;
+    p.resid_mode = resid_mode;
+    p.store_x = out != nullptr ? 1 : 0;
+    p.ln_w = ln_weight;
+    p.ln_b = ln_bias;
+    p.eps = eps;
+    p.norm_row_valid = normed_row_valid;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const bool f16 = normed_dtype == DOTL_F16;
+    if (bn == 256)
+        return f16 ? launch_gemm_ln<256, 3, true>(ta, tw, tx, tn, p, dev, s) : launch_gemm_ln<256, 3, false>(ta, tw, tx, tn, p, dev, s);
+    if (bn == 128)
+        return f16 ? launch_gemm_ln<128, 5, true>(ta, tw, tx, tn, p, dev, s) : launch_gemm_ln<128, 5, false>(ta, tw, tx, tn, p, dev, s);
+    return f16 ? launch_gemm_ln<64, 7, true>(ta, tw, tx, tn, p, dev, s) : launch_gemm_ln<64, 7, false>(ta, tw, tx, tn, p, dev, s);
 }
 
 int dotl_attention(const void* q, const void* k, const void* v, int B, int H, int S, int head_dim,

@@ -110,6 +110,72 @@ __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity) {
     return true;
 }
 
+// ----------------------------------------------------- thread-block clusters --
+// Distributed shared memory: a CTA reaches a peer's shared memory through the
+// shared::cluster window (mapa), stores there, and arrives on the peer's
+// mbarriers with release semantics at cluster scope; the peer waits on its own
+// barrier with acquire at cluster scope. No TMA multicast anywhere.
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// The shared::cluster address of local shared address `addr` in CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ void st_cluster_v2f32(uint32_t caddr, float a, float b) {
+    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(caddr), "f"(a), "f"(b) : "memory");
+}
+
+// Arrives on an mbarrier of a peer CTA (shared::cluster address), ordering this
+// thread's earlier stores (remote ones included) before the arrival.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// mbar_wait for barriers that peers arrive on: acquire at cluster scope, so the
+// peers' stores into this CTA's shared memory are visible afterwards. Bounded
+// like mbar_wait (limit_ns), and returns at once if this CTA aborted.
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                                  unsigned long long limit_ns = kWaitLimitNs) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    while (true) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if (abort_flag != nullptr && *abort_flag) return false;
+        if (global_ns() - t0 > limit_ns) {
+            if (abort_flag != nullptr) *abort_flag = 1;
+            atomicOr(&g_dotl_dev_error, kDevErrWaitTimeout);
+            return false;
+        }
+    }
+}
+
+// Every thread of every CTA of the cluster, once, right after the barriers
+// are initialised (before any peer may arrive on them). Nothing precedes it
+// that could stall: all CTAs of a cluster are launched together.
+__device__ __forceinline__ void cluster_sync_after_init() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // ---------------------------------------------- programmatic dependent launch --
 // Kernels are launched with programmatic stream serialization: the next kernel
 // in the stream may start its prologue while this one drains. pdl_wait() blocks

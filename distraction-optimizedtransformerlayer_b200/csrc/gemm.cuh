@@ -63,7 +63,7 @@ struct GemmSmem {
     static constexpr uint32_t kOffStage = kOffB + STAGES * kBTileBytes;
     static constexpr uint32_t kStageBufBytes = 32 * 128;
     static constexpr uint32_t kOffBar = kOffStage + 8 * kStageBufBytes;
-    // full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], drain
+    // full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], drain (GemmBars)
     static constexpr uint32_t kNumBars = 2 * STAGES + 5;
     static constexpr uint32_t kOffSlot = kOffBar + kNumBars * 8;
     static constexpr uint32_t kOffAbort = kOffSlot + 4;
@@ -71,6 +71,118 @@ struct GemmSmem {
     static constexpr uint32_t kAlloc = kBytes + 1024;   // room to align the base to 1024
     static constexpr uint32_t kTmemCols = 2 * BN;
 };
+
+// Which output tiles a CTA visits: t = first, first + stride, ... < count.
+// With n_fixed < 0, t enumerates (m, n) with n fastest; otherwise t is the M
+// block and every tile is in N block n_fixed (the cluster-row schedule of the
+// LayerNorm epilogue kernel).
+struct TileSched {
+    int first, stride, count, n_tiles, n_fixed;
+    __device__ __forceinline__ void decode(int t, int& m_blk, int& n_blk) const {
+        if (n_fixed >= 0) {
+            m_blk = t;
+            n_blk = n_fixed;
+        } else {
+            m_blk = t / n_tiles;
+            n_blk = t - m_blk * n_tiles;
+        }
+    }
+};
+
+// Barriers every GEMM kernel keeps at the start of its barrier block:
+// full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], drain.
+template <int STAGES>
+struct GemmBars {
+    uint32_t bar0;
+    __device__ __forceinline__ uint32_t full(int s) const { return bar0 + 8u * s; }
+    __device__ __forceinline__ uint32_t empty(int s) const { return bar0 + 8u * (STAGES + s); }
+    __device__ __forceinline__ uint32_t accf(int b) const { return bar0 + 8u * (2 * STAGES + b); }
+    __device__ __forceinline__ uint32_t acce(int b) const { return bar0 + 8u * (2 * STAGES + 2 + b); }
+    __device__ __forceinline__ uint32_t drain() const { return bar0 + 8u * (2 * STAGES + 4); }
+    static constexpr int kCount = 2 * STAGES + 5;
+};
+
+// TMA producer (one thread): A and W k-blocks of every scheduled tile into
+// the STAGES-deep ring. On abort, waits out the copies still in flight.
+template <int BN, int STAGES>
+__device__ __forceinline__ void gemm_produce(const CUtensorMap* tmap_a, const CUtensorMap* tmap_w, uint32_t sbase,
+                                             GemmBars<STAGES> bars, volatile int* abort_flag, const TileSched& ts,
+                                             int num_kb) {
+    using L = GemmSmem<BN, STAGES>;
+    int stage = 0;
+    uint32_t phase = 0;
+    int issued_phase[STAGES];
+    for (int s = 0; s < STAGES; ++s) issued_phase[s] = -1;
+    for (int t = ts.first; t < ts.count; t += ts.stride) {
+        int m_blk, n_blk;
+        ts.decode(t, m_blk, n_blk);
+        for (int kb = 0; kb < num_kb; ++kb) {
+            if (!mbar_wait(bars.empty(stage), phase ^ 1u, abort_flag)) goto producer_done;
+            mbar_arrive_expect_tx(bars.full(stage), L::kStageBytes);
+            tma_load_2d(sbase + L::kOffA + stage * kGemmATileBytes, tmap_a, bars.full(stage), kb * kGemmBK,
+                        m_blk * kGemmBM);
+            tma_load_2d(sbase + L::kOffB + stage * L::kBTileBytes, tmap_w, bars.full(stage), kb * kGemmBK,
+                        n_blk * BN);
+            issued_phase[stage] = static_cast<int>(phase);
+            if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1u;
+            }
+        }
+    }
+producer_done:
+    if (*abort_flag) {
+        // Copies still in flight land in this CTA's smem: wait them out.
+        for (int s = 0; s < STAGES; ++s)
+            if (issued_phase[s] >= 0) mbar_wait_drain(bars.full(s), static_cast<uint32_t>(issued_phase[s]));
+    }
+}
+
+// MMA issuer (one thread): each scheduled tile into TMEM accumulator
+// 0, 1, 0, ... (BN columns each); every issued MMA has completed on return.
+template <int BN, int STAGES>
+__device__ __forceinline__ void gemm_mma(uint32_t sbase, uint32_t tmem_base, GemmBars<STAGES> bars,
+                                         volatile int* abort_flag, const TileSched& ts, int num_kb) {
+    using L = GemmSmem<BN, STAGES>;
+    constexpr uint32_t idesc = idesc_f16_f32(kGemmBM, BN, false, false);
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = ts.first; t < ts.count; t += ts.stride) {
+        if (!mbar_wait(bars.acce(acc), acc_phase ^ 1u, abort_flag)) goto mma_done;
+        tc_fence_after();
+        {
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+            for (int kb = 0; kb < num_kb; ++kb) {
+                if (!mbar_wait(bars.full(stage), phase, abort_flag)) goto mma_done;
+                tc_fence_after();
+                const uint32_t a_addr = sbase + L::kOffA + stage * kGemmATileBytes;
+                const uint32_t b_addr = sbase + L::kOffB + stage * L::kBTileBytes;
+#pragma unroll
+                for (int kk = 0; kk < kGemmBK / 16; ++kk) {
+                    const uint64_t ad = smem_desc(a_addr + kk * 32, 16, 1024, kSwizzle128);
+                    const uint64_t bd = smem_desc(b_addr + kk * 32, 16, 1024, kSwizzle128);
+                    mma_f16_ss(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+                }
+                tc_commit(bars.empty(stage));
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+        }
+        tc_commit(bars.accf(acc));
+        if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1u;
+        }
+    }
+mma_done:
+    // Every MMA this thread issued has completed once drain fires.
+    tc_commit(bars.drain());
+    mbar_wait_drain(bars.drain(), 0);
+}
 
 template <int BN, int STAGES, bool OUT_F16>
 __global__ void __launch_bounds__(kGemmThreads, 1)
@@ -82,11 +194,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                                ~static_cast<uintptr_t>(1023));
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bar0 = sbase + L::kOffBar;
-    auto full_bar = [&](int s) { return bar0 + 8u * s; };
-    auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
-    auto accf_bar = [&](int b) { return bar0 + 8u * (2 * STAGES + b); };
-    auto acce_bar = [&](int b) { return bar0 + 8u * (2 * STAGES + 2 + b); };
-    const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 4);
+    const GemmBars<STAGES> bars{bar0};
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffAbort);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffSlot);
 
@@ -95,14 +203,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(full_bar(s), 1);
-            mbar_init(empty_bar(s), 1);
+            mbar_init(bars.full(s), 1);
+            mbar_init(bars.empty(s), 1);
         }
         for (int b = 0; b < 2; ++b) {
-            mbar_init(accf_bar(b), 1);
-            mbar_init(acce_bar(b), 256);
+            mbar_init(bars.accf(b), 1);
+            mbar_init(bars.acce(b), 256);
         }
-        mbar_init(drain_bar, 1);
+        mbar_init(bars.drain(), 1);
         *abort_flag = 0;
         fence_barrier_init();
         tma_prefetch_map(&tmap_a);
@@ -123,73 +231,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int num_tiles = p.num_m_tiles * p.num_n_tiles;
     const int num_kb = (p.K + kGemmBK - 1) / kGemmBK;
 
+    const TileSched ts{static_cast<int>(blockIdx.x), static_cast<int>(gridDim.x), num_tiles, p.num_n_tiles, -1};
     if (warp == 0 && lane == 0) {
-        // ---------------------------------------------------- TMA producer --
-        int stage = 0;
-        uint32_t phase = 0;
-        int issued_phase[STAGES];
-        for (int s = 0; s < STAGES; ++s) issued_phase[s] = -1;
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-            const int m_blk = tile / p.num_n_tiles;
-            const int n_blk = tile - m_blk * p.num_n_tiles;
-            for (int kb = 0; kb < num_kb; ++kb) {
-                if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) goto producer_done;
-                mbar_arrive_expect_tx(full_bar(stage), L::kStageBytes);
-                tma_load_2d(sbase + L::kOffA + stage * kGemmATileBytes, &tmap_a, full_bar(stage),
-                            kb * kGemmBK, m_blk * kGemmBM);
-                tma_load_2d(sbase + L::kOffB + stage * L::kBTileBytes, &tmap_w, full_bar(stage),
-                            kb * kGemmBK, n_blk * BN);
-                issued_phase[stage] = static_cast<int>(phase);
-                if (++stage == STAGES) {
-                    stage = 0;
-                    phase ^= 1u;
-                }
-            }
-        }
-    producer_done:
-        if (*abort_flag) {
-            // Copies still in flight land in this CTA's smem: wait them out.
-            for (int s = 0; s < STAGES; ++s)
-                if (issued_phase[s] >= 0) mbar_wait_drain(full_bar(s), static_cast<uint32_t>(issued_phase[s]));
-        }
+        gemm_produce<BN, STAGES>(&tmap_a, &tmap_w, sbase, bars, abort_flag, ts, num_kb);
     } else if (warp == 1 && lane == 0) {
-        // ------------------------------------------------------ MMA issuer --
-        constexpr uint32_t idesc = idesc_f16_f32(kGemmBM, BN, false, false);
-        int stage = 0;
-        uint32_t phase = 0;
-        int acc = 0;
-        uint32_t acc_phase = 0;
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-            if (!mbar_wait(acce_bar(acc), acc_phase ^ 1u, abort_flag)) goto mma_done;
-            tc_fence_after();
-            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-            for (int kb = 0; kb < num_kb; ++kb) {
-                if (!mbar_wait(full_bar(stage), phase, abort_flag)) goto mma_done;
-                tc_fence_after();
-                const uint32_t a_addr = sbase + L::kOffA + stage * kGemmATileBytes;
-                const uint32_t b_addr = sbase + L::kOffB + stage * L::kBTileBytes;
-#pragma unroll
-                for (int kk = 0; kk < kGemmBK / 16; ++kk) {
-                    const uint64_t ad = smem_desc(a_addr + kk * 32, 16, 1024, kSwizzle128);
-                    const uint64_t bd = smem_desc(b_addr + kk * 32, 16, 1024, kSwizzle128);
-                    mma_f16_ss(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
-                }
-                tc_commit(empty_bar(stage));
-                if (++stage == STAGES) {
-                    stage = 0;
-                    phase ^= 1u;
-                }
-            }
-            tc_commit(accf_bar(acc));
-            if (++acc == 2) {
-                acc = 0;
-                acc_phase ^= 1u;
-            }
-        }
-    mma_done:
-        // Every MMA this thread issued has completed once drain_bar fires.
-        tc_commit(drain_bar);
-        mbar_wait_drain(drain_bar, 0);
+        gemm_mma<BN, STAGES>(sbase, tmem_base, bars, abort_flag, ts, num_kb);
     } else if (warp >= 2) {
         // -------------------------------------------------------- epilogue --
         // Eight warps, two per TMEM lane quarter (the 32 rows a warp may
@@ -234,7 +280,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             };
             float b_cur = load_bias(n0 + half * kCW);
             load_resid(n0 + half * kCW);
-            bool ok = mbar_wait(accf_bar(acc), acc_phase, abort_flag);
+            bool ok = mbar_wait(bars.accf(acc), acc_phase, abort_flag);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             tc_fence_after();
@@ -322,7 +368,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 b_cur = b_next;
             }
             tc_fence_before();
-            mbar_arrive(acce_bar(acc));
+            mbar_arrive(bars.acce(acc));
             if (++acc == 2) {
                 acc = 0;
                 acc_phase ^= 1u;

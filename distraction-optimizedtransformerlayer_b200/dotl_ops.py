@@ -48,6 +48,8 @@ _SIGNATURES = {
     "dotl_layernorm": ([_vp, _vp, _vp, _vp, _vp, _vp, _i32, _vp, _i64, _i64, _f32, _vp], _i32),
     "dotl_linear": ([_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i32, _vp, _i64, _vp, _i32,
                      _vp, _i32, _i64, _i32, _vp], _i32),
+    "dotl_linear_ln": ([_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _i32, _vp, _i64,
+                        _vp, _vp, _f32, _vp, _i32, _i64, _vp, _i32, _vp], _i32),
     "dotl_attention": ([_vp, _vp, _vp, _i32, _i32, _i32, _i32, _P64, _P64, _P64, _vp, _i32, _P64,
                         _i32, _f32, _vp, _i32, _vp], _i32),
 }
@@ -205,6 +207,59 @@ def linear_fp16(a16: torch.Tensor, w16: torch.Tensor, bias: torch.Tensor, act: i
         out.stride(-2) if out.dim() >= 2 else N, tile_n, _stream(a16.device))
     _check(rc)
     return out
+
+
+def linear_ln_supported(N: int) -> bool:
+    """Whether dotl_linear_ln covers a row of N columns (64, 128 or 256 times
+    a cluster of at most 8 CTAs)."""
+    return any(N % bn == 0 and N // bn <= 8 for bn in (64, 128, 256))
+
+
+_SMS: Optional[int] = None
+
+
+def linear_ln_preferred(M: int, N: int) -> bool:
+    """Whether the layer should take dotl_linear_ln over the GEMM + LayerNorm
+    kernel pair for an [M, N] output. The fused kernel saves the LayerNorm's
+    HBM round trip but holds each row block in a cluster of N / tile CTAs that
+    must exchange statistics; measured on B200 it wins when a 256-wide tile
+    covers the row with at most 4 CTAs per cluster and the row blocks fill at
+    least two waves of the SMs, and loses on small or 8-wide-cluster shapes."""
+    global _SMS
+    if N % 256 != 0 or N // 256 > 4:
+        return False
+    if _SMS is None:
+        _SMS = num_sms()
+    return ((M + 127) // 128) * (N // 256) >= 2 * _SMS
+
+
+def linear_ln(a16: torch.Tensor, w16: torch.Tensor, bias: torch.Tensor, ln_w: torch.Tensor,
+              ln_b: torch.Tensor, eps: float, resid: Optional[torch.Tensor] = None,
+              row_valid: Optional[torch.Tensor] = None, resid_mode: int = RESID_NONE,
+              store_x: bool = True, normed_half: bool = True,
+              normed_row_valid: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+              normed: Optional[torch.Tensor] = None, tile_n: int = 0):
+    """(x_new, normed): x_new = resid epilogue(a16 @ w16^T + bias) in fp32 (None
+    when store_x is False) and normed = LayerNorm(x_new) * ln_w + ln_b, from one
+    kernel whose CTA cluster shares each row's statistics."""
+    K = a16.shape[-1]
+    M = a16.numel() // K
+    N = w16.shape[0]
+    lead = a16.shape[:-1]
+    if store_x and out is None:
+        out = torch.empty((*lead, N), dtype=torch.float32, device=a16.device)
+    if normed is None:
+        normed = torch.empty((*lead, N), dtype=torch.float16 if normed_half else torch.float32,
+                             device=a16.device)
+    rc = lib().dotl_linear_ln(
+        a16.data_ptr(), M, K, a16.stride(-2) if a16.dim() >= 2 else K, w16.data_ptr(), N, w16.stride(0),
+        bias.data_ptr(), _ptr(resid), resid.stride(-2) if resid is not None and resid.dim() >= 2 else N,
+        _ptr(row_valid), resid_mode, out.data_ptr() if store_x else None,
+        out.stride(-2) if store_x and out.dim() >= 2 else N, ln_w.data_ptr(), ln_b.data_ptr(), float(eps),
+        normed.data_ptr(), F16 if normed.dtype == torch.float16 else F32,
+        normed.stride(-2) if normed.dim() >= 2 else N, _ptr(normed_row_valid), tile_n, _stream(a16.device))
+    _check(rc)
+    return (out if store_x else None), normed
 
 
 def attention_packed(q16: torch.Tensor, k16: torch.Tensor, v16: torch.Tensor, causal: bool,

@@ -69,6 +69,25 @@ def _linear(a16: torch.Tensor, w16: torch.Tensor, bias32: torch.Tensor, act: int
                          resid_mode=resid_mode, out_half=out_half)
 
 
+def _linear_ln_ok(rows: int, n: int) -> bool:
+    """Whether the layer takes the GEMM + LayerNorm kernel for rows x n outputs
+    (where it beats the GEMM and LayerNorm kernels run one after the other)."""
+    return _custom_kernels().linear_ln_preferred(rows, n)
+
+
+def _linear_ln(a16: torch.Tensor, w16: torch.Tensor, bias32: torch.Tensor, norm,
+               resid: Optional[torch.Tensor] = None, row_valid: Optional[torch.Tensor] = None,
+               resid_mode: int = 0, store_x: bool = True, normed_half: bool = True,
+               normed_row_valid: Optional[torch.Tensor] = None):
+    """(x_new, norm(x_new)) from one kernel: x_new = epilogue(a16 @ w16^T + bias)
+    as _linear computes it (fp32; None when store_x is False), then the
+    LayerNorm over its rows (fp16 or fp32, padded rows 0 with normed_row_valid)."""
+    k = _custom_kernels()
+    return k.linear_ln(a16, w16, bias32, _f32_param(norm, "weight"), _f32_param(norm, "bias"), norm.eps,
+                       resid=resid, row_valid=row_valid, resid_mode=resid_mode, store_x=store_x,
+                       normed_half=normed_half, normed_row_valid=normed_row_valid)
+
+
 def _linear_bias(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,
                  out_half: bool = False) -> torch.Tensor:
     """x @ weight^T + bias with the reference signature (fp32 weight)."""

@@ -25,7 +25,8 @@ import torch
 import torch.nn as nn
 
 from . import config
-from .kernels import (_attention_dispatch, _f32_param, _layernorm, _linear, _linear_bias)
+from .kernels import (_attention_dispatch, _f32_param, _layernorm, _linear, _linear_bias, _linear_ln,
+                      _linear_ln_ok)
 from .util import _version_or_none
 
 RESID_ADD, RESID_ADD_MASKSUB, RESID_ADD_MASKALL = 1, 2, 3
@@ -104,12 +105,14 @@ class MySelfAttention(nn.Module):
 
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None,
                 causal: bool = False, mask_is_trivial: bool = False,
-                residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+                residual: Optional[torch.Tensor] = None, norm: Optional["MyLayerNorm"] = None):
         """out_proj(attention(x)) with padded rows zeroed, plus `residual` if given.
 
         x is the block's normalised input [B,S,d] (fp16 or fp32). With
         `residual`, the add x + attn happens in the out_proj epilogue and the
-        fp32 sum is returned; without it, the attention output alone.
+        fp32 sum is returned; without it, the attention output alone. With
+        `norm` as well, returns (sum, norm(sum) in fp16) from one GEMM +
+        LayerNorm kernel.
         """
         batch, seq_len, d_model = x.shape
         x16 = x if x.dtype == torch.float16 else x.to(torch.float16)
@@ -128,6 +131,10 @@ class MySelfAttention(nn.Module):
             return _linear(context, self.out_proj.half_weight(), _f32_param(self.out_proj, "bias"),
                            resid=zeros, row_valid=row_valid,
                            resid_mode=RESID_ADD_MASKSUB if use_mask else RESID_ADD)
+        if norm is not None:
+            return _linear_ln(context, self.out_proj.half_weight(), _f32_param(self.out_proj, "bias"), norm,
+                              resid=residual, row_valid=row_valid,
+                              resid_mode=RESID_ADD_MASKSUB if use_mask else RESID_ADD)
         return _linear(context, self.out_proj.half_weight(), _f32_param(self.out_proj, "bias"),
                        resid=residual, row_valid=row_valid,
                        resid_mode=RESID_ADD_MASKSUB if use_mask else RESID_ADD)
@@ -154,17 +161,34 @@ class MyTransformerBlock(nn.Module):
         the next block's norm1 or the model's final_norm; when it is the final
         norm (next_norm_is_output) its output is fp32 with padded rows zeroed
         (the model's final masked_fill), otherwise fp16 for the next QKV GEMM.
+        After the last block the residual stream is only returned when the
+        unfused path ran (None otherwise: nothing reads it).
         """
         use_mask = valid_token_mask is not None and not mask_is_trivial
         row_valid = valid_token_mask.reshape(-1) if use_mask else None
-        x1 = self.attention(normed, valid_token_mask, self.causal, mask_is_trivial, residual=x)
-        n2 = _layernorm(x1, self.norm2, out_half=True)
+        # out_proj + residual + norm2, and ffn_out + residual + next norm, each
+        # as one GEMM whose epilogue also normalises (a thread-block cluster
+        # shares each row's statistics) on the shapes where that is faster.
+        fused = _linear_ln_ok(x.numel() // x.shape[-1], x.shape[-1])
+        if fused:
+            x1, n2 = self.attention(normed, valid_token_mask, self.causal, mask_is_trivial, residual=x,
+                                    norm=self.norm2)
+        else:
+            x1 = self.attention(normed, valid_token_mask, self.causal, mask_is_trivial, residual=x)
+            n2 = _layernorm(x1, self.norm2, out_half=True)
         h = _linear(n2, self.ffn_in.half_weight(), _f32_param(self.ffn_in, "bias"), act=1,
                     out_half=True)
         # x1 + ffn_out(h); padded rows of the whole sum zeroed (the block's
         # trailing masked_fill), before the next LayerNorm reads it.
+        mode = RESID_ADD_MASKALL if use_mask else RESID_ADD
+        if fused:
+            # the model's output: x2 itself is not needed, only its final norm
+            return _linear_ln(h, self.ffn_out.half_weight(), _f32_param(self.ffn_out, "bias"), next_norm,
+                              resid=x1, row_valid=row_valid, resid_mode=mode,
+                              store_x=not next_norm_is_output, normed_half=not next_norm_is_output,
+                              normed_row_valid=row_valid if next_norm_is_output else None)
         x2 = _linear(h, self.ffn_out.half_weight(), _f32_param(self.ffn_out, "bias"), resid=x1,
-                     row_valid=row_valid, resid_mode=RESID_ADD_MASKALL if use_mask else RESID_ADD)
+                     row_valid=row_valid, resid_mode=mode)
         if next_norm_is_output:
             return x2, _layernorm(x2, next_norm, out_half=False, row_valid=row_valid)
         return x2, _layernorm(x2, next_norm, out_half=True)

@@ -95,12 +95,32 @@ int dotl_layernorm(const float* x, const float* sub, const float* weight, const 
  *   resid_mode: DOTL_RESID_*; resid is fp32 [M, ldr]; row_valid [M] uint8
  *   out_dtype: DOTL_F32 or DOTL_F16, leading dimension ldo
  * Requirements: K % 8 == 0, lda % 8 == 0, ldw % 8 == 0, a/w 16-byte aligned
- * (TMA), N % 8 == 0. tile_n: 0 = auto, else 128 or 256.
+ * (TMA), N % 8 == 0. tile_n: 0 = auto, else 64, 128 or 256.
  */
 int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N,
                 int64_t ldw, const float* bias, int act, const float* resid, int64_t ldr,
                 const uint8_t* row_valid, int resid_mode, void* out, int out_dtype, int64_t ldo,
                 int tile_n, void* stream);
+
+/*
+ * dotl_linear with a residual + LayerNorm epilogue, in one kernel. Replaces the
+ * pairs linear_bias -> fused_add_layernorm / fused_layernorm of the layer
+ * (linear_gelu.cuh:598-756 then add_layernorm.cuh:663-692):
+ *   x_new  = resid_mode epilogue(a w^T + bias)   fp32; stored to out unless out == NULL
+ *   normed = LN(x_new) * ln_weight + ln_bias      over all N columns, eps as given
+ *   normed_row_valid (optional, [M] uint8): rows with 0 get normed = 0
+ * resid_mode: NONE, ADD, ADD_MASKSUB or ADD_MASKALL (as dotl_linear; row_valid
+ * for the masked ones). normed_dtype DOTL_F32 or DOTL_F16, leading dimension ldn.
+ * The row is shared by a cluster of N / tile_n CTAs, so N must be 64, 128 or
+ * 256 times a cluster size of at most 8 (tile_n 0 = auto). Other requirements
+ * as dotl_linear; ln_weight and ln_bias 16-byte aligned.
+ */
+int dotl_linear_ln(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N,
+                   int64_t ldw, const float* bias, const float* resid, int64_t ldr,
+                   const uint8_t* row_valid, int resid_mode, float* out, int64_t ldo,
+                   const float* ln_weight, const float* ln_bias, float eps, void* normed,
+                   int normed_dtype, int64_t ldn, const uint8_t* normed_row_valid, int tile_n,
+                   void* stream);
 
 /*
  * Flash attention forward, fp16 q/k/v, fp32 softmax, fp16 output.

@@ -128,3 +128,30 @@ def test_host_pipeline_matches_forward(kernels, cfg_id):
         ref = [model(x.cuda(), m.cuda()).cpu() for x, m in zip(xs, ms)]
     for o, r in zip(outs, ref):
         assert torch.equal(o, r)
+
+
+@pytest.mark.parametrize("name", GOLDEN_CASES)
+def test_layer_fused_ln_path_matches_golden(kernels, name, monkeypatch):
+    """The layer with every out_proj / ffn_out taking the GEMM + LayerNorm
+    kernel wherever it covers d_model (the shape rule normally keeps it to
+    large row counts), against the reference's golden outputs."""
+    from optimized import config, layers
+
+    z = np.load(os.path.join(GOLDEN, f"{name}.npz"))
+    B, S, d, H, F, L, causal = (int(v) for v in z["cfg"])
+    if not kernels.linear_ln_supported(d):
+        pytest.skip(f"d_model {d} is outside the fused kernel's cluster shapes")
+    monkeypatch.setattr(layers, "_linear_ln_ok", lambda rows, n: kernels.linear_ln_supported(n))
+    cfg = O.TransformerConfig(B, S, d, H, F, L, bool(causal))
+    model, _ = _model(cfg, int(z["seed"]))
+    x = torch.from_numpy(z["x"]).cuda()
+    mask = torch.from_numpy(z["mask"]).cuda()
+    old = config.CUDA_GRAPH
+    config.CUDA_GRAPH = "off"
+    try:
+        with torch.inference_mode():
+            out = model(x, mask)
+    finally:
+        config.CUDA_GRAPH = old
+    r = O.compare_outputs(torch.from_numpy(z["out"]), out.cpu(), rtol=RTOL, atol=ATOL)
+    assert r.passed, (r.failed_elements, r.max_abs_error, r.worst_index)
