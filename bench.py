@@ -419,14 +419,18 @@ def _allreduce_roofline(dist, dev, numel, world, reps=20):
             "ms_per_allreduce": ms, "allreduces_per_step": 2}
 
 
+# DRAM bytes (read + write) per launch of a layer kernel, from one ncu capture
+# each (dram__bytes_read.sum + dram__bytes_write.sum); the captures and their
+# commands are summarised in profiles/<kernel>_cfg<N>.md.
+TRAFFIC_BYTES = {
+    (2, "gemm_ffn_out_residual"): 14_721_536,
+    (3, "attention"): 107_401_984 + 24_509_184,
+    (3, "gemm_ffn_out_ln"): 214_991_104 + 42_022_912,
+}
+
+
 def _traffic_for(config_id, kernel):
-    path = os.path.join(REPO, "profiles", "traffic.json")
-    try:
-        with open(path) as f:
-            d = json.load(f)
-        return d.get(f"cfg{config_id}", {}).get(kernel)
-    except Exception:  # noqa: BLE001
-        return None
+    return TRAFFIC_BYTES.get((config_id, kernel))
 
 
 def run_ours(args, rank, world, local_rank):
@@ -496,11 +500,13 @@ def run_ours(args, rank, world, local_rank):
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         barrier()
+        torch.cuda.nvtx.range_push("timed_steps")    # the launch-list profile selects this range
         for i in range(args.steps):
             flush.zero_()
             starts[i].record(stream)
             model(x, mask)
             ends[i].record(stream)
+        torch.cuda.nvtx.range_pop()
         barrier()
     clocks = sampler.stop()
     total_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
