@@ -114,6 +114,21 @@ def shard_rows(batch, world, rank, strong):
     return rank * per, (rank + 1) * per
 
 
+def settle(step, seconds, dist, device):
+    """Runs step() until `seconds` have passed, deciding after every call
+    together with the other ranks (an all-reduce of "keep going"), so every
+    rank runs the same number of steps: a step with collectives inside (tensor
+    parallel) would otherwise pair up different collectives across ranks."""
+    t_end = time.perf_counter() + seconds
+    while True:
+        step()
+        more = torch.tensor([1 if time.perf_counter() < t_end else 0], dtype=torch.int32, device=device)
+        if dist is not None:
+            dist.all_reduce(more, op=dist.ReduceOp.MAX)
+        if not int(more.item()):
+            return
+
+
 def max_over_ranks(values, dist, device):
     """Elementwise max of a list of floats over all ranks (the slowest rank's
     time is the job's time)."""
@@ -444,8 +459,19 @@ def run_ours(args, rank, world, local_rank):
         import datetime
 
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=dev)
+        # NCCL prints a version banner on stdout when the communicator comes up
+        # (eagerly here, device_id is bound): send it to stderr, so rank 0's
+        # stdout carries only the JSON line.
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+            dist.barrier()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
     kernels = kernel_ext.get_kernels()
     if kernels is None:
         raise RuntimeError(f"libdotl failed to load: {kernel_ext.load_error()}")
@@ -493,10 +519,7 @@ def run_ours(args, rank, world, local_rank):
         for _ in range(args.warmup):
             model(x, mask)
         # about a second of untimed steps so the clocks settle before timing
-        t_end = time.perf_counter() + args.settle
-        while time.perf_counter() < t_end:
-            model(x, mask)
-            torch.cuda.synchronize(dev)
+        settle(lambda: model(x, mask), args.settle, dist, dev)
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         barrier()
@@ -524,14 +547,10 @@ def run_ours(args, rank, world, local_rank):
     with torch.inference_mode():
         # W warm-up steps, then about a second more: the first pipelined
         # copies out of freshly pinned buffers run well below steady state
-        warm = args.warmup
-        t_end = time.perf_counter() + args.settle
-        while True:
-            pipe.run([x_host] * warm, [mask_host] * warm if mask_host is not None else None,
-                     [out_hosts[i & 1] for i in range(warm)])
-            if time.perf_counter() >= t_end:
-                break
-            warm = 20
+        pipe.run([x_host] * args.warmup, [mask_host] * args.warmup if mask_host is not None else None,
+                 [out_hosts[i & 1] for i in range(args.warmup)])
+        settle(lambda: pipe.run([x_host] * 20, [mask_host] * 20 if mask_host is not None else None,
+                                [out_hosts[i & 1] for i in range(20)]), args.settle, dist, dev)
         e_start = torch.cuda.Event(enable_timing=True)
         e_end = torch.cuda.Event(enable_timing=True)
         barrier()

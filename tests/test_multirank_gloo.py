@@ -67,3 +67,43 @@ def test_shard_rows_arithmetic():
     assert bench.shard_rows(8, 4, 3, strong=False) == (0, 8)
     with pytest.raises(ValueError, match="divisible"):
         bench.shard_rows(4, 8, 0, strong=True)
+
+
+def _settle_worker(rank, world, port, result_path):
+    import sys
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path.insert(0, os.path.dirname(here))
+    import bench
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        count = [0]
+
+        def step():
+            # a step with a collective inside, as a tensor-parallel forward has
+            t = torch.ones(3)
+            dist.all_reduce(t)
+            count[0] += 1
+
+        # rank 1 would stop at once on its own clock, rank 0 only after 0.3 s
+        bench.settle(step, 0.3 if rank == 0 else 0.0, dist, torch.device("cpu"))
+        counts = torch.tensor([count[0]])
+        gathered = [torch.zeros(1, dtype=torch.int64) for _ in range(world)]
+        dist.all_gather(gathered, counts)
+        if rank == 0:
+            torch.save([int(g.item()) for g in gathered], result_path)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_settle_runs_the_same_steps_on_every_rank(tmp_path):
+    """bench.settle: ranks with different clocks still take the same number of
+    steps, so the collectives inside the steps pair up."""
+    path = str(tmp_path / "s.pt")
+    mp.start_processes(_settle_worker, args=(2, _free_port(), path), nprocs=2,
+                       start_method="spawn", join=True)
+    counts = torch.load(path)
+    assert counts[0] == counts[1] and counts[0] > 1
