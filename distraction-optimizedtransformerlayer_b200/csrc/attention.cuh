@@ -45,6 +45,9 @@
 namespace dotl {
 
 constexpr int kAttnThreads = 384;        // softmax warpgroups 0-1, producer/MMA warpgroup 2
+constexpr int kAttnRegsSoftmax = 192;    // setmaxnreg of the two softmax warpgroups
+constexpr int kAttnRegsOther = 104;      // and of the producer/MMA warpgroup
+constexpr int kAttnRegSplit = 256 * kAttnRegsSoftmax + 128 * kAttnRegsOther;
 constexpr int kAttnTile = 128;          // query rows per tile and keys per key tile
 constexpr float kRescaleLog2 = 8.0f;    // lazy-rescale threshold, in log2 units
 
@@ -245,7 +248,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     };
 
     if (warp >= 8) {
-        regs_dec<104>();
+        regs_dec<kAttnRegsOther>();
         if (warp == 8) {
             // --------------------------------------------------- producer --
             // Loads follow the MMA issuer's order: K(0..NS-1), then V(j) and
@@ -409,7 +412,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
     } else {
         // -------------------------------------------- softmax warpgroups --
-        regs_inc<192>();
+        regs_inc<kAttnRegsSoftmax>();
         const int grp = warp >> 2;                     // warpgroup 0 or 1
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;            // query row within the tile

@@ -74,6 +74,22 @@ int ensure_smem(Kernel kernel, uint32_t bytes, int dev, bool* done_flags) {
     return DOTL_OK;
 }
 
+// Kernels that move registers between warpgroups (setmaxnreg) need their
+// launch to grant at least `needed` registers in total; a raise that the
+// launch cannot cover would wait forever, so such a build refuses to launch.
+template <typename Kernel>
+int check_regs(Kernel kernel, int threads, int needed, bool* done_flags, int dev, const char* who) {
+    if (dev >= 0 && dev < kMaxDevices && done_flags[dev]) return DOTL_OK;
+    cudaFuncAttributes fa;
+    const cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
+    if (e != cudaSuccess) return fail(DOTL_ECUDA, "%s: cudaFuncGetAttributes failed: %s", who, cudaGetErrorString(e));
+    if (fa.numRegs * threads < needed)
+        return fail(DOTL_EUNSUPPORTED, "%s: kernel built with %d registers per thread, its warpgroup split needs %d in total",
+                    who, fa.numRegs, needed);
+    if (dev >= 0 && dev < kMaxDevices) done_flags[dev] = true;
+    return DOTL_OK;
+}
+
 // Launches with programmatic stream serialization, so the kernel's prologue
 // can overlap the previous kernel's tail (each kernel starts with
 // griddepcontrol.wait before it touches its inputs).
@@ -258,7 +274,9 @@ int launch_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap&
     using L = dotl::AttnSmem<HD, STAGES>;
     auto kernel = dotl::attn_tc_kernel<HD, STAGES>;
     static bool done[kMaxDevices] = {false};
+    static bool regs_ok[kMaxDevices] = {false};
     if (int rc = ensure_smem(kernel, L::kAlloc, dev, done)) return rc;
+    if (int rc = check_regs(kernel, dotl::kAttnThreads, dotl::kAttnRegSplit, regs_ok, dev, "dotl_attention")) return rc;
     const int items = p.num_streams * p.num_q_tiles;
     const int grid = items < sm_count(dev) ? items : sm_count(dev);
     const cudaError_t e = launch_pdl(kernel, dim3(grid), dim3(dotl::kAttnThreads), L::kAlloc, stream, tq, tk, tv, p);

@@ -429,6 +429,56 @@ __device__ __forceinline__ float gelu_fast(float v) {
     return fmaf(-u, __fdividef(1.0f, t), fmaxf(v, 0.0f));
 }
 
+// ---- packed fp32 pairs (sm_100 f32x2 arithmetic: two IEEE fp32 lanes per
+// instruction, each lane exactly what the scalar fmaf / fmul computes)
+__device__ __forceinline__ unsigned long long f32x2(float lo, float hi) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void f32x2_split(unsigned long long r, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+__device__ __forceinline__ unsigned long long fma_x2(unsigned long long a, unsigned long long b,
+                                                      unsigned long long c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ unsigned long long mul_x2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// gelu_fast on two values at once: the polynomial, the squarings and the
+// final FMA run as f32x2 instructions (half the issue slots of the scalar
+// form, the same per-lane arithmetic); the reciprocal and the max stay scalar.
+__device__ __forceinline__ void gelu_fast_pair(float& v0, float& v1) {
+    const float u0 = fabsf(v0), u1 = fabsf(v1);
+    const unsigned long long u = f32x2(u0, u1);
+    unsigned long long t = fma_x2(u, f32x2(5.6212997e-06f, 5.6212997e-06f), f32x2(5.1055209e-05f, 5.1055209e-05f));
+    t = fma_x2(t, u, f32x2(3.9686137e-05f, 3.9686137e-05f));
+    t = fma_x2(t, u, f32x2(3.4227392e-03f, 3.4227392e-03f));
+    t = fma_x2(t, u, f32x2(2.2076998e-02f, 2.2076998e-02f));
+    t = fma_x2(t, u, f32x2(5.2075163e-02f, 5.2075163e-02f));
+    t = fma_x2(t, u, f32x2(1.0442738f, 1.0442738f));
+    t = mul_x2(t, t);
+    t = mul_x2(t, t);
+    t = mul_x2(t, t);
+    t = mul_x2(t, t);
+    float t0, t1;
+    f32x2_split(t, t0, t1);
+    const unsigned long long r =
+        fma_x2(f32x2(-u0, -u1), f32x2(rcp_approx(t0), rcp_approx(t1)), f32x2(fmaxf(v0, 0.0f), fmaxf(v1, 0.0f)));
+    f32x2_split(r, v0, v1);
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);

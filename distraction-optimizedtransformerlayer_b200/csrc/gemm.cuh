@@ -305,7 +305,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     for (int j = 0; j < kCW; ++j) v[j] += __shfl_sync(0xffffffffu, b_cur, j);
                     if (p.act == 1) {
 #pragma unroll
-                        for (int j = 0; j < kCW; ++j) v[j] = gelu_fast(v[j]);
+                        for (int j = 0; j < kCW; j += 2) gelu_fast_pair(v[j], v[j + 1]);
                     }
                     if (p.resid_mode == kMaskRows && !valid) {
 #pragma unroll
