@@ -149,16 +149,37 @@ int encode_f16_map(CUtensorMap* map, const void* base, int rank, const cuuint64_
 
 // ------------------------------------------------------------------ GEMM --
 
-template <int BN, int STAGES, bool OUT_F16>
+template <int BN, int STAGES, bool OUT_F16, bool SPLIT2 = false>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const dotl::GemmParams& p,
                 int dev, cudaStream_t stream) {
     using L = dotl::GemmSmem<BN, STAGES>;
-    auto kernel = dotl::gemm_tc_kernel<BN, STAGES, OUT_F16>;
+    auto kernel = dotl::gemm_tc_kernel<BN, STAGES, OUT_F16, SPLIT2>;
     static bool done[kMaxDevices] = {false};
     if (int rc = ensure_smem(kernel, L::kAlloc, dev, done)) return rc;
     const int tiles = p.num_m_tiles * p.num_n_tiles;
-    const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
-    const cudaError_t e = launch_pdl(kernel, dim3(grid), dim3(dotl::kGemmThreads), L::kAlloc, stream, ta, tw, to, p);
+    cudaError_t e;
+    if constexpr (SPLIT2) {
+        // one cluster of two CTAs per tile (the exchange buffer reuses the
+        // stage ring, so no CTA may own a second tile)
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(static_cast<unsigned>(2 * tiles));
+        cfg.blockDim = dim3(dotl::kGemmThreads);
+        cfg.dynamicSmemBytes = L::kAlloc;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = 2;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 2;
+        e = cudaLaunchKernelEx(&cfg, kernel, ta, tw, to, p);
+    } else {
+        const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
+        e = launch_pdl(kernel, dim3(grid), dim3(dotl::kGemmThreads), L::kAlloc, stream, ta, tw, to, p);
+    }
     if (e != cudaSuccess) return fail(DOTL_ECUDA, "dotl_linear: launch failed: %s", cudaGetErrorString(e));
     return check_launch("dotl_linear");
 }
@@ -430,9 +451,27 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
 
     int dev;
     if (int rc = current_device(&dev)) return rc;
+    const int64_t nkb = (K + dotl::kGemmBK - 1) / dotl::kGemmBK;
+    const int64_t mt = (M + dotl::kGemmBM - 1) / dotl::kGemmBM;
     int bn = tile_n;
-    if (bn == 0) bn = pick_tile_n(M, N, K, sm_count(dev));
-    if (bn != 64 && bn != 128 && bn != 256) return fail(DOTL_EINVAL, "%s: tile_n must be 0, 64, 128 or 256", who);
+    bool split2 = false;
+    if (bn == 0) {
+        bn = pick_tile_n(M, N, K, sm_count(dev));
+        // Too few tiles for the SMs even at width 64, and a long K: split K
+        // between the two CTAs of a cluster at width 128 instead (each CTA
+        // streams half the k-blocks of a tile twice as wide).
+        // (below ~24 k-blocks the pair's exchange costs more than it saves)
+        if (bn == 64 && nkb >= 24 && 2 * mt * ((N + 127) / 128) <= sm_count(dev)) {
+            bn = 128;
+            split2 = true;
+        }
+    } else if (bn == -128) {
+        if (nkb < 2) return fail(DOTL_EINVAL, "%s: split-K needs at least two k-blocks (K > 64)", who);
+        bn = 128;
+        split2 = true;
+    }
+    if (bn != 64 && bn != 128 && bn != 256)
+        return fail(DOTL_EINVAL, "%s: tile_n must be 0, 64, 128, 256 or -128 (split K)", who);
 
     CUtensorMap ta, tw;
     const cuuint64_t adims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
@@ -459,6 +498,9 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
     p.out = out;
     p.ldo = ldo;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (split2)
+        return out_dtype == DOTL_F16 ? launch_gemm<128, 5, true, true>(ta, tw, to, p, dev, s)
+                                     : launch_gemm<128, 5, false, true>(ta, tw, to, p, dev, s);
     if (bn == 256)
         return out_dtype == DOTL_F16 ? launch_gemm<256, 4, true>(ta, tw, to, p, dev, s)
                                      : launch_gemm<256, 4, false>(ta, tw, to, p, dev, s);

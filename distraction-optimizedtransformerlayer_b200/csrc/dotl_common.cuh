@@ -133,6 +133,11 @@ __device__ __forceinline__ void st_cluster_v2f32(uint32_t caddr, float a, float 
     asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(caddr), "f"(a), "f"(b) : "memory");
 }
 
+__device__ __forceinline__ void st_cluster_v4f32(uint32_t caddr, float a, float b, float c, float d) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(caddr), "f"(a), "f"(b), "f"(c), "f"(d)
+                 : "memory");
+}
+
 // Arrives on an mbarrier of a peer CTA (shared::cluster address), ordering this
 // thread's earlier stores (remote ones included) before the arrival.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {

@@ -63,8 +63,9 @@ struct GemmSmem {
     static constexpr uint32_t kOffStage = kOffB + STAGES * kBTileBytes;
     static constexpr uint32_t kStageBufBytes = 32 * 128;
     static constexpr uint32_t kOffBar = kOffStage + 8 * kStageBufBytes;
-    // full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], drain (GemmBars)
-    static constexpr uint32_t kNumBars = 2 * STAGES + 5;
+    // full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], drain (GemmBars),
+    // then the split-K pair's peer_ready, recv_full and exit
+    static constexpr uint32_t kNumBars = 2 * STAGES + 8;
     static constexpr uint32_t kOffSlot = kOffBar + kNumBars * 8;
     static constexpr uint32_t kOffAbort = kOffSlot + 4;
     static constexpr uint32_t kBytes = kOffAbort + 4;
@@ -102,12 +103,12 @@ struct GemmBars {
     static constexpr int kCount = 2 * STAGES + 5;
 };
 
-// TMA producer (one thread): A and W k-blocks of every scheduled tile into
-// the STAGES-deep ring. On abort, waits out the copies still in flight.
+// TMA producer (one thread): A and W k-blocks [kb0, kb1) of every scheduled
+// tile into the STAGES-deep ring. On abort, waits out the copies in flight.
 template <int BN, int STAGES>
 __device__ __forceinline__ void gemm_produce(const CUtensorMap* tmap_a, const CUtensorMap* tmap_w, uint32_t sbase,
                                              GemmBars<STAGES> bars, volatile int* abort_flag, const TileSched& ts,
-                                             int num_kb) {
+                                             int kb0, int kb1) {
     using L = GemmSmem<BN, STAGES>;
     int stage = 0;
     uint32_t phase = 0;
@@ -116,7 +117,7 @@ __device__ __forceinline__ void gemm_produce(const CUtensorMap* tmap_a, const CU
     for (int t = ts.first; t < ts.count; t += ts.stride) {
         int m_blk, n_blk;
         ts.decode(t, m_blk, n_blk);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
             if (!mbar_wait(bars.empty(stage), phase ^ 1u, abort_flag)) goto producer_done;
             mbar_arrive_expect_tx(bars.full(stage), L::kStageBytes);
             tma_load_2d(sbase + L::kOffA + stage * kGemmATileBytes, tmap_a, bars.full(stage), kb * kGemmBK,
@@ -138,11 +139,12 @@ producer_done:
     }
 }
 
-// MMA issuer (one thread): each scheduled tile into TMEM accumulator
-// 0, 1, 0, ... (BN columns each); every issued MMA has completed on return.
+// MMA issuer (one thread): k-blocks [kb0, kb1) of each scheduled tile into
+// TMEM accumulator 0, 1, 0, ... (BN columns each); every issued MMA has
+// completed on return.
 template <int BN, int STAGES>
 __device__ __forceinline__ void gemm_mma(uint32_t sbase, uint32_t tmem_base, GemmBars<STAGES> bars,
-                                         volatile int* abort_flag, const TileSched& ts, int num_kb) {
+                                         volatile int* abort_flag, const TileSched& ts, int kb0, int kb1) {
     using L = GemmSmem<BN, STAGES>;
     constexpr uint32_t idesc = idesc_f16_f32(kGemmBM, BN, false, false);
     int stage = 0;
@@ -154,7 +156,7 @@ __device__ __forceinline__ void gemm_mma(uint32_t sbase, uint32_t tmem_base, Gem
         tc_fence_after();
         {
             const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-            for (int kb = 0; kb < num_kb; ++kb) {
+            for (int kb = kb0; kb < kb1; ++kb) {
                 if (!mbar_wait(bars.full(stage), phase, abort_flag)) goto mma_done;
                 tc_fence_after();
                 const uint32_t a_addr = sbase + L::kOffA + stage * kGemmATileBytes;
@@ -163,7 +165,7 @@ __device__ __forceinline__ void gemm_mma(uint32_t sbase, uint32_t tmem_base, Gem
                 for (int kk = 0; kk < kGemmBK / 16; ++kk) {
                     const uint64_t ad = smem_desc(a_addr + kk * 32, 16, 1024, kSwizzle128);
                     const uint64_t bd = smem_desc(b_addr + kk * 32, 16, 1024, kSwizzle128);
-                    mma_f16_ss(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+                    mma_f16_ss(d_tmem, ad, bd, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
                 }
                 tc_commit(bars.empty(stage));
                 if (++stage == STAGES) {
@@ -184,7 +186,14 @@ mma_done:
     mbar_wait_drain(bars.drain(), 0);
 }
 
-template <int BN, int STAGES, bool OUT_F16>
+// SPLIT2: a cluster of two CTAs shares each output tile, CTA r running
+// k-blocks [r nkb/2, (r+1) nkb/2). After the main loop each sends the other's
+// column half of its partial accumulator into the other's shared memory (the
+// stage ring, idle by then: every CTA has exactly one tile) and finishes its
+// own half as partial_0 + partial_1 (one fp32 add, which commutes: both CTAs
+// and every run give the same bits). Used when a problem has too few tiles
+// to fill the SMs with long K.
+template <int BN, int STAGES, bool OUT_F16, bool SPLIT2 = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
                    const __grid_constant__ CUtensorMap tmap_out, const GemmParams p) {
@@ -195,11 +204,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bar0 = sbase + L::kOffBar;
     const GemmBars<STAGES> bars{bar0};
+    const uint32_t peer_ready = bar0 + 8u * (GemmBars<STAGES>::kCount);
+    const uint32_t recv_full = bar0 + 8u * (GemmBars<STAGES>::kCount + 1);
+    const uint32_t exit_bar = bar0 + 8u * (GemmBars<STAGES>::kCount + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffAbort);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffSlot);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const uint32_t rank = SPLIT2 ? cluster_ctarank() : 0u;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -211,12 +224,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             mbar_init(bars.acce(b), 256);
         }
         mbar_init(bars.drain(), 1);
+        mbar_init(peer_ready, 256);
+        mbar_init(recv_full, 256);
+        mbar_init(exit_bar, 2);
         *abort_flag = 0;
         fence_barrier_init();
         tma_prefetch_map(&tmap_a);
         tma_prefetch_map(&tmap_w);
         tma_prefetch_map(&tmap_out);
     }
+    if constexpr (SPLIT2) cluster_sync_after_init();
     pdl_wait();
     pdl_launch_dependents();
     if (warp == 1) {
@@ -231,11 +248,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int num_tiles = p.num_m_tiles * p.num_n_tiles;
     const int num_kb = (p.K + kGemmBK - 1) / kGemmBK;
 
-    const TileSched ts{static_cast<int>(blockIdx.x), static_cast<int>(gridDim.x), num_tiles, p.num_n_tiles, -1};
+    const int cta_unit = SPLIT2 ? static_cast<int>(blockIdx.x) / 2 : static_cast<int>(blockIdx.x);
+    const int units = SPLIT2 ? static_cast<int>(gridDim.x) / 2 : static_cast<int>(gridDim.x);
+    const TileSched ts{cta_unit, units, num_tiles, p.num_n_tiles, -1};
+    const int kb0 = SPLIT2 ? static_cast<int>(rank) * (num_kb / 2) : 0;
+    const int kb1 = SPLIT2 ? (rank == 0 ? num_kb / 2 : num_kb) : num_kb;
     if (warp == 0 && lane == 0) {
-        gemm_produce<BN, STAGES>(&tmap_a, &tmap_w, sbase, bars, abort_flag, ts, num_kb);
+        gemm_produce<BN, STAGES>(&tmap_a, &tmap_w, sbase, bars, abort_flag, ts, kb0, kb1);
     } else if (warp == 1 && lane == 0) {
-        gemm_mma<BN, STAGES>(sbase, tmem_base, bars, abort_flag, ts, num_kb);
+        gemm_mma<BN, STAGES>(sbase, tmem_base, bars, abort_flag, ts, kb0, kb1);
     } else if (warp >= 2) {
         // -------------------------------------------------------- epilogue --
         // Eight warps, two per TMEM lane quarter (the 32 rows a warp may
@@ -255,9 +276,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         uint32_t nstore = 0;                              // chunks this warp has staged
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-            const int m_blk = tile / p.num_n_tiles;
-            const int n_blk = tile - m_blk * p.num_n_tiles;
+        for (int t = ts.first; t < ts.count; t += ts.stride) {
+            int m_blk, n_blk;
+            ts.decode(t, m_blk, n_blk);
             const int row = m_blk * kGemmBM + row_in_tile;
             const int n0 = n_blk * BN;
             const bool row_ok = row < p.M;
@@ -278,19 +299,54 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     for (int j = 0; j < kCW / 4; ++j) rr[j] = rp[j];
                 }
             };
-            float b_cur = load_bias(n0 + half * kCW);
-            load_resid(n0 + half * kCW);
+            // Columns this CTA finishes: all BN, or its half of a split-K pair.
+            const int c_lo = SPLIT2 ? static_cast<int>(rank) * (BN / 2) : 0;
+            const int c_hi = SPLIT2 ? c_lo + BN / 2 : BN;
+            const int c_first = c_lo + half * kCW;
+            float b_cur = load_bias(n0 + c_first);
+            load_resid(n0 + c_first);
             bool ok = mbar_wait(bars.accf(acc), acc_phase, abort_flag);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             tc_fence_after();
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN);
+            // Split-K exchange buffer: [128 rows][BN/2 fp32] in the stage ring,
+            // 16-byte granule g of row r at g ^ (r & mask) (conflict-free).
+            constexpr int kHalfGranules = BN / 8;
+            const uint32_t recv_row = static_cast<uint32_t>(row_in_tile) * (BN / 2) * 4;
+            auto recv_pos = [&](int col) -> uint32_t {
+                return recv_row + static_cast<uint32_t>(((col >> 2) ^ (row_in_tile & (kHalfGranules - 1))) << 4);
+            };
+            if constexpr (SPLIT2) {
+                // This CTA's only tile is accumulated, so its ring is idle: the
+                // partner may write there. Send the partner's half, receive ours.
+                const uint32_t partner = rank ^ 1u;
+                mbar_arrive_cluster(mapa_shared(peer_ready, partner));
+                bool ok2 = mbar_wait_cluster(peer_ready, 0, abort_flag);
+                if (!__all_sync(0xffffffffu, ok2)) break;
+                const int p_lo = static_cast<int>(partner) * (BN / 2);
+                const uint32_t recv_remote = mapa_shared(sbase + L::kOffA, partner);
 #pragma unroll 1
-            for (int c = half * kCW; c < BN; c += 2 * kCW) {
+                for (int c = p_lo + half * kCW; c < p_lo + BN / 2; c += 2 * kCW) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(t_row + c, r);
+                    tmem_ld_wait(r);
+#pragma unroll
+                    for (int q = 0; q < kCW / 4; ++q)
+                        st_cluster_v4f32(recv_remote + recv_pos(c - p_lo + 4 * q), __uint_as_float(r[4 * q]),
+                                         __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
+                                         __uint_as_float(r[4 * q + 3]));
+                }
+                mbar_arrive_cluster(mapa_shared(recv_full, partner));
+                ok2 = mbar_wait_cluster(recv_full, 0, abort_flag);
+                if (!__all_sync(0xffffffffu, ok2)) break;
+            }
+#pragma unroll 1
+            for (int c = c_first; c < c_hi; c += 2 * kCW) {
                 const int nc = n0 + c;
-                if (c != half * kCW) load_resid(nc);
-                const float b_next = c + 2 * kCW < BN ? load_bias(nc + 2 * kCW) : 0.0f;
+                if (c != c_first) load_resid(nc);
+                const float b_next = c + 2 * kCW < c_hi ? load_bias(nc + 2 * kCW) : 0.0f;
                 float v[kCW];
                 {
                     uint32_t r[32];
@@ -298,6 +354,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     tmem_ld_wait(r);
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+                }
+                if constexpr (SPLIT2) {
+                    // partial_0 + partial_1 (a single add: the same bits in either order)
+#pragma unroll
+                    for (int q = 0; q < kCW / 4; ++q) {
+                        const float4 f = *reinterpret_cast<const float4*>(smem + L::kOffA + recv_pos(c - c_lo + 4 * q));
+                        v[4 * q] += f.x;
+                        v[4 * q + 1] += f.y;
+                        v[4 * q + 2] += f.z;
+                        v[4 * q + 3] += f.w;
+                    }
                 }
                 if (nc < p.N) {
                     const bool full = nc + kCW <= p.N;
@@ -381,6 +448,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncwarp();
     tc_fence_before();
     __syncthreads();
+    if constexpr (SPLIT2) {
+        // neither CTA of the pair exits while the other may still write into it
+        if (threadIdx.x == 0) {
+            mbar_arrive_cluster(mapa_shared(exit_bar, 0));
+            mbar_arrive_cluster(mapa_shared(exit_bar, 1));
+            mbar_wait_cluster(exit_bar, 0, nullptr, 4 * kWaitLimitNs);
+        }
+        __syncthreads();
+    }
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, L::kTmemCols);

@@ -144,9 +144,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const TileSched ts{cluster_id, num_clusters, p.num_m_tiles, 1, static_cast<int>(rank)};
 
     if (warp == 0 && lane == 0) {
-        gemm_produce<BN, STAGES>(&tmap_a, &tmap_w, sbase, bars, abort_flag, ts, num_kb);
+        gemm_produce<BN, STAGES>(&tmap_a, &tmap_w, sbase, bars, abort_flag, ts, 0, num_kb);
     } else if (warp == 1 && lane == 0) {
-        gemm_mma<BN, STAGES>(sbase, tmem_base, bars, abort_flag, ts, num_kb);
+        gemm_mma<BN, STAGES>(sbase, tmem_base, bars, abort_flag, ts, 0, num_kb);
     } else if (warp >= 2) {
         // -------------------------------------------------------- epilogue --
         // Thread = one row of the tile (lane quarter of its warp) and the

@@ -95,7 +95,10 @@ int dotl_layernorm(const float* x, const float* sub, const float* weight, const 
  *   resid_mode: DOTL_RESID_*; resid is fp32 [M, ldr]; row_valid [M] uint8
  *   out_dtype: DOTL_F32 or DOTL_F16, leading dimension ldo
  * Requirements: K % 8 == 0, lda % 8 == 0, ldw % 8 == 0, a/w 16-byte aligned
- * (TMA), N % 8 == 0. tile_n: 0 = auto, else 64, 128 or 256.
+ * (TMA), N % 8 == 0. tile_n: 0 = auto, else 64, 128 or 256, or -128 for two
+ * CTAs per 128-wide tile that split K and add their partial sums (auto picks it
+ * for long K when the tiles cannot fill the SMs; the add is one fp32 sum, so
+ * results are the same on every run).
  */
 int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N,
                 int64_t ldw, const float* bias, int act, const float* resid, int64_t ldr,

@@ -125,3 +125,34 @@ def test_gelu_epilogue_matches_exact_erf(kernels):
     ref = F.gelu(v.double(), approximate="none")
     err = (out - ref).abs()
     assert (err <= 1e-6 * (1.0 + v.double().abs())).all(), err.max().item()
+
+
+@pytest.mark.parametrize("M,N,K", [(2048, 512, 2048), (300, 392, 576), (128, 128, 128), (1000, 256, 1088)])
+@pytest.mark.parametrize("mode", [0, 1, 3])
+def test_split_k_pair(kernels, M, N, K, mode):
+    """tile_n=-128: two CTAs of a cluster split K and add their partial sums
+    (ragged M and N tiles, odd k-block counts, every epilogue kind)."""
+    a, w, b = _operands(M, N, K, M + K + mode)
+    g = torch.Generator(device="cuda").manual_seed(6)
+    resid = torch.randn(M, N, device="cuda", generator=g)
+    valid = torch.rand(M, device="cuda", generator=g) > 0.25
+    if mode == 0:
+        out = kernels.linear_fp16(a, w, b, act=1, out_half=True, tile_n=-128)
+        ref = _ref(a, w, b, act=True)
+        err = (out.double() - ref).abs() / (ref.abs() + 1e-2)
+        assert err.max().item() < 2 ** -10
+    else:
+        out = kernels.linear_fp16(a, w, b, resid=resid, row_valid=valid, resid_mode=mode, tile_n=-128)
+        proj = _ref(a, w, b)
+        ref = resid.double() + proj if mode == 1 else (resid.double() + proj).masked_fill(~valid[:, None], 0)
+        err = ((out.double() - ref).abs() / (_scale(a, w) + resid.double().abs())).max().item()
+        assert err < 1e-5, err
+        again = kernels.linear_fp16(a, w, b, resid=resid, row_valid=valid, resid_mode=mode, tile_n=-128)
+        assert torch.equal(out, again), "the pair's sum must not depend on timing"
+
+
+def test_split_k_is_auto_for_long_k_few_tiles(kernels):
+    """The shape rule takes the split pair for the config-2 ffn_out GEMM
+    (128 tiles of width 64 and 32 k-blocks): auto and forced give the same bits."""
+    a, w, b = _operands(2048, 512, 2048, 77)
+    assert torch.equal(kernels.linear_fp16(a, w, b), kernels.linear_fp16(a, w, b, tile_n=-128))
