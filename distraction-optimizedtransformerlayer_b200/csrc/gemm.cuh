@@ -397,41 +397,45 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         }
                     }
                 }
-                // fp16 chunks alternate between the two halves of the buffer:
-                // wait until the store that last read this half is done
-                const uint32_t sb = OUT_F16 ? (nstore & 1u) * 2048u : 0u;
-                if (lane == 0) {
-                    if constexpr (OUT_F16) bulk_wait_read<1>();
-                    else bulk_wait_read<0>();
-                }
-                __syncwarp();
-                uint8_t* srow = stage_ptr + sb + lane * kRowB;
-                if constexpr (OUT_F16) {
-                    // 64 B rows, 64B swizzle: granule q of row r at q ^ ((r >> 1) & 3)
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        uint4 w;
-                        w.x = pack_half2(v[8 * q], v[8 * q + 1]);
-                        w.y = pack_half2(v[8 * q + 2], v[8 * q + 3]);
-                        w.z = pack_half2(v[8 * q + 4], v[8 * q + 5]);
-                        w.w = pack_half2(v[8 * q + 6], v[8 * q + 7]);
-                        *reinterpret_cast<uint4*>(srow + ((q ^ ((lane >> 1) & 3)) << 4)) = w;
+                // Chunks past N (the unused columns of a partial tile) stage and
+                // store nothing. fp16 chunks alternate between the two halves of
+                // the buffer, so before writing a half wait until the store that
+                // last read it is done: it is at most the one before the newest.
+                if (nc < p.N) {
+                    const uint32_t sb = OUT_F16 ? (nstore & 1u) * 2048u : 0u;
+                    if (lane == 0) {
+                        if constexpr (OUT_F16) bulk_wait_read<1>();
+                        else bulk_wait_read<0>();
                     }
-                } else {
-                    // 128 B rows, 128B swizzle: granule q of row r at q ^ (r & 7)
+                    __syncwarp();
+                    uint8_t* srow = stage_ptr + sb + lane * kRowB;
+                    if constexpr (OUT_F16) {
+                        // 64 B rows, 64B swizzle: granule q of row r at q ^ ((r >> 1) & 3)
 #pragma unroll
-                    for (int q = 0; q < 8; ++q)
-                        *reinterpret_cast<uint4*>(srow + ((q ^ (lane & 7)) << 4)) =
-                            make_uint4(__float_as_uint(v[4 * q]), __float_as_uint(v[4 * q + 1]),
-                                       __float_as_uint(v[4 * q + 2]), __float_as_uint(v[4 * q + 3]));
+                        for (int q = 0; q < 4; ++q) {
+                            uint4 w;
+                            w.x = pack_half2(v[8 * q], v[8 * q + 1]);
+                            w.y = pack_half2(v[8 * q + 2], v[8 * q + 3]);
+                            w.z = pack_half2(v[8 * q + 4], v[8 * q + 5]);
+                            w.w = pack_half2(v[8 * q + 6], v[8 * q + 7]);
+                            *reinterpret_cast<uint4*>(srow + ((q ^ ((lane >> 1) & 3)) << 4)) = w;
+                        }
+                    } else {
+                        // 128 B rows, 128B swizzle: granule q of row r at q ^ (r & 7)
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            *reinterpret_cast<uint4*>(srow + ((q ^ (lane & 7)) << 4)) =
+                                make_uint4(__float_as_uint(v[4 * q]), __float_as_uint(v[4 * q + 1]),
+                                           __float_as_uint(v[4 * q + 2]), __float_as_uint(v[4 * q + 3]));
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tmap_out, stage_addr + sb, nc, m_blk * kGemmBM + quarter * 32);
+                        bulk_commit();
+                    }
+                    ++nstore;
                 }
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0 && nc < p.N) {
-                    tma_store_2d(&tmap_out, stage_addr + sb, nc, m_blk * kGemmBM + quarter * 32);
-                    bulk_commit();
-                }
-                ++nstore;
                 b_cur = b_next;
             }
             tc_fence_before();

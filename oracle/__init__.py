@@ -21,6 +21,7 @@ from .layer import (  # noqa: F401
     attention_reference,
     baseline_forward,
     compare_outputs,
+    fp16_operand_forward,
     generate_random_case,
     init_params,
     param_checksum,

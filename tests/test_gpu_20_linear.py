@@ -75,6 +75,19 @@ def test_linear_residual_modes(kernels, mode):
         assert torch.all(out[~valid] == 0)
 
 
+@pytest.mark.parametrize("N", [384, 320, 448])
+def test_partial_last_tile_f16_many_tiles(kernels, N):
+    """fp16 output, width-256 tiles whose last N tile is partial, ~34 tiles per
+    CTA (the dashboard's B=10000 QKV shape): the chunks past N stage nothing, so
+    the double-buffered staging never overwrites a half a store still reads."""
+    M, K = 320000, 128
+    a, w, b = _operands(M, N, K, N)
+    out = kernels.linear_fp16(a, w, b, out_half=True, tile_n=256)
+    ref = _ref(a, w, b)
+    err = (out.double() - ref).abs() / (ref.abs() + _scale(a, w) * 1e-3)
+    assert err.max().item() < 2 ** -10, err.max().item()
+
+
 def test_reference_named_entry_points(kernels):
     """linear_bias / linear_gelu take fp32 x and fp32 nn.Linear weights, as upstream."""
     g = torch.Generator(device="cuda").manual_seed(9)
