@@ -434,6 +434,45 @@ def _allreduce_roofline(dist, dev, numel, world, reps=20):
             "ms_per_allreduce": ms, "allreduces_per_step": 2}
 
 
+def _fused_allreduce_roofline(model, dist, dev, T, d, world, reps=20):
+    """One dotl_allreduce_ln launch (the layer's out_proj reduction + add +
+    LayerNorm) timed alone on the group's own buffers. NVLink bytes each GPU
+    sends per launch: one-shot, every peer reads its whole fp32 partial sum,
+    (P-1) T d 4; push, peers read 1/P of it from each rank and each rank
+    stores its 1/P of x_new (fp32) and normed (fp16) into every peer,
+    (P-1)/P T d (4 + 6). Against the measured 770 GB/s per direction of a peer
+    copy on this pool."""
+    pg = model.peer
+    w = model.w
+    x = pg.view("xa", T)
+
+    def once():
+        pg.allreduce_ln(x, w["layers.0.bo_full"], w["layers.0.norm2.weight"], w["layers.0.norm2.bias"],
+                        model.eps, "xb", "n16", T)
+
+    for _ in range(3):
+        once()
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(reps):
+        once()
+    ev1.record()
+    torch.cuda.synchronize(dev)
+    ms = max_over_ranks([ev0.elapsed_time(ev1) / reps], dist, dev)[0]
+    if pg.push:
+        nbytes = (world - 1) / world * T * d * 10
+    else:
+        nbytes = (world - 1) * T * d * 4
+    achieved = nbytes / (ms / 1e3) / 1e9
+    return {"kernel": "allreduce_ln_" + ("push" if pg.push else "oneshot"), "bound": "nvlink",
+            "achieved": achieved, "peak": 770.0, "unit": "GB/s", "frac": achieved / 770.0,
+            "peak_source": "measured peer copy of this pool, per direction per GPU", "traffic": None,
+            "nvlink_bytes_per_gpu": nbytes, "ms_per_launch": ms, "launches_per_step": 2}
+
+
 # DRAM bytes (read + write) per launch of a layer kernel, from one ncu capture
 # each (dram__bytes_read.sum + dram__bytes_write.sum); the captures and their
 # commands are summarised in profiles/<kernel>_cfg<N>.md.
@@ -489,7 +528,8 @@ def run_ours(args, rank, world, local_rank):
         from optimized.tensor_parallel import TensorParallelTransformer
 
         state = {k: v.detach() for k, v in model.state_dict().items()}
-        model = TensorParallelTransformer(cfg, state, device=dev)
+        model = TensorParallelTransformer(cfg, state, device=dev, fused=args.tp_impl == "fused",
+                                          push=not args.tp_oneshot)
         args.strong = True
     else:
         model = model.to(dev).eval()
@@ -518,6 +558,11 @@ def run_ours(args, rank, world, local_rank):
     with torch.inference_mode():
         for _ in range(args.warmup):
             model(x, mask)
+        # a wait that ran out (e.g. a peer that never arrived) would make every
+        # later step wait out its limit too: stop here instead
+        word = kernels.device_error(clear=False)
+        if word:
+            raise RuntimeError(f"device error word {word:#x} after the warm-up steps")
         # about a second of untimed steps so the clocks settle before timing
         settle(lambda: model(x, mask), args.settle, dist, dev)
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -565,7 +610,9 @@ def run_ours(args, rank, world, local_rank):
 
     breakdown = None
     allreduce = None
-    if args.tp:
+    if args.tp and model.fused:
+        allreduce = _fused_allreduce_roofline(model, dist, dev, x.numel() // cfg.d_model, cfg.d_model, world)
+    elif args.tp:
         allreduce = _allreduce_roofline(dist, dev, x.numel(), world)
     elif rank == 0:
         with torch.inference_mode():
@@ -583,7 +630,9 @@ def run_ours(args, rank, world, local_rank):
             "config": {"workload": _describe(args.config), "global_batch": cfg.batch_size,
                        "seq_len": cfg.seq_len, "layers": cfg.num_layers, "parallelism": f"tp{world}",
                        "l2": "flushed between steps (256 MiB write)", "cuda_graph": False,
-                       "arithmetic": "fp16 tensor-core operands, fp32 accumulate, fp32 partial sums all-reduced"},
+                       "arithmetic": "fp16 tensor-core operands, fp32 accumulate, fp32 partial sums all-reduced",
+                       "allreduce": ("dotl_allreduce_ln over peer memory, " + ("push" if model.peer.push else "one-shot"))
+                       if model.fused else "NCCL all_reduce + LayerNorm kernel"},
             "clocks": clocks,
             "e2e": {"value": job_tokens * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
@@ -632,6 +681,8 @@ def run_ours(args, rank, world, local_rank):
     if dist is not None:
         if hasattr(model, "release_graphs"):
             model.release_graphs()
+        if hasattr(model, "close"):
+            model.close()   # collective: unmaps and frees the peer buffers
         dist.barrier()
         dist.destroy_process_group()
     return 0
@@ -676,6 +727,10 @@ def main() -> int:
     ap.add_argument("--tp", action="store_true",
                     help="tensor parallel across all ranks (heads and FFN columns sharded, two NCCL "
                          "all-reduces per layer); one global batch per step")
+    ap.add_argument("--tp-impl", choices=("fused", "nccl"), default="fused",
+                    help="--tp: each all-reduce + add + LayerNorm as one peer-memory kernel, or NCCL + LN")
+    ap.add_argument("--tp-oneshot", action="store_true",
+                    help="--tp fused: one-shot mode (every rank reduces every row)")
     ap.add_argument("--strong", action="store_true",
                     help="split the config's batch across ranks (strong scaling) instead of a full batch per rank")
     ap.add_argument("--no-cpu-baseline", action="store_true")

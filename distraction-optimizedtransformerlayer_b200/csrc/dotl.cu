@@ -5,16 +5,19 @@
 // kernel. Argument checks mirror the reference's TORCH_CHECKs
 // (attention_dispatch.cuh:351-369, linear_gelu.cuh:606-625,
 // add_layernorm.cuh:500-552): a rejected call returns a code and a message
-// and enqueues nothing. Nothing here allocates device memory.
+// and enqueues nothing. Nothing on the forward path allocates device memory;
+// only the peer-memory setup calls (dotl_peer_alloc, dotl_ipc_open) do.
 
 #include "../../include/dotl.h"
 #include "attention.cuh"
 #include "gemm.cuh"
 #include "gemm_ln.cuh"
 #include "layernorm.cuh"
+#include "peer_ln.cuh"
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 #include <string>
 #include <algorithm>
@@ -692,6 +695,142 @@ int dotl_attention(const void* q, const void* k, const void* v, int B, int H, in
         case 64: return launch_attn<64, 3>(maps[0], maps[1], maps[2], p, dev, s);
         default: return launch_attn<128, 2>(maps[0], maps[1], maps[2], p, dev, s);
     }
+}
+
+// ------------------------------------------------------------ peer memory --
+
+int dotl_peer_alloc(int64_t bytes, void** ptr) {
+    if (ptr == nullptr || bytes <= 0) return fail(DOTL_EINVAL, "dotl_peer_alloc: bad arguments");
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, static_cast<size_t>(bytes));
+    if (e != cudaSuccess) return fail(DOTL_ECUDA, "dotl_peer_alloc(%lld bytes): %s", (long long)bytes, cudaGetErrorString(e));
+    e = cudaMemset(p, 0, static_cast<size_t>(bytes));
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return fail(DOTL_ECUDA, "dotl_peer_alloc: zeroing failed: %s", cudaGetErrorString(e));
+    }
+    *ptr = p;
+    return DOTL_OK;
+}
+
+int dotl_peer_free(void* ptr) {
+    if (ptr == nullptr) return DOTL_OK;
+    const cudaError_t e = cudaFree(ptr);
+    if (e != cudaSuccess) return fail(DOTL_ECUDA, "dotl_peer_free: %s", cudaGetErrorString(e));
+    return DOTL_OK;
+}
+
+int dotl_ipc_handle(const void* ptr, void* handle) {
+    if (ptr == nullptr || handle == nullptr) return fail(DOTL_EINVAL, "dotl_ipc_handle: NULL pointer");
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+    if (e != cudaSuccess) return fail(DOTL_ECUDA, "dotl_ipc_handle: %s", cudaGetErrorString(e));
+    static_assert(sizeof(h) == DOTL_IPC_HANDLE_BYTES, "IPC handle size");
+    memcpy(handle, &h, sizeof(h));
+    return DOTL_OK;
+}
+
+int dotl_ipc_open(const void* handle, void** ptr) {
+    if (ptr == nullptr || handle == nullptr) return fail(DOTL_EINVAL, "dotl_ipc_open: NULL pointer");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    void* p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return fail(DOTL_ECUDA, "dotl_ipc_open: %s", cudaGetErrorString(e));
+    *ptr = p;
+    return DOTL_OK;
+}
+
+int dotl_ipc_close(void* ptr) {
+    if (ptr == nullptr) return DOTL_OK;
+    const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    if (e != cudaSuccess) return fail(DOTL_ECUDA, "dotl_ipc_close: %s", cudaGetErrorString(e));
+    return DOTL_OK;
+}
+
+int dotl_peer_blocks(int* blocks) {
+    if (blocks == nullptr) return fail(DOTL_EINVAL, "dotl_peer_blocks: out is NULL");
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    *blocks = sm_count(dev) * dotl::kPeerBlocksPerSm;
+    return DOTL_OK;
+}
+
+int dotl_peer_signal_bytes(int blocks, int64_t* bytes) {
+    if (bytes == nullptr || blocks <= 0) return fail(DOTL_EINVAL, "dotl_peer_signal_bytes: bad arguments");
+    *bytes = dotl::peer_signal_words(blocks) * 4;
+    return DOTL_OK;
+}
+
+int dotl_allreduce_ln(int world, int rank, const float* const* parts, void* const* signals, float* const* x_new,
+                      void* const* normed, int normed_dtype, int push, const float* x, const float* bias,
+                      const uint8_t* sum_row_valid, const float* ln_weight, const float* ln_bias, float eps,
+                      const uint8_t* normed_row_valid, int64_t rows, int64_t D, int blocks, int timeout_ms,
+                      void* stream) {
+    const char* who = "dotl_allreduce_ln";
+    if (world < 1 || world > dotl::kPeerMax || rank < 0 || rank >= world)
+        return fail(DOTL_EINVAL, "%s: world %d / rank %d outside 1..%d", who, world, rank, dotl::kPeerMax);
+    if (rows < 0 || D <= 0 || D % 4 != 0 || D > 2048)
+        return fail(DOTL_EINVAL, "%s: rows=%lld, D=%lld (D must be a multiple of 4 up to 2048)", who, (long long)rows,
+                    (long long)D);
+    if (normed_dtype != DOTL_F32 && normed_dtype != DOTL_F16)
+        return fail(DOTL_EINVAL, "%s: normed dtype must be DOTL_F32 or DOTL_F16", who);
+    if (timeout_ms < 1 || timeout_ms > 60000) return fail(DOTL_EINVAL, "%s: timeout_ms must be in 1..60000", who);
+    if (parts == nullptr || signals == nullptr || normed == nullptr || x == nullptr || ln_weight == nullptr ||
+        ln_bias == nullptr)
+        return fail(DOTL_EINVAL, "%s: NULL pointer", who);
+    dotl::PeerLnParams p = {};
+    const int d0 = push ? 0 : rank, d1 = push ? world : rank + 1;
+    for (int i = 0; i < world; ++i) {
+        if (parts[i] == nullptr || signals[i] == nullptr) return fail(DOTL_EINVAL, "%s: rank %d buffer is NULL", who, i);
+        if (!aligned16(parts[i]) || !aligned16(signals[i]))
+            return fail(DOTL_EINVAL, "%s: rank %d buffers must be 16-byte aligned", who, i);
+        p.part[i] = parts[i];
+        p.signal[i] = static_cast<unsigned int*>(signals[i]);
+        if (i >= d0 && i < d1) {
+            if (normed[i] == nullptr) return fail(DOTL_EINVAL, "%s: normed output of rank %d is NULL", who, i);
+            p.normed[i] = normed[i];
+            p.x_new[i] = x_new != nullptr ? x_new[i] : nullptr;
+            if (!aligned16(p.normed[i]) || !aligned16(p.x_new[i]))
+                return fail(DOTL_EINVAL, "%s: outputs must be 16-byte aligned", who);
+        }
+    }
+    if (!aligned16(x) || !aligned16(bias) || !aligned16(ln_weight) || !aligned16(ln_bias))
+        return fail(DOTL_EINVAL, "%s: x, bias and LayerNorm parameters must be 16-byte aligned", who);
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    const int cap = sm_count(dev) * dotl::kPeerBlocksPerSm;
+    if (blocks < 1 || blocks > cap)
+        return fail(DOTL_EINVAL, "%s: blocks %d outside 1..%d (every CTA must be resident at once)", who, blocks, cap);
+    if (rows == 0) return DOTL_OK;
+    p.x = x;
+    p.bias = bias;
+    p.sum_row_valid = sum_row_valid;
+    p.ln_w = ln_weight;
+    p.ln_b = ln_bias;
+    p.normed_row_valid = normed_row_valid;
+    p.rows = rows;
+    p.D = static_cast<int>(D);
+    p.eps = eps;
+    p.world = world;
+    p.rank = rank;
+    p.push = push ? 1 : 0;
+    p.timeout_ns = static_cast<unsigned long long>(timeout_ms) * 1000000ull;
+    const dim3 grid(static_cast<unsigned>(blocks)), block(dotl::kPeerWarps * 32);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t le;
+#define DOTL_ARLN(EPL)                                                                                   \
+    le = normed_dtype == DOTL_F16 ? launch_pdl(dotl::allreduce_ln_kernel<EPL, __half>, grid, block, 0, s, p) \
+                                  : launch_pdl(dotl::allreduce_ln_kernel<EPL, float>, grid, block, 0, s, p)
+    if (D <= 128) DOTL_ARLN(4);
+    else if (D <= 256) DOTL_ARLN(8);
+    else if (D <= 512) DOTL_ARLN(16);
+    else if (D <= 1024) DOTL_ARLN(32);
+    else DOTL_ARLN(64);
+#undef DOTL_ARLN
+    if (le != cudaSuccess) return fail(DOTL_ECUDA, "%s: launch failed: %s", who, cudaGetErrorString(le));
+    return check_launch(who);
 }
 
 }  // extern "C"

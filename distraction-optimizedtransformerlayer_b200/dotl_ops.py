@@ -52,7 +52,18 @@ _SIGNATURES = {
                         _vp, _vp, _f32, _vp, _i32, _i64, _vp, _i32, _vp], _i32),
     "dotl_attention": ([_vp, _vp, _vp, _i32, _i32, _i32, _i32, _P64, _P64, _P64, _vp, _i32, _P64,
                         _i32, _f32, _vp, _i32, _vp], _i32),
+    "dotl_peer_alloc": ([_i64, ctypes.POINTER(_vp)], _i32),
+    "dotl_peer_free": ([_vp], _i32),
+    "dotl_ipc_handle": ([_vp, _vp], _i32),
+    "dotl_ipc_open": ([_vp, ctypes.POINTER(_vp)], _i32),
+    "dotl_ipc_close": ([_vp], _i32),
+    "dotl_peer_blocks": ([ctypes.POINTER(ctypes.c_int)], _i32),
+    "dotl_peer_signal_bytes": ([_i32, _P64], _i32),
+    "dotl_allreduce_ln": ([_i32, _i32, _vp, _vp, _vp, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _f32, _vp,
+                           _i64, _i64, _i32, _i32, _vp], _i32),
 }
+
+IPC_HANDLE_BYTES = 64
 
 
 def load(path: str) -> ctypes.CDLL:
@@ -536,3 +547,64 @@ layernorm_warp_width = _getter("layernorm_warp_width", 2048)
 layernorm_set_block_threads = _setter("layernorm_block_threads")
 layernorm_set_fused_reduce = _setter("layernorm_fused_reduce")
 layernorm_fused_reduce_enabled = _getter("layernorm_fused_reduce", True)
+
+
+# ------------------------------------------------------------ peer memory ---
+
+def peer_alloc(nbytes: int) -> int:
+    """A zeroed device buffer whose IPC handle other processes can open."""
+    p = ctypes.c_void_p(0)
+    _check(lib().dotl_peer_alloc(int(nbytes), ctypes.byref(p)))
+    return int(p.value)
+
+
+def peer_free(ptr: int) -> None:
+    _check(lib().dotl_peer_free(ptr))
+
+
+def ipc_handle(ptr: int) -> bytes:
+    buf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    _check(lib().dotl_ipc_handle(ptr, buf))
+    return buf.raw
+
+
+def ipc_open(handle: bytes) -> int:
+    if len(handle) != IPC_HANDLE_BYTES:
+        raise ValueError(f"an IPC handle is {IPC_HANDLE_BYTES} bytes, got {len(handle)}")
+    buf = ctypes.create_string_buffer(handle, IPC_HANDLE_BYTES)
+    p = ctypes.c_void_p(0)
+    _check(lib().dotl_ipc_open(buf, ctypes.byref(p)))
+    return int(p.value)
+
+
+def ipc_close(ptr: int) -> None:
+    _check(lib().dotl_ipc_close(ptr))
+
+
+def peer_blocks() -> int:
+    n = ctypes.c_int(0)
+    _check(lib().dotl_peer_blocks(ctypes.byref(n)))
+    return int(n.value)
+
+
+def peer_signal_bytes(blocks: int) -> int:
+    n = ctypes.c_int64(0)
+    _check(lib().dotl_peer_signal_bytes(int(blocks), ctypes.byref(n)))
+    return int(n.value)
+
+
+def _ptrarr(vals) -> ctypes.Array:
+    return (ctypes.c_void_p * len(vals))(*[None if v is None else int(v) for v in vals])
+
+
+def allreduce_ln(world: int, rank: int, parts, signals, x_new, normed, normed_half: bool, push: bool,
+                 x: torch.Tensor, bias: Optional[torch.Tensor], ln_w: torch.Tensor, ln_b: torch.Tensor,
+                 eps: float, sum_row_valid: Optional[torch.Tensor], normed_row_valid: Optional[torch.Tensor],
+                 rows: int, D: int, blocks: int, timeout_ms: int) -> None:
+    """dotl_allreduce_ln: parts / signals / x_new / normed are per-rank lists of
+    device addresses as this process sees them (None where not used)."""
+    _check(lib().dotl_allreduce_ln(
+        world, rank, _ptrarr(parts), _ptrarr(signals), None if x_new is None else _ptrarr(x_new),
+        _ptrarr(normed), F16 if normed_half else F32, 1 if push else 0, x.data_ptr(), _ptr(bias),
+        _ptr(sum_row_valid), ln_w.data_ptr(), ln_b.data_ptr(), float(eps), _ptr(normed_row_valid),
+        int(rows), int(D), int(blocks), int(timeout_ms), _stream(x.device)))

@@ -19,10 +19,16 @@ Per layer, on every rank (x replicated, fp32):
     h_r = GELU(n2 W1_r^T + b1_r); part = mask(h_r W2_r^T + [b2]) -> all_reduce
     x2, out = x1 + part, next LN(x1 + part)
 
-The partial sums stay fp32 through the reduction. Padded rows are zeroed in
-the partials, so they add nothing; the residual stream keeps x there, which
-differs from the reference's zeroed rows only on padded rows, which no valid
-row attends to and the final LayerNorm writes as 0.
+With fused=True (the default where it applies) each all_reduce + add + LN
+pair is one dotl_allreduce_ln kernel over peer memory (optimized/peer.py):
+the GEMMs write bias-free partial sums and the kernel adds the full bias once,
+on valid rows only. Otherwise NCCL all-reduces partials that carry the bias on
+rank 0 and are zeroed on padded rows.
+
+The partial sums stay fp32 through the reduction. Padded rows add nothing;
+the residual stream keeps x there, which differs from the reference's zeroed
+rows only on padded rows, which no valid row attends to and the final
+LayerNorm writes as 0.
 """
 
 from __future__ import annotations
@@ -106,7 +112,9 @@ class TensorParallelTransformer:
     """
 
     def __init__(self, config, state_dict: Dict[str, torch.Tensor], group=None,
-                 device: Optional[torch.device] = None, eps: float = 1e-5) -> None:
+                 device: Optional[torch.device] = None, eps: float = 1e-5,
+                 fused: Optional[bool] = None, push: Optional[bool] = None,
+                 timeout_ms: int = 2000) -> None:
         import torch.distributed as dist
 
         self.dist = dist
@@ -123,13 +131,78 @@ class TensorParallelTransformer:
         for k, t in shards.items():
             half = k.split(".")[-1] in ("wqkv", "wo", "w1", "w2")
             self.w[k] = t.detach().to(dev, torch.float16 if half else torch.float32).contiguous()
+        d = config.d_model
+        if fused is None:
+            fused = d % 4 == 0 and d <= 2048 and world <= 8
+        self.fused, self.push, self.timeout_ms = bool(fused), push, timeout_ms
+        self.peer = None
+        if self.fused:
+            # the fused reduction adds the full biases itself; the GEMMs get zeros
+            for i in range(config.num_layers):
+                p = f"layers.{i}."
+                self.w[p + "bo_full"] = state_dict[p + "attention.out_proj.bias"].detach().to(dev, torch.float32).contiguous()
+                self.w[p + "b2_full"] = state_dict[p + "ffn_out.bias"].detach().to(dev, torch.float32).contiguous()
+            self.w["zero_d"] = torch.zeros(d, dtype=torch.float32, device=dev)
 
     def _kernels(self):
         from .kernels import _custom_kernels
 
         return _custom_kernels()
 
+    def _peer_group(self, rows: int):
+        from .peer import PeerGroup
+
+        if self.peer is None or self.peer.rows < rows:
+            if self.peer is not None:
+                self.peer.close()
+            self.peer = PeerGroup(self.group, rows, self.config.d_model, self.device, self.push,
+                                  self.timeout_ms)
+        return self.peer
+
+    def close(self) -> None:
+        """Collective: releases the peer-mapped buffers of the fused path."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
+
+    def _forward_fused(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]) -> torch.Tensor:
+        """The layer with each all-reduce + add + LayerNorm as one
+        dotl_allreduce_ln over peer memory. Returns the group's `out` buffer
+        viewed as [B, S, d]: it is overwritten by the next forward."""
+        k = self._kernels()
+        cfg, plan, w = self.config, self.plan, self.w
+        B, S, d = x.shape
+        T = B * S
+        pg = self._peer_group(T)
+        use_mask = valid_token_mask is not None and not bool(valid_token_mask.all())
+        mask = valid_token_mask.contiguous() if use_mask else None
+        rv = mask.reshape(-1) if use_mask else None
+        hd, hl = plan.head_dim, plan.local_heads
+        bufs = {n: pg.view(n, T) for n in ("part", "xa", "xb", "n16", "out")}
+        part, n16 = bufs["part"], bufs["n16"]
+        bufs["xa"].copy_(x.reshape(T, d))
+        k.layernorm_rows(bufs["xa"], w["layers.0.norm1.weight"], w["layers.0.norm1.bias"], self.eps, out=n16)
+        cur, alt = "xa", "xb"
+        for i in range(cfg.num_layers):
+            p = f"layers.{i}."
+            qkv = k.linear_fp16(n16.view(B, S, d), w[p + "wqkv"], w[p + "bqkv"], out_half=True)
+            q, kk, v = qkv.view(B, S, 3, hl, hd).permute(2, 0, 3, 1, 4).unbind(0)
+            ctx = k.attention_packed(q, kk, v, cfg.causal, hd ** -0.5, key_mask=mask)
+            k.linear_fp16(ctx.reshape(T, -1), w[p + "wo"], w["zero_d"], out=part)
+            pg.allreduce_ln(bufs[cur], w[p + "bo_full"], w[p + "norm2.weight"], w[p + "norm2.bias"], self.eps,
+                            alt, "n16", T, sum_row_valid=rv)
+            h = k.linear_fp16(n16, w[p + "w1"], w[p + "b1"], act=1, out_half=True)
+            k.linear_fp16(h, w[p + "w2"], w["zero_d"], out=part)
+            last = i == cfg.num_layers - 1
+            nn_ = "final_norm." if last else f"layers.{i + 1}.norm1."
+            pg.allreduce_ln(bufs[alt], w[p + "b2_full"], w[nn_ + "weight"], w[nn_ + "bias"], self.eps,
+                            None if last else cur, "out" if last else "n16", T, sum_row_valid=rv,
+                            normed_row_valid=rv if last else None)
+        return bufs["out"].view(B, S, d)
+
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if self.fused:
+            return self._forward_fused(x.float().contiguous(), valid_token_mask)
         k = self._kernels()
         cfg, plan, w = self.config, self.plan, self.w
         B, S, d = x.shape

@@ -2,8 +2,8 @@
  * libdotl: the C ABI of the B200 (sm_100a) single-transformer-layer forward.
  *
  * Every entry point takes plain device pointers, sizes and strides, and a
- * cudaStream_t passed as `void* stream`. No entry point allocates device
- * memory or synchronises: outputs and temporaries are the caller's, and work
+ * cudaStream_t passed as `void* stream`. No compute entry point allocates
+ * device memory or synchronises (the peer-memory setup calls below do): outputs and temporaries are the caller's, and work
  * is enqueued on `stream` (so the calls can be captured in a CUDA graph).
  *
  * Return value: 0 on success; a nonzero DOTL_E* code otherwise, with a
@@ -139,6 +139,55 @@ int dotl_attention(const void* q, const void* k, const void* v, int B, int H, in
                    const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
                    const uint8_t* mask, int mask_kind, const int64_t* mask_strides, int causal,
                    float scale, void* out, int out_layout, void* stream);
+
+/*
+ * Peer memory for the tensor-parallel layer (one process per GPU). These are
+ * setup calls, made once per peer group, and the only entry points that
+ * allocate or map device memory:
+ *   dotl_peer_alloc    cudaMalloc'd, zeroed buffer whose IPC handle peers can open
+ *   dotl_ipc_handle    its handle (DOTL_IPC_HANDLE_BYTES opaque bytes) for the peers
+ *   dotl_ipc_open      maps a peer's buffer into this process (peer access enabled)
+ *   dotl_ipc_close / dotl_peer_free undo them (close peers' mappings first)
+ *   dotl_peer_blocks   the grid dotl_allreduce_ln may use on this device (every CTA
+ *                      resident at once); all ranks must pass the same value
+ *   dotl_peer_signal_bytes  size of one rank's signal area for that grid
+ * No reference counterpart: the reference runs on one GPU.
+ */
+#define DOTL_IPC_HANDLE_BYTES 64
+int dotl_peer_alloc(int64_t bytes, void** ptr);
+int dotl_peer_free(void* ptr);
+int dotl_ipc_handle(const void* ptr, void* handle);
+int dotl_ipc_open(const void* handle, void** ptr);
+int dotl_ipc_close(void* ptr);
+int dotl_peer_blocks(int* blocks);
+int dotl_peer_signal_bytes(int blocks, int64_t* bytes);
+
+/*
+ * Sum over the ranks of fp32 partial sums + bias + residual + LayerNorm, in one
+ * kernel over peer memory. Replaces all_reduce(part) followed by
+ * fused_add_layernorm (add_layernorm.cuh:663-672) after each row-parallel GEMM
+ * of the tensor-parallel layer (the single-GPU pairs are optimized/layers.py:
+ * 241-243 and 258-261):
+ *   sum    = parts[0] + ... + parts[world-1] (+ bias)   in rank order: same bits on every rank
+ *   x_new  = x + (sum_row_valid ? sum : 0)              fp32; not stored where x_new[i] is NULL
+ *   normed = LN(x_new) * ln_weight + ln_bias            0 on rows normed_row_valid marks 0
+ * parts / signals / x_new / normed are host arrays of `world` device pointers,
+ * entry i being rank i's buffer as this process sees it (its own, or a peer's
+ * mapped by dotl_ipc_open); signal areas are zeroed dotl_peer_alloc memory of
+ * dotl_peer_signal_bytes(blocks). push = 0: this rank computes every row and
+ * writes only x_new[rank] / normed[rank]. push = 1: rank r computes rows
+ * [r*ceil(rows/world), ...) and writes them into every rank's outputs (which
+ * must then be peer-mapped too). Every rank must make the same calls with the
+ * same rows, D, push and blocks, in the same order. A wait for a peer longer than
+ * timeout_ms sets bit 4 of the device error word and ends the call's work; the
+ * group's counters then disagree and it must be rebuilt. D % 4 == 0, D <= 2048,
+ * world <= 8, all pointers 16-byte aligned.
+ */
+int dotl_allreduce_ln(int world, int rank, const float* const* parts, void* const* signals, float* const* x_new,
+                      void* const* normed, int normed_dtype, int push, const float* x, const float* bias,
+                      const uint8_t* sum_row_valid, const float* ln_weight, const float* ln_bias, float eps,
+                      const uint8_t* normed_row_valid, int64_t rows, int64_t D, int blocks, int timeout_ms,
+                      void* stream);
 
 #ifdef __cplusplus
 }

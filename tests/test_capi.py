@@ -110,3 +110,31 @@ def test_build_flags_target_sm100a():
 
     cmd = " ".join(kernel_ext.build_command())
     assert "arch=compute_100a,code=sm_100a" in cmd and "-lineinfo" in cmd
+
+
+def test_allreduce_ln_rejects(lib):
+    P2 = ctypes.c_void_p * 2
+    parts, sigs, outs = P2(16, 32), P2(48, 64), P2(80, 96)
+
+    def call(world=2, rank=0, D=128, dtype=0, timeout=2000, p=parts):
+        return lib.dotl_allreduce_ln(world, rank, p, sigs, None, outs, dtype, 0, 16, None, None, 16, 16,
+                                     1e-5, None, 8, D, 1, timeout, None)
+
+    assert call(world=9) == 1 and "world" in _err(lib)
+    assert call(rank=2) == 1 and "rank" in _err(lib)
+    assert call(D=130) == 1 and "multiple of 4" in _err(lib)
+    assert call(D=4096) == 1
+    assert call(dtype=5) == 1 and "dtype" in _err(lib)
+    assert call(timeout=0) == 1 and "timeout_ms" in _err(lib)
+    assert call(p=P2(16, None)) == 1 and "NULL" in _err(lib)
+    assert call(p=P2(16, 40)) == 1 and "aligned" in _err(lib)
+
+
+def test_peer_setup_rejects_and_sizes(lib):
+    n = ctypes.c_int64(0)
+    assert lib.dotl_peer_signal_bytes(296, ctypes.byref(n)) == 0 and n.value == 296 * 17 * 4
+    assert lib.dotl_peer_signal_bytes(0, ctypes.byref(n)) == 1
+    p = ctypes.c_void_p(0)
+    assert lib.dotl_peer_alloc(0, ctypes.byref(p)) == 1
+    assert lib.dotl_ipc_open(None, ctypes.byref(p)) == 1
+    assert lib.dotl_peer_free(None) == 0 and lib.dotl_ipc_close(None) == 0

@@ -1,7 +1,10 @@
-"""Tensor-parallel layer over NCCL on 2 GPUs against the oracle (gpu).
+"""Tensor-parallel layer on 2 GPUs against the oracle (gpu), with each
+all-reduce + add + LayerNorm either fused over peer memory (one-shot and push
+modes of dotl_allreduce_ln) or as NCCL all-reduce + the LayerNorm kernel.
 
 Runs only where at least two GPUs are visible; the CPU decomposition test in
-test_tensor_parallel_gloo.py covers the sharding everywhere."""
+test_tensor_parallel_gloo.py covers the sharding everywhere, and
+test_gpu_55_allreduce_ln.py the fused kernel's arithmetic on one GPU."""
 
 import os
 import socket
@@ -19,7 +22,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, path, case):
+def _worker(rank, world, port, path, case, mode):
     import sys
     import datetime
 
@@ -41,30 +44,39 @@ def _worker(rank, world, port, path, case):
         cfg = O.TransformerConfig(B, S, d, H, Fd, L, causal)
         params = O.init_params(cfg, 21)
         x, mask = O.generate_random_case(cfg, 22, pad, 1.0)
-        tp = TensorParallelTransformer(cfg, params)
-        with torch.inference_mode():
-            out = tp(x.cuda(), mask.cuda() if pad > 0 else None).cpu()
-            out2 = tp(x.cuda(), mask.cuda() if pad > 0 else None).cpu()
-        torch.cuda.synchronize()
+        tp = TensorParallelTransformer(cfg, params, fused=mode != "nccl", push=mode == "push")
+        try:
+            with torch.inference_mode():
+                out = tp(x.cuda(), mask.cuda() if pad > 0 else None).cpu()
+                out2 = tp(x.cuda(), mask.cuda() if pad > 0 else None).cpu()
+            torch.cuda.synchronize()
+            word = tp._kernels().device_error(clear=True)
+        finally:
+            tp.close()
+        torch.save({"out": out, "out2": out2, "word": word}, f"{path}.{rank}")
         if rank == 0:
             ref = O.baseline_forward(params, cfg, x, mask if pad > 0 else None, query_block=256)
-            torch.save({"out": out, "out2": out2, "ref": ref}, path)
+            torch.save({"ref": ref}, path)
     finally:
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("mode", ["oneshot", "push", "nccl"])
 @pytest.mark.parametrize("case", [(2, 256, 512, 8, 1024, 1, True, 0.0),
                                   (2, 192, 256, 4, 512, 2, False, 0.5),
                                   (1, 512, 1024, 8, 2048, 1, True, 0.0)])
-def test_tp2_matches_oracle(kernels, tmp_path, case):
+def test_tp2_matches_oracle(kernels, tmp_path, case, mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("tensor parallelism needs two GPUs")
     from oracle import layer as O
 
     path = str(tmp_path / "tp.pt")
-    mp.start_processes(_worker, args=(2, _free_port(), path, case), nprocs=2, start_method="spawn",
+    mp.start_processes(_worker, args=(2, _free_port(), path, case, mode), nprocs=2, start_method="spawn",
                        join=True)
-    r = torch.load(path)
-    assert torch.equal(r["out"], r["out2"])
-    res = O.compare_outputs(r["ref"], r["out"])
+    ref = torch.load(path)["ref"]
+    r0, r1 = torch.load(f"{path}.0"), torch.load(f"{path}.1")
+    assert r0["word"] == 0 and r1["word"] == 0
+    assert torch.equal(r0["out"], r0["out2"])
+    assert torch.equal(r0["out"], r1["out"]), "every rank must hold the same bits"
+    res = O.compare_outputs(ref, r0["out"])
     assert res.passed, (res.failed_elements, res.max_abs_error)
