@@ -12,6 +12,7 @@
 #include "attention.cuh"
 #include "gemm.cuh"
 #include "gemm_ln.cuh"
+#include "ffn.cuh"
 #include "layernorm.cuh"
 #include "peer_ln.cuh"
 
@@ -306,6 +307,22 @@ int launch_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap&
     const cudaError_t e = launch_pdl(kernel, dim3(grid), dim3(dotl::kAttnThreads), L::kAlloc, stream, tq, tk, tv, p);
     if (e != cudaSuccess) return fail(DOTL_ECUDA, "dotl_attention: launch failed: %s", cudaGetErrorString(e));
     return check_launch("dotl_attention");
+}
+
+// ------------------------------------------------------------- fused MLP --
+
+template <int D, bool NF16>
+int launch_ffn(const CUtensorMap& ta, const CUtensorMap& tw1, const CUtensorMap& tw2, const CUtensorMap& tr,
+               const CUtensorMap& tx, const CUtensorMap& tn, const dotl::FfnParams& p, int dev, cudaStream_t stream) {
+    using L = dotl::FfnSmem<D>;
+    auto kernel = dotl::ffn_kernel<D, NF16>;
+    static bool done[kMaxDevices] = {false};
+    if (int rc = ensure_smem(kernel, L::kAlloc, dev, done)) return rc;
+    const int grid = p.num_m_tiles < sm_count(dev) ? p.num_m_tiles : sm_count(dev);
+    const cudaError_t e =
+        launch_pdl(kernel, dim3(grid), dim3(dotl::kFfnThreads), L::kAlloc, stream, ta, tw1, tw2, tr, tx, tn, p);
+    if (e != cudaSuccess) return fail(DOTL_ECUDA, "dotl_ffn: launch failed: %s", cudaGetErrorString(e));
+    return check_launch("dotl_ffn");
 }
 
 }  // namespace
@@ -695,6 +712,90 @@ int dotl_attention(const void* q, const void* k, const void* v, int B, int H, in
         case 64: return launch_attn<64, 3>(maps[0], maps[1], maps[2], p, dev, s);
         default: return launch_attn<128, 2>(maps[0], maps[1], maps[2], p, dev, s);
     }
+}
+
+int dotl_ffn(const void* a, int64_t M, int64_t D, int64_t lda, const void* w1, int64_t F, int64_t ldw1,
+             const float* b1, const void* w2, int64_t ldw2, const float* b2, const float* resid, int64_t ldr,
+             const uint8_t* row_valid, int resid_mode, float* x_out, int64_t ldx, const float* ln_weight,
+             const float* ln_bias, float eps, void* normed, int normed_dtype, int64_t ldn,
+             const uint8_t* normed_row_valid, void* stream) {
+    const char* who = "dotl_ffn";
+    if (M < 0 || M > (int64_t)0x7fffffff - 256) return fail(DOTL_EINVAL, "%s: bad M=%lld", who, (long long)M);
+    if (D != 128 && D != 256) return fail(DOTL_EUNSUPPORTED, "%s: D=%lld (d_model) must be 128 or 256", who, (long long)D);
+    if (F <= 0 || F % dotl::kFfnChunk != 0 || F > 0x7fffffff)
+        return fail(DOTL_EUNSUPPORTED, "%s: F=%lld (ffn_dim) must be a positive multiple of 128", who, (long long)F);
+    if (resid_mode != DOTL_RESID_NONE && resid_mode != DOTL_RESID_ADD && resid_mode != DOTL_RESID_ADD_MASKSUB &&
+        resid_mode != DOTL_RESID_ADD_MASKALL)
+        return fail(DOTL_EINVAL, "%s: residual mode %d is not one of NONE, ADD, ADD_MASKSUB, ADD_MASKALL", who, resid_mode);
+    if (normed_dtype != DOTL_F32 && normed_dtype != DOTL_F16) return fail(DOTL_EINVAL, "%s: normed dtype must be DOTL_F32 or DOTL_F16", who);
+    if (!(eps >= 0.0f)) return fail(DOTL_EINVAL, "%s: eps must be >= 0", who);
+    if (M == 0) return DOTL_OK;
+    if (a == nullptr || w1 == nullptr || w2 == nullptr || b1 == nullptr || b2 == nullptr || ln_weight == nullptr ||
+        ln_bias == nullptr || normed == nullptr)
+        return fail(DOTL_EINVAL, "%s: NULL pointer", who);
+    if (lda < D || ldw1 < D || ldw2 < F || lda % 8 != 0 || ldw1 % 8 != 0 || ldw2 % 8 != 0)
+        return fail(DOTL_EUNSUPPORTED, "%s: lda, ldw1 >= D and ldw2 >= F must be multiples of 8", who);
+    if (!aligned16(a) || !aligned16(w1) || !aligned16(w2) || !aligned16(b1) || !aligned16(b2) ||
+        !aligned16(ln_weight) || !aligned16(ln_bias))
+        return fail(DOTL_EUNSUPPORTED, "%s: operands, biases and LayerNorm parameters must be 16-byte aligned", who);
+    if (resid_mode != DOTL_RESID_NONE) {
+        if (resid == nullptr) return fail(DOTL_EINVAL, "%s: residual mode %d needs resid", who, resid_mode);
+        if (!aligned16(resid) || ldr % 4 != 0 || ldr < D) return fail(DOTL_EUNSUPPORTED, "%s: resid must be 16-byte aligned with ldr >= D, ldr %% 4 == 0", who);
+    }
+    if ((resid_mode == DOTL_RESID_ADD_MASKSUB || resid_mode == DOTL_RESID_ADD_MASKALL) && row_valid == nullptr)
+        return fail(DOTL_EINVAL, "%s: masked residual mode needs row_valid", who);
+    if (x_out != nullptr && (!aligned16(x_out) || ldx % 4 != 0 || ldx < D))
+        return fail(DOTL_EUNSUPPORTED, "%s: x_out must be 16-byte aligned with ldx >= D, ldx %% 4 == 0", who);
+    if (!aligned16(normed) || ldn % 8 != 0 || ldn < D)
+        return fail(DOTL_EUNSUPPORTED, "%s: normed must be 16-byte aligned with ldn >= D, ldn %% 8 == 0", who);
+
+    CUtensorMap ta, tw1, tw2;
+    const cuuint64_t adims[2] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(M)};
+    const cuuint64_t astr[1] = {static_cast<cuuint64_t>(lda) * 2};
+    if (int rc = encode_f16_map(&ta, a, 2, adims, astr, dotl::kGemmBK, dotl::kGemmBM, who)) return rc;
+    const cuuint64_t w1dims[2] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(F)};
+    const cuuint64_t w1str[1] = {static_cast<cuuint64_t>(ldw1) * 2};
+    if (int rc = encode_f16_map(&tw1, w1, 2, w1dims, w1str, dotl::kGemmBK, 128, who)) return rc;
+    const cuuint64_t w2dims[2] = {static_cast<cuuint64_t>(F), static_cast<cuuint64_t>(D)};
+    const cuuint64_t w2str[1] = {static_cast<cuuint64_t>(ldw2) * 2};
+    if (int rc = encode_f16_map(&tw2, w2, 2, w2dims, w2str, dotl::kGemmBK, 128, who)) return rc;
+    // residual in, x_new and normed out: 32 x 32 blocks (unused maps describe `normed`)
+    CUtensorMap tr, tx, tn;
+    if (int rc = encode_out_map(&tn, normed, M, D, ldn, normed_dtype, who)) return rc;
+    tr = tn;
+    tx = tn;
+    if (resid_mode != DOTL_RESID_NONE)
+        if (int rc = encode_out_map(&tr, const_cast<float*>(resid), M, D, ldr, DOTL_F32, who)) return rc;
+    if (x_out != nullptr)
+        if (int rc = encode_out_map(&tx, x_out, M, D, ldx, DOTL_F32, who)) return rc;
+
+    dotl::FfnParams p;
+    p.M = static_cast<int>(M);
+    p.D = static_cast<int>(D);
+    p.F = static_cast<int>(F);
+    p.num_m_tiles = static_cast<int>((M + dotl::kGemmBM - 1) / dotl::kGemmBM);
+    p.b1 = b1;
+    p.b2 = b2;
+    p.resid = resid;
+    p.ldr = ldr;
+    p.row_valid = row_valid;
+    p.resid_mode = resid_mode;
+    p.x_out = x_out;
+    p.ldx = ldx;
+    p.ln_w = ln_weight;
+    p.ln_b = ln_bias;
+    p.eps = eps;
+    p.normed = normed;
+    p.ldn = ldn;
+    p.norm_row_valid = normed_row_valid;
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (D == 128)
+        return normed_dtype == DOTL_F16 ? launch_ffn<128, true>(ta, tw1, tw2, tr, tx, tn, p, dev, s)
+                                        : launch_ffn<128, false>(ta, tw1, tw2, tr, tx, tn, p, dev, s);
+    return normed_dtype == DOTL_F16 ? launch_ffn<256, true>(ta, tw1, tw2, tr, tx, tn, p, dev, s)
+                                    : launch_ffn<256, false>(ta, tw1, tw2, tr, tx, tn, p, dev, s);
 }
 
 // ------------------------------------------------------------ peer memory --

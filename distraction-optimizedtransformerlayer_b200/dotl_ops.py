@@ -52,6 +52,8 @@ _SIGNATURES = {
                         _vp, _vp, _f32, _vp, _i32, _i64, _vp, _i32, _vp], _i32),
     "dotl_attention": ([_vp, _vp, _vp, _i32, _i32, _i32, _i32, _P64, _P64, _P64, _vp, _i32, _P64,
                         _i32, _f32, _vp, _i32, _vp], _i32),
+    "dotl_ffn": ([_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _i64, _vp, _i32,
+                  _vp, _i64, _vp, _vp, _f32, _vp, _i32, _i64, _vp, _vp], _i32),
     "dotl_peer_alloc": ([_i64, ctypes.POINTER(_vp)], _i32),
     "dotl_peer_free": ([_vp], _i32),
     "dotl_ipc_handle": ([_vp, _vp], _i32),
@@ -218,6 +220,34 @@ def linear_fp16(a16: torch.Tensor, w16: torch.Tensor, bias: torch.Tensor, act: i
         out.stride(-2) if out.dim() >= 2 else N, tile_n, _stream(a16.device))
     _check(rc)
     return out
+
+
+def ffn_supported(d: int, f: int) -> bool:
+    """Whether dotl_ffn covers d_model d and ffn_dim f."""
+    return d in (128, 256) and f > 0 and f % 128 == 0
+
+
+def ffn(a16: torch.Tensor, w1_16: torch.Tensor, b1: torch.Tensor, w2_16: torch.Tensor, b2: torch.Tensor,
+        ln_w: torch.Tensor, ln_b: torch.Tensor, eps: float, resid: Optional[torch.Tensor] = None,
+        row_valid: Optional[torch.Tensor] = None, resid_mode: int = RESID_NONE,
+        x_out: Optional[torch.Tensor] = None, normed_half: bool = False,
+        normed_row_valid: Optional[torch.Tensor] = None, normed: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The MLP in one kernel: normed = LN(resid-mode(GELU(a w1^T + b1) w2^T + b2)),
+    x_new into x_out when given. a16 [..., D] fp16; returns normed (a16's shape)."""
+    D = a16.shape[-1]
+    M = a16.numel() // D
+    F = w1_16.shape[0]
+    if normed is None:
+        normed = torch.empty(a16.shape, dtype=torch.float16 if normed_half else torch.float32, device=a16.device)
+    rc = lib().dotl_ffn(
+        a16.data_ptr(), M, D, a16.stride(-2) if a16.dim() >= 2 else D, w1_16.data_ptr(), F, w1_16.stride(0),
+        b1.data_ptr(), w2_16.data_ptr(), w2_16.stride(0), b2.data_ptr(), _ptr(resid),
+        resid.stride(-2) if resid is not None and resid.dim() >= 2 else D, _ptr(row_valid), resid_mode,
+        _ptr(x_out), x_out.stride(-2) if x_out is not None and x_out.dim() >= 2 else D, ln_w.data_ptr(),
+        ln_b.data_ptr(), float(eps), normed.data_ptr(), F16 if normed.dtype == torch.float16 else F32,
+        normed.stride(-2) if normed.dim() >= 2 else D, _ptr(normed_row_valid), _stream(a16.device))
+    _check(rc)
+    return normed
 
 
 def linear_ln_supported(N: int) -> bool:

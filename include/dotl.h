@@ -126,6 +126,25 @@ int dotl_linear_ln(const void* a, int64_t M, int64_t K, int64_t lda, const void*
                    void* stream);
 
 /*
+ * The layer's whole MLP in one kernel, the [M, F] hidden kept on chip.
+ * Replaces linear_gelu -> linear_bias -> fused_add_layernorm (linear_gelu.cuh:
+ * 598-756, add_layernorm.cuh:663-692; the sequence of optimized/layers.py:
+ * 241-261) and supersedes fused_ffn_block (ffn_block.cuh:270-311, which covers
+ * only d = F <= 64):
+ *   h      = GELU_erf(a w1^T + b1)              a fp16 [M, D]; h rounded to fp16, never stored
+ *   x_new  = resid_mode epilogue(h w2^T + b2)   as dotl_linear; stored to x_out unless NULL
+ *   normed = LN(x_new) * ln_weight + ln_bias     0 where normed_row_valid is 0
+ * w1 fp16 [F, D], w2 fp16 [D, F] (nn.Linear layouts). D (d_model) 128 or 256;
+ * F a multiple of 128. resid_mode NONE, ADD, ADD_MASKSUB or ADD_MASKALL.
+ * Leading dimensions multiples of 8 (4 for the fp32 ones), pointers 16-byte aligned.
+ */
+int dotl_ffn(const void* a, int64_t M, int64_t D, int64_t lda, const void* w1, int64_t F, int64_t ldw1,
+             const float* b1, const void* w2, int64_t ldw2, const float* b2, const float* resid, int64_t ldr,
+             const uint8_t* row_valid, int resid_mode, float* x_out, int64_t ldx, const float* ln_weight,
+             const float* ln_bias, float eps, void* normed, int normed_dtype, int64_t ldn,
+             const uint8_t* normed_row_valid, void* stream);
+
+/*
  * Flash attention forward, fp16 q/k/v, fp32 softmax, fp16 output.
  * Replaces fused_attention_forward (attention_dispatch.cuh:332-519).
  *   q/k/v: [B,H,S,head_dim] addressed by {batch, head, seq} element strides
