@@ -320,33 +320,11 @@ def _layer_ops(model, x, mask, kernels, cfg):
     x2 = kernels.linear_fp16(h, layer.ffn_out.half_weight(), _f32_param(layer.ffn_out, "bias"), resid=x1,
                              row_valid=row_valid, resid_mode=3 if use_mask else 1)
     pairs = _attention_pairs(cfg, mask.cpu() if use_mask else None)
-    if kernels.linear_ln_preferred(T, d):
-        # the layer's own kernel list: out_proj and ffn_out carry the LayerNorms
-        lnw2, lnb2 = _f32_param(layer.norm2, "weight"), _f32_param(layer.norm2, "bias")
-        lnwf, lnbf = _f32_param(model.final_norm, "weight"), _f32_param(model.final_norm, "bias")
-        out_f = torch.empty_like(x)
-        return [
-            ("layernorm_entry", "hbm", T * d * 6,
-             lambda: kernels.layernorm_rows(x, _f32_param(layer.norm1, "weight"),
-                                            _f32_param(layer.norm1, "bias"), 1e-5, out_half=True, out=n1)),
-            ("gemm_qkv", "tensor", 2 * T * 3 * d * d,
-             lambda: kernels.linear_fp16(n1, qkv_w, qkv_b, out_half=True, out=qkv)),
-            ("attention", "tensor", 4 * hd * H * pairs,
-             lambda: kernels.attention_packed(q, k, v, cfg.causal, hd ** -0.5, key_mask=mask, out=ctx)),
-            ("gemm_out_proj_ln", "tensor", 2 * T * d * d,
-             lambda: kernels.linear_ln(ctx, layer.attention.out_proj.half_weight(),
-                                       _f32_param(layer.attention.out_proj, "bias"), lnw2, lnb2, 1e-5,
-                                       resid=x, row_valid=row_valid, resid_mode=2 if use_mask else 1,
-                                       out=x1, normed=n2)),
-            ("gemm_ffn_in_gelu", "tensor", 2 * T * d * F,
-             lambda: kernels.linear_fp16(n2, layer.ffn_in.half_weight(), _f32_param(layer.ffn_in, "bias"),
-                                         act=1, out_half=True, out=h)),
-            ("gemm_ffn_out_ln", "tensor", 2 * T * F * d,
-             lambda: kernels.linear_ln(h, layer.ffn_out.half_weight(), _f32_param(layer.ffn_out, "bias"),
-                                       lnwf, lnbf, 1e-5, resid=x1, row_valid=row_valid,
-                                       resid_mode=3 if use_mask else 1, store_x=False, normed_half=False,
-                                       normed_row_valid=row_valid, normed=out_f)),
-        ]
+    lnw2, lnb2 = _f32_param(layer.norm2, "weight"), _f32_param(layer.norm2, "bias")
+    lnwf, lnbf = _f32_param(model.final_norm, "weight"), _f32_param(model.final_norm, "bias")
+    out_f = torch.empty_like(x)
+    # the layer's own kernel list (optimized/layers.py MyTransformerBlock)
+    ln_fused = kernels.linear_ln_preferred(T, d)
     ops = [
         ("layernorm_entry", "hbm", T * d * 6,
          lambda: kernels.layernorm_rows(x, _f32_param(layer.norm1, "weight"),
@@ -355,24 +333,48 @@ def _layer_ops(model, x, mask, kernels, cfg):
          lambda: kernels.linear_fp16(n1, qkv_w, qkv_b, out_half=True, out=qkv)),
         ("attention", "tensor", 4 * hd * H * pairs,
          lambda: kernels.attention_packed(q, k, v, cfg.causal, hd ** -0.5, key_mask=mask, out=ctx)),
-        ("gemm_out_proj_residual", "tensor", 2 * T * d * d,
-         lambda: kernels.linear_fp16(ctx, layer.attention.out_proj.half_weight(),
-                                     _f32_param(layer.attention.out_proj, "bias"), resid=x,
-                                     row_valid=row_valid, resid_mode=2 if use_mask else 1, out=x1)),
-        ("layernorm_2", "hbm", T * d * 6,
-         lambda: kernels.layernorm_rows(x1, _f32_param(layer.norm2, "weight"),
-                                        _f32_param(layer.norm2, "bias"), 1e-5, out_half=True, out=n2)),
-        ("gemm_ffn_in_gelu", "tensor", 2 * T * d * F,
-         lambda: kernels.linear_fp16(n2, layer.ffn_in.half_weight(), _f32_param(layer.ffn_in, "bias"),
-                                     act=1, out_half=True, out=h)),
-        ("gemm_ffn_out_residual", "tensor", 2 * T * F * d,
-         lambda: kernels.linear_fp16(h, layer.ffn_out.half_weight(), _f32_param(layer.ffn_out, "bias"),
-                                     resid=x1, row_valid=row_valid, resid_mode=3 if use_mask else 1,
-                                     out=x2)),
-        ("layernorm_final", "hbm", T * d * 8,
-         lambda: kernels.layernorm_rows(x2, _f32_param(model.final_norm, "weight"),
-                                        _f32_param(model.final_norm, "bias"), 1e-5, row_valid=row_valid)),
     ]
+    if ln_fused:
+        ops.append(("gemm_out_proj_ln", "tensor", 2 * T * d * d,
+                    lambda: kernels.linear_ln(ctx, layer.attention.out_proj.half_weight(),
+                                              _f32_param(layer.attention.out_proj, "bias"), lnw2, lnb2, 1e-5,
+                                              resid=x, row_valid=row_valid, resid_mode=2 if use_mask else 1,
+                                              out=x1, normed=n2)))
+    else:
+        ops += [
+            ("gemm_out_proj_residual", "tensor", 2 * T * d * d,
+             lambda: kernels.linear_fp16(ctx, layer.attention.out_proj.half_weight(),
+                                         _f32_param(layer.attention.out_proj, "bias"), resid=x,
+                                         row_valid=row_valid, resid_mode=2 if use_mask else 1, out=x1)),
+            ("layernorm_2", "hbm", T * d * 6,
+             lambda: kernels.layernorm_rows(x1, lnw2, lnb2, 1e-5, out_half=True, out=n2)),
+        ]
+    if kernels.ffn_preferred(T, d, F):
+        ops.append(("ffn_fused", "tensor", 4 * T * d * F,
+                    lambda: kernels.ffn(n2, layer.ffn_in.half_weight(), _f32_param(layer.ffn_in, "bias"),
+                                        layer.ffn_out.half_weight(), _f32_param(layer.ffn_out, "bias"),
+                                        lnwf, lnbf, 1e-5, resid=x1, row_valid=row_valid,
+                                        resid_mode=3 if use_mask else 1, normed_row_valid=row_valid,
+                                        normed=out_f)))
+        return ops
+    ops.append(("gemm_ffn_in_gelu", "tensor", 2 * T * d * F,
+                lambda: kernels.linear_fp16(n2, layer.ffn_in.half_weight(), _f32_param(layer.ffn_in, "bias"),
+                                            act=1, out_half=True, out=h)))
+    if ln_fused:
+        ops.append(("gemm_ffn_out_ln", "tensor", 2 * T * F * d,
+                    lambda: kernels.linear_ln(h, layer.ffn_out.half_weight(), _f32_param(layer.ffn_out, "bias"),
+                                              lnwf, lnbf, 1e-5, resid=x1, row_valid=row_valid,
+                                              resid_mode=3 if use_mask else 1, store_x=False, normed_half=False,
+                                              normed_row_valid=row_valid, normed=out_f)))
+    else:
+        ops += [
+            ("gemm_ffn_out_residual", "tensor", 2 * T * F * d,
+             lambda: kernels.linear_fp16(h, layer.ffn_out.half_weight(), _f32_param(layer.ffn_out, "bias"),
+                                         resid=x1, row_valid=row_valid, resid_mode=3 if use_mask else 1,
+                                         out=x2)),
+            ("layernorm_final", "hbm", T * d * 8,
+             lambda: kernels.layernorm_rows(x2, lnwf, lnbf, 1e-5, row_valid=row_valid)),
+        ]
     return ops
 
 
@@ -649,7 +651,7 @@ def run_ours(args, rank, world, local_rank):
         else:
             achieved = dom["work"] / (dom["ms"] / 1e3) / 1e9
             peak, unit = hbm, "GB/s"
-        launches_per_step = 1 + (5 if kernels.linear_ln_preferred(tokens_per_rank, cfg.d_model) else 7) * cfg.num_layers
+        launches_per_step = 1 + (len(breakdown) - 1) * cfg.num_layers   # entry LN + each layer's kernels
         value = job_tokens * args.steps / (total_ms / 1e3)
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,

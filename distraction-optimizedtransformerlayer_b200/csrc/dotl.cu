@@ -247,7 +247,7 @@ int max_clusters(Kernel kernel, int cs, uint32_t smem, int* out) {
 
 template <int BN, int STAGES, bool NORM_F16>
 int launch_gemm_ln(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tn,
-                   const dotl::GemmLnParams& p, int dev, cudaStream_t stream) {
+                   const CUtensorMap& tr, const dotl::GemmLnParams& p, int dev, cudaStream_t stream) {
     using L = dotl::GemmLnSmem<BN, STAGES>;
     auto kernel = dotl::gemm_ln_kernel<BN, STAGES, NORM_F16>;
     static bool done[kMaxDevices] = {false};
@@ -273,7 +273,7 @@ int launch_gemm_ln(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorM
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tw, tx, tn, p);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tw, tx, tn, tr, p);
     if (e != cudaSuccess) return fail(DOTL_ECUDA, "dotl_linear_ln: launch failed: %s", cudaGetErrorString(e));
     return check_launch("dotl_linear_ln");
 }
@@ -586,6 +586,10 @@ int dotl_linear_ln(const void* a, int64_t M, int64_t K, int64_t lda, const void*
                                 out != nullptr ? ldo : ldn, out != nullptr ? DOTL_F32 : normed_dtype, who))
         return rc;
     if (int rc = encode_out_map(&tn, normed, M, N, ldn, normed_dtype, who)) return rc;
+    // residual in as 32 x 32 fp32 blocks (without a residual the map is unused)
+    CUtensorMap tr = tn;
+    if (resid_mode != DOTL_RESID_NONE)
+        if (int rc = encode_out_map(&tr, const_cast<float*>(resid), M, N, ldr, DOTL_F32, who)) return rc;
 
     dotl::GemmLnParams p;
     p.M = static_cast<int>(M);
@@ -606,10 +610,13 @@ int dotl_linear_ln(const void* a, int64_t M, int64_t K, int64_t lda, const void*
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const bool f16 = normed_dtype == DOTL_F16;
     if (bn == 256)
-        return f16 ? launch_gemm_ln<256, 3, true>(ta, tw, tx, tn, p, dev, s) : launch_gemm_ln<256, 3, false>(ta, tw, tx, tn, p, dev, s);
+        return f16 ? launch_gemm_ln<256, 3, true>(ta, tw, tx, tn, tr, p, dev, s)
+                   : launch_gemm_ln<256, 3, false>(ta, tw, tx, tn, tr, p, dev, s);
     if (bn == 128)
-        return f16 ? launch_gemm_ln<128, 5, true>(ta, tw, tx, tn, p, dev, s) : launch_gemm_ln<128, 5, false>(ta, tw, tx, tn, p, dev, s);
-    return f16 ? launch_gemm_ln<64, 7, true>(ta, tw, tx, tn, p, dev, s) : launch_gemm_ln<64, 7, false>(ta, tw, tx, tn, p, dev, s);
+        return f16 ? launch_gemm_ln<128, 4, true>(ta, tw, tx, tn, tr, p, dev, s)
+                   : launch_gemm_ln<128, 4, false>(ta, tw, tx, tn, tr, p, dev, s);
+    return f16 ? launch_gemm_ln<64, 6, true>(ta, tw, tx, tn, tr, p, dev, s)
+               : launch_gemm_ln<64, 6, false>(ta, tw, tx, tn, tr, p, dev, s);
 }
 
 int dotl_attention(const void* q, const void* k, const void* v, int B, int H, int S, int head_dim,

@@ -57,20 +57,24 @@ struct GemmLnSmem {
     using G = GemmSmem<BN, STAGES>;
     static constexpr uint32_t kOffStage = G::kOffStage;              // 8 x 4 KB staging
     static constexpr uint32_t kStageBufBytes = G::kStageBufBytes;
-    static constexpr uint32_t kOffStats = kOffStage + 8 * kStageBufBytes;   // [2][8][128] (mean, M2)
+    static constexpr uint32_t kOffStage2 = kOffStage + 8 * kStageBufBytes;  // 8 x 4 KB, residual double buffer
+    static constexpr uint32_t kOffStats = kOffStage2 + 8 * kStageBufBytes;  // [2][8][128] (mean, M2)
     static constexpr uint32_t kStatsParityBytes = kLnMaxCluster * kGemmBM * 8;
     static constexpr uint32_t kOffHalf = kOffStats + 2 * kStatsParityBytes;  // [128] (mean, M2) of half 1
     static constexpr uint32_t kOffBar = kOffHalf + kGemmBM * 8;
-    // GemmBars, then stats_full[2], half_ready[4] (one per lane quarter), exit
+    // GemmBars, then stats_full[2], half_ready[4] (one per lane quarter), exit,
+    // resid_full[8 warps][2 buffers]
     static constexpr int kBarStats = GemmBars<STAGES>::kCount;
     static constexpr int kBarHalf = kBarStats + 2;
     static constexpr int kBarExit = kBarHalf + 4;
-    static constexpr uint32_t kNumBars = kBarExit + 1;
+    static constexpr int kBarResid = kBarExit + 1;
+    static constexpr uint32_t kNumBars = kBarResid + 16;
     static constexpr uint32_t kOffSlot = kOffBar + kNumBars * 8;
     static constexpr uint32_t kOffAbort = kOffSlot + 4;
     static constexpr uint32_t kBytes = kOffAbort + 4;
     static constexpr uint32_t kAlloc = kBytes + 1024;
     static constexpr uint32_t kTmemCols = 2 * BN;
+    static_assert(kAlloc <= 232448, "dynamic shared memory over the 227 KB an sm_100a CTA may use");
 };
 
 // (mean_a, m2_a) over n_a values merged with (mean_b, m2_b) over n_b.
@@ -87,7 +91,7 @@ template <int BN, int STAGES, bool NORM_F16>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_ln_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
                    const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_n,
-                   const GemmLnParams p) {
+                   const __grid_constant__ CUtensorMap tmap_r, const GemmLnParams p) {
     using L = GemmLnSmem<BN, STAGES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -117,6 +121,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             mbar_init(stats_full(b), 128 * cs);   // the half-0 lanes of every CTA
         }
         for (int q = 0; q < 4; ++q) mbar_init(half_ready(q), 32);
+        for (int i = 0; i < 16; ++i) mbar_init(bar0 + 8u * (L::kBarResid + i), 1);
         mbar_init(bars.drain(), 1);
         mbar_init(exit_bar, cs);
         *abort_flag = 0;
@@ -125,6 +130,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tma_prefetch_map(&tmap_w);
         tma_prefetch_map(&tmap_x);
         tma_prefetch_map(&tmap_n);
+        if (p.resid_mode != kResidNone) tma_prefetch_map(&tmap_r);
     }
     cluster_sync_after_init();
     pdl_wait();
@@ -162,6 +168,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const float2* stats = reinterpret_cast<const float2*>(smem + L::kOffStats);
         const bool has_resid = p.resid_mode != kResidNone && p.resid_mode != kMaskRows;
         const int n_cta0 = static_cast<int>(rank) * BN;   // first column of this CTA
+        // Residual 32 x 32 blocks arrive by TMA, alternating between the warp's
+        // two staging buffers (128B swizzle: lane l's row at l * 128, granule g
+        // at g ^ (l & 7)); the next block is in flight while this one is used,
+        // and x_new leaves from the buffer its residual arrived in.
+        uint8_t* sbuf[2] = {stage_ptr, smem + L::kOffStage2 + (warp - 2) * L::kStageBufBytes};
+        const uint32_t saddr[2] = {stage_addr, sbase + L::kOffStage2 + static_cast<uint32_t>(warp - 2) * L::kStageBufBytes};
+        const uint32_t rbar[2] = {bar0 + 8u * (L::kBarResid + 2 * (warp - 2)),
+                                  bar0 + 8u * (L::kBarResid + 2 * (warp - 2) + 1)};
+        uint32_t ruse[2] = {0u, 0u};                      // completed waits per buffer
+        uint32_t rissued[2] = {0u, 0u};
         int acc = 0;
         uint32_t acc_phase = 0;
         uint32_t it = 0;                                  // tiles done by this CTA
@@ -172,16 +188,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const bool row_ok = row < p.M;
             const bool valid = (p.row_valid == nullptr) || !row_ok || (p.row_valid[row] != 0);
             const bool nvalid = (p.norm_row_valid == nullptr) || !row_ok || (p.norm_row_valid[row] != 0);
-            float4 rr[kCW / 4];
-            auto load_resid = [&](int nc) {
-                if (has_resid && row_ok) {
-                    const float4* rp = reinterpret_cast<const float4*>(p.resid + static_cast<int64_t>(row) * p.ldr + nc);
-#pragma unroll
-                    for (int j = 0; j < kCW / 4; ++j) rr[j] = rp[j];
+            auto issue_resid = [&](int nc, int slot) {
+                __syncwarp();
+                if (lane == 0) {
+                    bulk_wait_read<0>();                  // stores still reading the buffer
+                    fence_proxy_async_smem();
+                    mbar_arrive_expect_tx(rbar[slot], 4096);
+                    tma_load_2d(saddr[slot], &tmap_r, rbar[slot], nc, m_blk * kGemmBM + quarter * 32);
                 }
+                ++rissued[slot];
             };
             float b_cur = __ldg(p.bias + n_cta0 + half * kCW + lane);
-            load_resid(n_cta0 + half * kCW);
+            if (has_resid) issue_resid(n_cta0 + half * kCW, 0);
             bool ok = mbar_wait(bars.accf(acc), acc_phase, abort_flag);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
@@ -195,7 +213,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int k = 0; k < kChunks; ++k) {
                 const int c = half * kCW + k * 2 * kCW;
                 const int nc = n_cta0 + c;
-                if (k != 0) load_resid(nc);
+                const int slot = k & 1;
+                if (has_resid && k + 1 < kChunks) issue_resid(nc + 2 * kCW, slot ^ 1);
                 const float b_next = k + 1 < kChunks ? __ldg(p.bias + nc + 2 * kCW + lane) : 0.0f;
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(t_row + c, r);
@@ -203,21 +222,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 float v[kCW];
 #pragma unroll
                 for (int j = 0; j < kCW; ++j) v[j] = __uint_as_float(r[j]) + __shfl_sync(0xffffffffu, b_cur, j);
-                if (has_resid && row_ok) {
+                if (has_resid) {
+                    ok = mbar_wait(rbar[slot], ruse[slot] & 1u, abort_flag);
+                    if (!__all_sync(0xffffffffu, ok)) {
+                        ok = false;
+                        break;
+                    }
+                    ++ruse[slot];
                     const bool keep_sub = valid || p.resid_mode == kResidAdd;
                     const bool keep_all = valid || p.resid_mode != kResidAddMaskAll;
+                    const uint8_t* rrow = sbuf[slot] + lane * 128;
 #pragma unroll
                     for (int j = 0; j < kCW; j += 4) {
-                        v[j] = keep_all ? rr[j / 4].x + (keep_sub ? v[j] : 0.0f) : 0.0f;
-                        v[j + 1] = keep_all ? rr[j / 4].y + (keep_sub ? v[j + 1] : 0.0f) : 0.0f;
-                        v[j + 2] = keep_all ? rr[j / 4].z + (keep_sub ? v[j + 2] : 0.0f) : 0.0f;
-                        v[j + 3] = keep_all ? rr[j / 4].w + (keep_sub ? v[j + 3] : 0.0f) : 0.0f;
+                        const float4 rr = *reinterpret_cast<const float4*>(rrow + (((j >> 2) ^ (lane & 7)) << 4));
+                        v[j] = keep_all ? rr.x + (keep_sub ? v[j] : 0.0f) : 0.0f;
+                        v[j + 1] = keep_all ? rr.y + (keep_sub ? v[j + 1] : 0.0f) : 0.0f;
+                        v[j + 2] = keep_all ? rr.z + (keep_sub ? v[j + 2] : 0.0f) : 0.0f;
+                        v[j + 3] = keep_all ? rr.w + (keep_sub ? v[j + 3] : 0.0f) : 0.0f;
                     }
                 }
                 if (p.store_x) {
-                    if (lane == 0) bulk_wait_read<0>();
-                    __syncwarp();
-                    uint8_t* srow = stage_ptr + lane * 128;
+                    if (!has_resid) {
+                        if (lane == 0) bulk_wait_read<0>();
+                        __syncwarp();
+                    }
+                    uint8_t* srow = sbuf[slot] + lane * 128;
 #pragma unroll
                     for (int q = 0; q < 8; ++q)
                         *reinterpret_cast<uint4*>(srow + ((q ^ (lane & 7)) << 4)) =
@@ -226,7 +255,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) {
-                        tma_store_2d(&tmap_x, stage_addr, nc, m_blk * kGemmBM + quarter * 32);
+                        tma_store_2d(&tmap_x, saddr[slot], nc, m_blk * kGemmBM + quarter * 32);
                         bulk_commit();
                     }
                 }
@@ -252,6 +281,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
                 b_cur = b_next;
             }
+            if (!ok) break;
             tmem_st_wait();
 
             // ---- the CTA's two halves, then the cluster exchange
@@ -346,7 +376,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 acc_phase ^= 1u;
             }
         }
-        if (lane == 0) bulk_wait_all();
+        if (lane == 0) {
+            bulk_wait_all();
+            // after an abort a residual block may still be landing in staging memory
+            for (int sl = 0; sl < 2; ++sl)
+                if (rissued[sl] != ruse[sl]) mbar_wait_drain(rbar[sl], ruse[sl] & 1u);
+        }
     }
 
     // ------------------------------------------------------------ teardown --

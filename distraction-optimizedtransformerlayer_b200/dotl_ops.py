@@ -227,6 +227,15 @@ def ffn_supported(d: int, f: int) -> bool:
     return d in (128, 256) and f > 0 and f % 128 == 0
 
 
+def ffn_preferred(rows: int, d: int, f: int) -> bool:
+    """The layer's rule for the one-kernel MLP: covered, and at least 32 row
+    blocks of 128 (below that one block per SM runs its whole F serially and
+    the two GEMMs' wider grids win: 36 vs 24 us at 256 x 256 x 1024; from 64
+    blocks on it wins, 15 vs 20 us at 8192 x 128 x 128, 412 vs 504 us at
+    262144 x 256 x 1024)."""
+    return ffn_supported(d, f) and (rows + 127) // 128 >= 32
+
+
 def ffn(a16: torch.Tensor, w1_16: torch.Tensor, b1: torch.Tensor, w2_16: torch.Tensor, b2: torch.Tensor,
         ln_w: torch.Tensor, ln_b: torch.Tensor, eps: float, resid: Optional[torch.Tensor] = None,
         row_valid: Optional[torch.Tensor] = None, resid_mode: int = RESID_NONE,

@@ -75,6 +75,26 @@ def _linear_ln_ok(rows: int, n: int) -> bool:
     return _custom_kernels().linear_ln_preferred(rows, n)
 
 
+def _ffn_ok(rows: int, d: int, f: int) -> bool:
+    """Whether the layer runs its MLP (ffn_in, GELU, ffn_out, residual, next
+    LayerNorm) as the one dotl_ffn kernel."""
+    return _custom_kernels().ffn_preferred(rows, d, f)
+
+
+def _ffn(n2: torch.Tensor, ffn_in, ffn_out, norm, resid: torch.Tensor,
+         row_valid: Optional[torch.Tensor], resid_mode: int, store_x: bool, normed_half: bool,
+         normed_row_valid: Optional[torch.Tensor] = None):
+    """(x_new, norm(x_new)) with x_new = resid-mode(GELU(n2 W1^T + b1) W2^T + b2),
+    the hidden never leaving the chip (x_new None when store_x is False)."""
+    k = _custom_kernels()
+    x_out = torch.empty_like(resid) if store_x else None
+    normed = k.ffn(n2, ffn_in.half_weight(), _f32_param(ffn_in, "bias"), ffn_out.half_weight(),
+                   _f32_param(ffn_out, "bias"), _f32_param(norm, "weight"), _f32_param(norm, "bias"),
+                   norm.eps, resid=resid, row_valid=row_valid, resid_mode=resid_mode, x_out=x_out,
+                   normed_half=normed_half, normed_row_valid=normed_row_valid)
+    return x_out, normed
+
+
 def _linear_ln(a16: torch.Tensor, w16: torch.Tensor, bias32: torch.Tensor, norm,
                resid: Optional[torch.Tensor] = None, row_valid: Optional[torch.Tensor] = None,
                resid_mode: int = 0, store_x: bool = True, normed_half: bool = True,

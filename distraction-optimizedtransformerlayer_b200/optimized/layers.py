@@ -13,8 +13,11 @@ Data flow of one block (T = B*S rows, d = d_model):
 
 Every residual add and masked_fill of the reference block
 (torch_transformer_benchmark.py:234-245) is folded into a GEMM epilogue or a
-LayerNorm, so a block is 6 kernels and never writes an intermediate it reads
-back only to add it.
+LayerNorm, so a block is at most 8 kernels and never writes an intermediate
+it reads back only to add it. Where the shape allows, out_proj -> norm2 and
+ffn_out -> next norm are each one GEMM + LayerNorm kernel (6 kernels), and for
+d_model 128/256 the whole MLP (ffn_in, GELU, ffn_out, residual, next norm) is
+one kernel that keeps h on chip (5 kernels with the former).
 """
 
 from __future__ import annotations
@@ -25,8 +28,8 @@ import torch
 import torch.nn as nn
 
 from . import config
-from .kernels import (_attention_dispatch, _f32_param, _layernorm, _linear, _linear_bias, _linear_ln,
-                      _linear_ln_ok)
+from .kernels import (_attention_dispatch, _f32_param, _ffn, _ffn_ok, _layernorm, _linear, _linear_bias,
+                      _linear_ln, _linear_ln_ok)
 from .util import _version_or_none
 
 RESID_ADD, RESID_ADD_MASKSUB, RESID_ADD_MASKALL = 1, 2, 3
@@ -176,11 +179,17 @@ class MyTransformerBlock(nn.Module):
         else:
             x1 = self.attention(normed, valid_token_mask, self.causal, mask_is_trivial, residual=x)
             n2 = _layernorm(x1, self.norm2, out_half=True)
-        h = _linear(n2, self.ffn_in.half_weight(), _f32_param(self.ffn_in, "bias"), act=1,
-                    out_half=True)
         # x1 + ffn_out(h); padded rows of the whole sum zeroed (the block's
         # trailing masked_fill), before the next LayerNorm reads it.
         mode = RESID_ADD_MASKALL if use_mask else RESID_ADD
+        if _ffn_ok(x.numel() // x.shape[-1], x.shape[-1], self.ffn_in.weight.shape[0]):
+            # ffn_in + GELU + ffn_out + residual + next norm in one kernel
+            x2, out = _ffn(n2, self.ffn_in, self.ffn_out, next_norm, x1, row_valid, mode,
+                           store_x=not next_norm_is_output, normed_half=not next_norm_is_output,
+                           normed_row_valid=row_valid if next_norm_is_output else None)
+            return (x2.view(x.shape) if x2 is not None else None), out
+        h = _linear(n2, self.ffn_in.half_weight(), _f32_param(self.ffn_in, "bias"), act=1,
+                    out_half=True)
         if fused:
             # the model's output: x2 itself is not needed, only its final norm
             return _linear_ln(h, self.ffn_out.half_weight(), _f32_param(self.ffn_out, "bias"), next_norm,
