@@ -661,8 +661,9 @@ def run_ours(args, rank, world, local_rank):
             "config": {"workload": _describe(args.config), "batch_per_gpu": hi - lo,
                        "global_batch": (hi - lo) * world, "seq_len": cfg.seq_len,
                        "layers": cfg.num_layers, "parallelism": f"dp{world}",
-                       "l2": "flushed between steps (256 MiB write); inputs smaller than L2",
-                       "cuda_graph": oconfig.CUDA_GRAPH != "off",
+                       "l2": "flushed between steps (256 MiB write); inputs "
+                             + ("larger" if x.numel() * 4 > 126 * 2 ** 20 else "smaller") + " than L2",
+                       "cuda_graph": bool(getattr(model, "_graphs", None)),
                        "arithmetic": "fp16 tensor-core operands, fp32 accumulate, fp32 I/O and LN"},
             "clocks": clocks,
             "e2e": {"value": job_tokens * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",

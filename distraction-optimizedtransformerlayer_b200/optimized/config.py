@@ -56,11 +56,15 @@ _GEMM_MATH_CODE = {"auto": -1, "tf32": 0}
 # activation B*S*d_model is at or under _GRAPH_MAX_ACTIVATION) or "always".
 CUDA_GRAPH = "auto"
 
-# Re-derived for B200. The upstream 524288 was measured on an RTX 3070, where
-# the GPU stopped starving at ~0.5 M activation elements; a B200 finishes the
-# same work ~30x sooner, so launch overhead dominates to much larger shapes.
-# Replay is bit-identical to eager, so the bound only caps the pinned pool.
-_GRAPH_MAX_ACTIVATION = 1 << 27
+# Re-derived for B200. A replay copies x into the graph's input buffer and its
+# output out of the graph's buffer: four passes over the activation in HBM,
+# which buy nothing once the launches are hidden behind a long enough step.
+# Measured on one B200 (bench.py, graph vs eager): config 2 (1 M elements,
+# 77 us per step) needs the graph, eager there is bound by host launch time;
+# configs 3, 4 and 5 (17 M, 67 M, 34 M elements) run 15 %, 20 % and 7 %
+# faster eager (679 vs 778, 1005 vs 1208, 1821 vs 1953 us). Replay is
+# bit-identical to eager.
+_GRAPH_MAX_ACTIVATION = 1 << 22
 _GRAPH_POOL_SAFETY_FRACTION = 0.25
 _GRAPH_MAX_ENTRIES = 4
 _GRAPH_WARMUP_ITERS = 3
