@@ -480,6 +480,8 @@ def _fused_allreduce_roofline(model, dist, dev, T, d, world, reps=20):
 # commands are summarised in profiles/<kernel>_cfg<N>.md.
 TRAFFIC_BYTES = {
     (2, "gemm_ffn_out_residual"): 14_721_536,
+    (4, "ffn_fused"): 403_830_528 + 230_381_056,
+    (4, "gemm_out_proj_ln"): 403_830_784 + 356_402_688,
     (3, "attention"): 107_401_984 + 24_509_184,
     (3, "gemm_ffn_out_ln"): 214_991_104 + 42_022_912,
 }

@@ -449,8 +449,9 @@ def fused_ffn_block(x, attn_out, norm1_w, norm1_b, ffn_in_w, ffn_in_b, ffn_out_w
                     norm2_w, norm2_b, eps) -> List[torch.Tensor]:
     """[x2, normed2] for add+LN -> Linear+GELU -> Linear -> add+LN
     (ffn_block.cuh:270-311 upstream). Covers every shape (the reference
-    declined above d_model 128); runs as LN, two tcgen05 GEMMs with the
-    GELU and residual fused into their epilogues, and a final LN."""
+    declined above d_model 64): LN, then for d_model 128/256 the one-kernel
+    MLP (dotl_ffn), elsewhere two tcgen05 GEMMs with the GELU and residual
+    fused into their epilogues and a final LN."""
     if not x.is_cuda:
         raise RuntimeError("fused_ffn_block: x must be CUDA")
     if x.shape != attn_out.shape:
@@ -464,6 +465,13 @@ def fused_ffn_block(x, attn_out, norm1_w, norm1_b, ffn_in_w, ffn_in_b, ffn_out_w
         raise RuntimeError(f"fused_ffn_block: weight shapes disagree with d_model={D} ffn_dim={F}")
     x1, n1 = layernorm_rows(x.contiguous(), norm1_w.float().contiguous(), norm1_b.float().contiguous(),
                             eps, sub=attn_out.contiguous(), out_half=True)
+    if ffn_supported(D, F):
+        # the MLP and the second LayerNorm in one kernel, the hidden on chip
+        x2 = torch.empty_like(x1)
+        n2 = ffn(n1, _half_weights.get(ffn_in_w), ffn_in_b.float().contiguous(), _half_weights.get(ffn_out_w),
+                 ffn_out_b.float().contiguous(), norm2_w.float().contiguous(), norm2_b.float().contiguous(), eps,
+                 resid=x1, resid_mode=RESID_ADD, x_out=x2)
+        return [x2, n2]
     h = linear_fp16(n1, _half_weights.get(ffn_in_w), ffn_in_b.float().contiguous(), act=1, out_half=True)
     x2 = linear_fp16(h, _half_weights.get(ffn_out_w), ffn_out_b.float().contiguous(), resid=x1,
                      resid_mode=RESID_ADD)

@@ -102,3 +102,29 @@ def test_ffn_rejects(kernels):
         kernels.ffn(a, w1[:96].contiguous(), b1[:96].contiguous(), w2[:, :96].contiguous(), b2, lw, lb, 1e-5)
     with pytest.raises(RuntimeError, match="needs row_valid"):
         kernels.ffn(a, w1, b1, w2, b2, lw, lb, 1e-5, resid=resid, resid_mode=RESID_ADD_MASKALL)
+
+
+@pytest.mark.parametrize("D,Fd", [(256, 1024), (64, 256)])
+def test_reference_fused_ffn_block(kernels, D, Fd):
+    """The reference-named entry point: [x2, LN2(x2)] for x + attn_out -> LN1 ->
+    Linear+GELU -> Linear -> + residual -> LN2 (ffn_block.cuh:270-311 upstream),
+    fp32 weights in; d_model 256 takes the one-kernel MLP, 64 the GEMM path."""
+    g = torch.Generator(device="cuda").manual_seed(D)
+    M = 4096
+    x = torch.randn(M, D, device="cuda", generator=g)
+    attn = torch.randn(M, D, device="cuda", generator=g) * 0.5
+    n1w, n1b = torch.ones(D, device="cuda"), torch.zeros(D, device="cuda")
+    n2w = torch.randn(D, device="cuda", generator=g) * 0.1 + 1.0
+    n2b = torch.randn(D, device="cuda", generator=g) * 0.1
+    w1 = torch.randn(Fd, D, device="cuda", generator=g) * D ** -0.5
+    b1 = torch.randn(Fd, device="cuda", generator=g) * 0.02
+    w2 = torch.randn(D, Fd, device="cuda", generator=g) * Fd ** -0.5
+    b2 = torch.randn(D, device="cuda", generator=g) * 0.02
+    x2, n2 = kernels.fused_ffn_block(x, attn, n1w, n1b, w1, b1, w2, b2, n2w, n2b, 1e-5)
+    x1 = (x + attn).double()
+    a = F.layer_norm(x1, (D,), eps=1e-5).half().double()
+    h = F.gelu(a @ w1.half().double().t() + b1.double(), approximate="none").half().double()
+    rx2 = x1 + h @ w2.half().double().t() + b2.double()
+    rn2 = F.layer_norm(rx2, (D,), n2w.double(), n2b.double(), 1e-5)
+    assert (x2.double() - rx2).abs().max().item() < 1e-3
+    assert (n2.double() - rn2).abs().max().item() < 2e-3
