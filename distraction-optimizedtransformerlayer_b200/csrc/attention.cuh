@@ -615,15 +615,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     }
                 } else {
                     // Some keys masked: two passes of 32 columns (compact code).
+                    // A 32-key block no row of the warp may see (other sequences
+                    // of a packed tile, keys above a causal diagonal) is skipped:
+                    // no scores read, no exponentials, its P written as zeros.
                     float mx8[8];
 #pragma unroll
                     for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
 #pragma unroll 1
                     for (int q4 = 0; q4 < 4; ++q4) {
+                        const uint32_t wq = q4 == 0 ? allow[0] : q4 == 1 ? allow[1] : q4 == 2 ? allow[2] : allow[3];
+                        if (!__any_sync(0xffffffffu, wq != 0u)) continue;
                         uint32_t sr[32];
                         tmem_ld_32x32b_x32(t_s + q4 * 32, sr);
                         tmem_ld_wait(sr);
-                        const uint32_t wq = q4 == 0 ? allow[0] : q4 == 1 ? allow[1] : q4 == 2 ? allow[2] : allow[3];
 #pragma unroll
                         for (int i = 0; i < 32; ++i)
                             mx8[i & 7] = fmaxf(mx8[i & 7], ((wq >> i) & 1u) ? __uint_as_float(sr[i]) : -INFINITY);
@@ -635,9 +639,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll 1
                     for (int q4 = 0; q4 < 4; ++q4) {
                         uint32_t sr[32], pk[16];
+                        const uint32_t wq = q4 == 0 ? allow[0] : q4 == 1 ? allow[1] : q4 == 2 ? allow[2] : allow[3];
+                        if (!__any_sync(0xffffffffu, wq != 0u)) {
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) pk[i] = 0u;
+                            tmem_st_32x32b_x16(t_s + q4 * 16, pk);
+                            continue;
+                        }
                         tmem_ld_32x32b_x32(t_s + q4 * 32, sr);
                         tmem_ld_wait(sr);
-                        const uint32_t wq = q4 == 0 ? allow[0] : q4 == 1 ? allow[1] : q4 == 2 ? allow[2] : allow[3];
 #pragma unroll
                         for (int i = 0; i < 16; ++i) {
                             float p0 = fast_exp2(fmaf(__uint_as_float(sr[2 * i]), c, -mc));
