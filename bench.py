@@ -442,15 +442,17 @@ def _fused_allreduce_roofline(model, dist, dev, T, d, world, reps=20):
     sends per launch: one-shot, every peer reads its whole fp32 partial sum,
     (P-1) T d 4; push, peers read 1/P of it from each rank and each rank
     stores its 1/P of x_new (fp32) and normed (fp16) into every peer,
-    (P-1)/P T d (4 + 6). Against the measured 770 GB/s per direction of a peer
+    (P-1)/P T d (4 + 6); push with the GEMMs scattering their tiles to the
+    row owners, only the stores, (P-1)/P T d 6. Against the measured 770 GB/s per direction of a peer
     copy on this pool."""
     pg = model.peer
     w = model.w
     x = pg.view("xa", T)
+    local = model.scatter is not False and pg.scatter_ok(T)
 
     def once():
         pg.allreduce_ln(x, w["layers.0.bo_full"], w["layers.0.norm2.weight"], w["layers.0.norm2.bias"],
-                        model.eps, "xb", "n16", T)
+                        model.eps, "xb", "n16", T, from_owners=local)
 
     for _ in range(3):
         once()
@@ -464,12 +466,15 @@ def _fused_allreduce_roofline(model, dist, dev, T, d, world, reps=20):
     ev1.record()
     torch.cuda.synchronize(dev)
     ms = max_over_ranks([ev0.elapsed_time(ev1) / reps], dist, dev)[0]
-    if pg.push:
+    if local:
+        nbytes = (world - 1) / world * T * d * 6    # the partial sums crossed inside the GEMMs
+    elif pg.push:
         nbytes = (world - 1) / world * T * d * 10
     else:
         nbytes = (world - 1) * T * d * 4
     achieved = nbytes / (ms / 1e3) / 1e9
-    return {"kernel": "allreduce_ln_" + ("push" if pg.push else "oneshot"), "bound": "nvlink",
+    kind = "push_from_owner_slots" if local else ("push" if pg.push else "oneshot")
+    return {"kernel": "allreduce_ln_" + kind, "bound": "nvlink",
             "achieved": achieved, "peak": 770.0, "unit": "GB/s", "frac": achieved / 770.0,
             "peak_source": "measured peer copy of this pool, per direction per GPU", "traffic": None,
             "nvlink_bytes_per_gpu": nbytes, "ms_per_launch": ms, "launches_per_step": 2}
@@ -533,7 +538,8 @@ def run_ours(args, rank, world, local_rank):
 
         state = {k: v.detach() for k, v in model.state_dict().items()}
         model = TensorParallelTransformer(cfg, state, device=dev, fused=args.tp_impl == "fused",
-                                          push=not args.tp_oneshot)
+                                          push=not args.tp_oneshot,
+                                          scatter=False if args.tp_no_scatter else None)
         args.strong = True
     else:
         model = model.to(dev).eval()
@@ -635,7 +641,10 @@ def run_ours(args, rank, world, local_rank):
                        "seq_len": cfg.seq_len, "layers": cfg.num_layers, "parallelism": f"tp{world}",
                        "l2": "flushed between steps (256 MiB write)", "cuda_graph": False,
                        "arithmetic": "fp16 tensor-core operands, fp32 accumulate, fp32 partial sums all-reduced",
-                       "allreduce": ("dotl_allreduce_ln over peer memory, " + ("push" if model.peer.push else "one-shot"))
+                       "allreduce": ("dotl_allreduce_ln over peer memory, " + ("push" if model.peer.push else "one-shot")
+                                     + (", GEMM tiles scattered to the row owners by dotl_linear_peer"
+                                        if model.scatter is not False and model.peer.scatter_ok(x.numel() // cfg.d_model)
+                                        else ""))
                        if model.fused else "NCCL all_reduce + LayerNorm kernel"},
             "clocks": clocks,
             "e2e": {"value": job_tokens * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
@@ -736,6 +745,8 @@ def main() -> int:
                     help="--tp: each all-reduce + add + LayerNorm as one peer-memory kernel, or NCCL + LN")
     ap.add_argument("--tp-oneshot", action="store_true",
                     help="--tp fused: one-shot mode (every rank reduces every row)")
+    ap.add_argument("--tp-no-scatter", action="store_true",
+                    help="--tp fused push: row-parallel GEMMs write locally (no scatter to the row owners)")
     ap.add_argument("--strong", action="store_true",
                     help="split the config's batch across ranks (strong scaling) instead of a full batch per rank")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -153,11 +153,13 @@ int encode_f16_map(CUtensorMap* map, const void* base, int rank, const cuuint64_
 
 // ------------------------------------------------------------------ GEMM --
 
-template <int BN, int STAGES, bool OUT_F16, bool SPLIT2 = false>
+template <int BN, int STAGES, bool OUT_F16, bool SPLIT2 = false, bool PEER = false>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const dotl::GemmParams& p,
-                int dev, cudaStream_t stream) {
+                int dev, cudaStream_t stream, const dotl::GemmPeerOut* po_in = nullptr) {
     using L = dotl::GemmSmem<BN, STAGES>;
-    auto kernel = dotl::gemm_tc_kernel<BN, STAGES, OUT_F16, SPLIT2>;
+    auto kernel = dotl::gemm_tc_kernel<BN, STAGES, OUT_F16, SPLIT2, PEER>;
+    static const dotl::GemmPeerOut kNoPeers = {};
+    const dotl::GemmPeerOut& po = po_in != nullptr ? *po_in : kNoPeers;
     static bool done[kMaxDevices] = {false};
     if (int rc = ensure_smem(kernel, L::kAlloc, dev, done)) return rc;
     const int tiles = p.num_m_tiles * p.num_n_tiles;
@@ -179,10 +181,10 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap&
         attr[1].val.clusterDim.z = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 2;
-        e = cudaLaunchKernelEx(&cfg, kernel, ta, tw, to, p);
+        e = cudaLaunchKernelEx(&cfg, kernel, ta, tw, to, p, po);
     } else {
         const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
-        e = launch_pdl(kernel, dim3(grid), dim3(dotl::kGemmThreads), L::kAlloc, stream, ta, tw, to, p);
+        e = launch_pdl(kernel, dim3(grid), dim3(dotl::kGemmThreads), L::kAlloc, stream, ta, tw, to, p, po);
     }
     if (e != cudaSuccess) return fail(DOTL_ECUDA, "dotl_linear: launch failed: %s", cudaGetErrorString(e));
     return check_launch("dotl_linear");
@@ -531,6 +533,54 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
                                  : launch_gemm<128, 5, false>(ta, tw, to, p, dev, s);
 }
 
+int dotl_linear_peer(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,
+                     const float* bias, int world, void* const* outs, int64_t rows_per_rank, int64_t ldo,
+                     void* stream) {
+    const char* who = "dotl_linear_peer";
+    if (world < 1 || world > dotl::kGemmPeerMax) return fail(DOTL_EINVAL, "%s: world %d outside 1..%d", who, world, dotl::kGemmPeerMax);
+    if (M < 0 || N <= 0 || K <= 0 || M > (int64_t)0x7fffffff - 256 || N > 0x7fffffff || K > 0x7fffffff)
+        return fail(DOTL_EINVAL, "%s: bad shape M=%lld N=%lld K=%lld", who, (long long)M, (long long)N, (long long)K);
+    if (rows_per_rank <= 0 || rows_per_rank % dotl::kGemmBM != 0 || M != rows_per_rank * world)
+        return fail(DOTL_EUNSUPPORTED, "%s: M=%lld must be world x rows_per_rank with rows_per_rank a multiple of 128",
+                    who, (long long)M);
+    if (a == nullptr || w == nullptr || outs == nullptr) return fail(DOTL_EINVAL, "%s: NULL pointer", who);
+    if (K % 8 != 0 || lda % 8 != 0 || ldw % 8 != 0 || lda < K || ldw < K)
+        return fail(DOTL_EUNSUPPORTED, "%s: K, lda and ldw must be multiples of 8", who);
+    if (!aligned16(a) || !aligned16(w) || !aligned16(bias)) return fail(DOTL_EUNSUPPORTED, "%s: a, w and bias must be 16-byte aligned", who);
+    if (N % 8 != 0 || ldo < N || ldo % 4 != 0) return fail(DOTL_EUNSUPPORTED, "%s: N %% 8 == 0 and ldo >= N, ldo %% 4 == 0", who);
+    dotl::GemmPeerOut po = {};
+    po.rows = static_cast<int>(rows_per_rank);
+    for (int r = 0; r < world; ++r) {
+        if (outs[r] == nullptr || !aligned16(outs[r])) return fail(DOTL_EINVAL, "%s: outs[%d] NULL or unaligned", who, r);
+        if (int rc = encode_out_map(&po.map[r], outs[r], rows_per_rank, N, ldo, DOTL_F32, who)) return rc;
+    }
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    const int bn = pick_tile_n(M, N, K, sm_count(dev));
+    CUtensorMap ta, tw;
+    const cuuint64_t adims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+    const cuuint64_t astr[1] = {static_cast<cuuint64_t>(lda) * 2};
+    if (int rc = encode_f16_map(&ta, a, 2, adims, astr, dotl::kGemmBK, dotl::kGemmBM, who)) return rc;
+    const cuuint64_t wdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
+    const cuuint64_t wstr[1] = {static_cast<cuuint64_t>(ldw) * 2};
+    if (int rc = encode_f16_map(&tw, w, 2, wdims, wstr, dotl::kGemmBK, static_cast<uint32_t>(bn), who)) return rc;
+    dotl::GemmParams p = {};
+    p.M = static_cast<int>(M);
+    p.N = static_cast<int>(N);
+    p.K = static_cast<int>(K);
+    p.num_m_tiles = static_cast<int>(M / dotl::kGemmBM);
+    p.num_n_tiles = static_cast<int>((N + bn - 1) / bn);
+    p.bias = bias;
+    p.resid_mode = DOTL_RESID_NONE;
+    p.act = 0;
+    p.out = outs[0];
+    p.ldo = ldo;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (bn == 256) return launch_gemm<256, 4, false, false, true>(ta, tw, po.map[0], p, dev, s, &po);
+    if (bn == 64) return launch_gemm<64, 7, false, false, true>(ta, tw, po.map[0], p, dev, s, &po);
+    return launch_gemm<128, 5, false, false, true>(ta, tw, po.map[0], p, dev, s, &po);
+}
+
 int dotl_linear_ln(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,
                    const float* bias, const float* resid, int64_t ldr, const uint8_t* row_valid, int resid_mode,
                    float* out, int64_t ldo, const float* ln_weight, const float* ln_bias, float eps, void* normed,
@@ -872,7 +922,7 @@ int dotl_peer_signal_bytes(int blocks, int64_t* bytes) {
 }
 
 int dotl_allreduce_ln(int world, int rank, const float* const* parts, void* const* signals, float* const* x_new,
-                      void* const* normed, int normed_dtype, int push, const float* x, const float* bias,
+                      void* const* normed, int normed_dtype, int push, int parts_local, const float* x, const float* bias,
                       const uint8_t* sum_row_valid, const float* ln_weight, const float* ln_bias, float eps,
                       const uint8_t* normed_row_valid, int64_t rows, int64_t D, int blocks, int timeout_ms,
                       void* stream) {
@@ -885,6 +935,7 @@ int dotl_allreduce_ln(int world, int rank, const float* const* parts, void* cons
     if (normed_dtype != DOTL_F32 && normed_dtype != DOTL_F16)
         return fail(DOTL_EINVAL, "%s: normed dtype must be DOTL_F32 or DOTL_F16", who);
     if (timeout_ms < 1 || timeout_ms > 60000) return fail(DOTL_EINVAL, "%s: timeout_ms must be in 1..60000", who);
+    if (parts_local && !push) return fail(DOTL_EINVAL, "%s: parts_local needs push mode (each rank reduces its own rows)", who);
     if (parts == nullptr || signals == nullptr || normed == nullptr || x == nullptr || ln_weight == nullptr ||
         ln_bias == nullptr)
         return fail(DOTL_EINVAL, "%s: NULL pointer", who);
@@ -924,6 +975,7 @@ int dotl_allreduce_ln(int world, int rank, const float* const* parts, void* cons
     p.world = world;
     p.rank = rank;
     p.push = push ? 1 : 0;
+    p.parts_local = parts_local ? 1 : 0;
     p.timeout_ns = static_cast<unsigned long long>(timeout_ms) * 1000000ull;
     const dim3 grid(static_cast<unsigned>(blocks)), block(dotl::kPeerWarps * 32);
     cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -52,6 +52,16 @@ struct GemmParams {
     int64_t ldo;
 };
 
+// Output tiles scattered over the ranks of a tensor-parallel group: row block
+// m (rows [128 m, 128 m + 128)) belongs to rank (128 m) / rows, which receives
+// it at row 128 m - rank * rows of map[rank] (its receive slot for this rank,
+// in its own memory, reached over NVLink). Plain TMA stores: no multicast.
+constexpr int kGemmPeerMax = 8;
+struct GemmPeerOut {
+    CUtensorMap map[kGemmPeerMax];
+    int rows;                // rows per rank; 0: the ordinary output map
+};
+
 template <int BN, int STAGES>
 struct GemmSmem {
     static constexpr uint32_t kBTileBytes = BN * kGemmBK * 2;
@@ -193,10 +203,11 @@ mma_done:
 // own half as partial_0 + partial_1 (one fp32 add, which commutes: both CTAs
 // and every run give the same bits). Used when a problem has too few tiles
 // to fill the SMs with long K.
-template <int BN, int STAGES, bool OUT_F16, bool SPLIT2 = false>
+template <int BN, int STAGES, bool OUT_F16, bool SPLIT2 = false, bool PEER = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
-                   const __grid_constant__ CUtensorMap tmap_out, const GemmParams p) {
+                   const __grid_constant__ CUtensorMap tmap_out, const GemmParams p,
+                   const __grid_constant__ GemmPeerOut po) {
     using L = GemmSmem<BN, STAGES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -232,6 +243,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tma_prefetch_map(&tmap_a);
         tma_prefetch_map(&tmap_w);
         tma_prefetch_map(&tmap_out);
+        if constexpr (PEER)
+            for (int r = 0; r * po.rows < p.M && r < kGemmPeerMax; ++r) tma_prefetch_map(&po.map[r]);
     }
     if constexpr (SPLIT2) cluster_sync_after_init();
     pdl_wait();
@@ -290,8 +303,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             // still runs).
             float4 rr[kCW / 4];
             auto load_bias = [&](int nc) -> float {
-                return nc + lane < p.N ? __ldg(p.bias + nc + lane) : 0.0f;
+                return (p.bias != nullptr && nc + lane < p.N) ? __ldg(p.bias + nc + lane) : 0.0f;
             };
+            // where this tile's rows go: the output map, or the owning rank's
+            const CUtensorMap* omap = &tmap_out;
+            int orow = m_blk * kGemmBM;
+            if constexpr (PEER) {
+                const int owner = orow / po.rows;
+                omap = &po.map[owner];
+                orow -= owner * po.rows;
+            }
             auto load_resid = [&](int nc) {
                 if (has_resid && row_ok && nc + kCW <= p.N) {
                     const float4* rp = reinterpret_cast<const float4*>(p.resid + static_cast<int64_t>(row) * p.ldr + nc);
@@ -431,7 +452,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) {
-                        tma_store_2d(&tmap_out, stage_addr + sb, nc, m_blk * kGemmBM + quarter * 32);
+                        tma_store_2d(omap, stage_addr + sb, nc, orow + quarter * 32);
                         bulk_commit();
                     }
                     ++nstore;

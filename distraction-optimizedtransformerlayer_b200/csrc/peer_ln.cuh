@@ -20,7 +20,10 @@
 //      normed = LN(x_new) * w + b (0 on rows that normed_row_valid marks);
 //      one-shot mode: every rank does every row and writes only locally;
 //      push mode: rank r does rows [r C, (r+1) C) and stores x_new / normed
-//      into every rank's output buffers;
+//      into every rank's output buffers; with parts_local, the row-parallel
+//      GEMMs have already scattered their tiles to the row owners
+//      (dotl_linear_peer), so rank r's partial sums of its rows are read
+//      from slots in its own memory and only the results cross NVLink;
 //   3. end barrier: the same handshake again, after which no peer still reads
 //      this rank's partial sums or still writes into its outputs.
 // Flags carry a per-CTA call counter (kept in the rank's own signal area), so
@@ -69,6 +72,7 @@ struct PeerLnParams {
     int world;
     int rank;
     int push;
+    int parts_local;               // part[i]: rows [lo, hi) of rank i's partial sums, in this rank's memory
     unsigned long long timeout_ns;
 };
 
@@ -133,13 +137,16 @@ __global__ void __launch_bounds__(kPeerWarps * 32, kPeerBlocksPerSm) allreduce_l
     const float inv_d = 1.0f / static_cast<float>(D);
     for (int64_t row = lo + warp0; row < hi; row += nwarps) {
         const int64_t base = row * D;
+        // rank src's partial sums of this row: its buffer over NVLink, or (when
+        // the GEMMs scattered their tiles to the row owners) this rank's slot
+        const int64_t pbase = p.parts_local ? (row - lo) * D : base;
         float4 s[EPL / 4];
-        // partial sums in rank order, local or over NVLink (L2-only loads:
-        // peer data is never cached in L1)
+        // partial sums in rank order (L2-only loads: peer data is never
+        // cached in L1)
 #pragma unroll
         for (int i = 0; i < EPL / 4; ++i) {
             const int c = (i * 32 + lane) * 4;
-            s[i] = c < D ? __ldcg(reinterpret_cast<const float4*>(p.part[0] + base + c))
+            s[i] = c < D ? __ldcg(reinterpret_cast<const float4*>(p.part[0] + pbase + c))
                          : make_float4(0.f, 0.f, 0.f, 0.f);
         }
         for (int src = 1; src < p.world; ++src) {
@@ -147,7 +154,7 @@ __global__ void __launch_bounds__(kPeerWarps * 32, kPeerBlocksPerSm) allreduce_l
             for (int i = 0; i < EPL / 4; ++i) {
                 const int c = (i * 32 + lane) * 4;
                 if (c < D) {
-                    const float4 t = __ldcg(reinterpret_cast<const float4*>(p.part[src] + base + c));
+                    const float4 t = __ldcg(reinterpret_cast<const float4*>(p.part[src] + pbase + c));
                     s[i].x += t.x; s[i].y += t.y; s[i].z += t.z; s[i].w += t.w;
                 }
             }

@@ -11,6 +11,8 @@ their CUDA IPC handles through the process group (all_gather_object) and
 maps every peer's with `dotl_ipc_open`:
 
     part      fp32 [rows, d]  the rank's partial sums (a row-parallel GEMM writes here)
+    recv      fp32 [rows, d]  slots [world][rows / world, d]: every rank's partial sums of
+                              this rank's rows, stored there by dotl_linear_peer
     xa, xb    fp32 [rows, d]  residual stream, ping-pong
     n16       fp16 [rows, d]  LayerNorm output feeding the next GEMM
     out       fp32 [rows, d]  the final LayerNorm output
@@ -33,7 +35,7 @@ from typing import Dict, List, Optional
 
 import torch
 
-_NAMES = ("part", "xa", "xb", "n16", "out")
+_NAMES = ("part", "recv", "xa", "xb", "n16", "out")
 
 
 class _DeviceView:
@@ -106,7 +108,7 @@ class PeerGroup:
     def allreduce_ln(self, x: torch.Tensor, bias: Optional[torch.Tensor], ln_w: torch.Tensor,
                      ln_b: torch.Tensor, eps: float, x_new: Optional[str], normed: str, rows: int,
                      sum_row_valid: Optional[torch.Tensor] = None,
-                     normed_row_valid: Optional[torch.Tensor] = None) -> None:
+                     normed_row_valid: Optional[torch.Tensor] = None, from_owners: bool = False) -> None:
         """x_new := x + valid * (sum over ranks of `part` + bias); normed := LN(x_new).
 
         x is this rank's residual (a [rows, d] fp32 tensor, the same values on
@@ -119,11 +121,31 @@ class PeerGroup:
         dsts = range(self.world) if self.push else (self.rank,)
         mask = [r in dsts for r in range(self.world)]
         pick = lambda n: [p if m else None for p, m in zip(self.ptrs[n], mask)]  # noqa: E731
+        if from_owners:
+            # the GEMMs left rank s's partial sums of this rank's rows in slot s
+            per = rows // self.world
+            base = self.ptrs["recv"][self.rank]
+            parts = [base + s * per * self.d * 4 for s in range(self.world)]
+        else:
+            parts = self.ptrs["part"]
         self.k.allreduce_ln(
-            self.world, self.rank, self.ptrs["part"], self.ptrs["signal"],
+            self.world, self.rank, parts, self.ptrs["signal"],
             None if x_new is None else pick(x_new), pick(normed), normed == "n16", self.push,
             x, bias, ln_w, ln_b, eps, sum_row_valid, normed_row_valid, rows, self.d, self.blocks,
-            self.timeout_ms)
+            self.timeout_ms, parts_local=from_owners)
+
+    def scatter_ok(self, rows: int) -> bool:
+        """Whether row-parallel GEMMs over `rows` rows can scatter their tiles
+        to the row owners (dotl_linear_peer): push mode, and 128-row blocks
+        that never straddle two ranks."""
+        return self.push and rows <= self.rows and rows % (128 * self.world) == 0
+
+    def gemm_to_owners(self, a16: torch.Tensor, w16: torch.Tensor, rows: int) -> None:
+        """part = a16 @ w16^T, each 128-row tile stored into the `recv` slot
+        (this rank's) of the rank that owns its rows."""
+        per = rows // self.world
+        slot = self.rank * per * self.d * 4
+        self.k.linear_peer(a16, w16, None, [p + slot for p in self.ptrs["recv"]], per, self.d)
 
     def _release(self) -> None:
         for p in self._opened:

@@ -114,7 +114,7 @@ class TensorParallelTransformer:
     def __init__(self, config, state_dict: Dict[str, torch.Tensor], group=None,
                  device: Optional[torch.device] = None, eps: float = 1e-5,
                  fused: Optional[bool] = None, push: Optional[bool] = None,
-                 timeout_ms: int = 2000) -> None:
+                 timeout_ms: int = 2000, scatter: Optional[bool] = None) -> None:
         import torch.distributed as dist
 
         self.dist = dist
@@ -135,6 +135,7 @@ class TensorParallelTransformer:
         if fused is None:
             fused = d % 4 == 0 and d <= 2048 and world <= 8
         self.fused, self.push, self.timeout_ms = bool(fused), push, timeout_ms
+        self.scatter = scatter   # None: wherever the rows allow it
         self.peer = None
         if self.fused:
             # the fused reduction adds the full biases itself; the GEMMs get zeros
@@ -180,6 +181,16 @@ class TensorParallelTransformer:
         hd, hl = plan.head_dim, plan.local_heads
         bufs = {n: pg.view(n, T) for n in ("part", "xa", "xb", "n16", "out")}
         part, n16 = bufs["part"], bufs["n16"]
+        # the row-parallel GEMMs scatter their tiles to the row owners while they
+        # run (the reduce-scatter inside the GEMM), or write locally for the
+        # reduction kernel to pull
+        scatter = self.scatter is not False and pg.scatter_ok(T)
+
+        def row_parallel(a16, w16):
+            if scatter:
+                pg.gemm_to_owners(a16, w16, T)
+            else:
+                k.linear_fp16(a16, w16, w["zero_d"], out=part)
         bufs["xa"].copy_(x.reshape(T, d))
         k.layernorm_rows(bufs["xa"], w["layers.0.norm1.weight"], w["layers.0.norm1.bias"], self.eps, out=n16)
         cur, alt = "xa", "xb"
@@ -188,16 +199,16 @@ class TensorParallelTransformer:
             qkv = k.linear_fp16(n16.view(B, S, d), w[p + "wqkv"], w[p + "bqkv"], out_half=True)
             q, kk, v = qkv.view(B, S, 3, hl, hd).permute(2, 0, 3, 1, 4).unbind(0)
             ctx = k.attention_packed(q, kk, v, cfg.causal, hd ** -0.5, key_mask=mask)
-            k.linear_fp16(ctx.reshape(T, -1), w[p + "wo"], w["zero_d"], out=part)
+            row_parallel(ctx.reshape(T, -1), w[p + "wo"])
             pg.allreduce_ln(bufs[cur], w[p + "bo_full"], w[p + "norm2.weight"], w[p + "norm2.bias"], self.eps,
-                            alt, "n16", T, sum_row_valid=rv)
+                            alt, "n16", T, sum_row_valid=rv, from_owners=scatter)
             h = k.linear_fp16(n16, w[p + "w1"], w[p + "b1"], act=1, out_half=True)
-            k.linear_fp16(h, w[p + "w2"], w["zero_d"], out=part)
+            row_parallel(h, w[p + "w2"])
             last = i == cfg.num_layers - 1
             nn_ = "final_norm." if last else f"layers.{i + 1}.norm1."
             pg.allreduce_ln(bufs[alt], w[p + "b2_full"], w[nn_ + "weight"], w[nn_ + "bias"], self.eps,
                             None if last else cur, "out" if last else "n16", T, sum_row_valid=rv,
-                            normed_row_valid=rv if last else None)
+                            normed_row_valid=rv if last else None, from_owners=scatter)
         return bufs["out"].view(B, S, d)
 
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:

@@ -182,6 +182,25 @@ int dotl_peer_blocks(int* blocks);
 int dotl_peer_signal_bytes(int blocks, int64_t* bytes);
 
 /*
+ * dotl_linear (fp32 out, optional bias, no residual or activation) whose
+ * output tiles go to the rank that owns their rows, for the row-parallel GEMMs
+ * of the tensor-parallel layer: row block m goes to rank (128 m) / rows_per_rank,
+ * at row 128 m - rank * rows_per_rank of outs[rank]. outs[i] is this rank's
+ * receive slot on rank i (peer-mapped with dotl_ipc_open; outs[own rank] its own
+ * memory). The stores are TMA bulk stores over NVLink, issued from the GEMM's
+ * epilogue while its tensor cores run the next tile: the reduce-scatter of
+ * all_reduce(part) (optimized/layers.py:241-243, 258-261 on one GPU) moves
+ * inside the GEMM, and dotl_allreduce_ln (parts_local = 1) finishes the
+ * reduction from local memory. M = world * rows_per_rank, rows_per_rank % 128
+ * == 0, world <= 8; other requirements as dotl_linear. The receive slots must
+ * not be read until every rank's GEMM is complete (dotl_allreduce_ln's start
+ * handshake ensures it).
+ */
+int dotl_linear_peer(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,
+                     const float* bias, int world, void* const* outs, int64_t rows_per_rank, int64_t ldo,
+                     void* stream);
+
+/*
  * Sum over the ranks of fp32 partial sums + bias + residual + LayerNorm, in one
  * kernel over peer memory. Replaces all_reduce(part) followed by
  * fused_add_layernorm (add_layernorm.cuh:663-672) after each row-parallel GEMM
@@ -196,14 +215,17 @@ int dotl_peer_signal_bytes(int blocks, int64_t* bytes);
  * dotl_peer_signal_bytes(blocks). push = 0: this rank computes every row and
  * writes only x_new[rank] / normed[rank]. push = 1: rank r computes rows
  * [r*ceil(rows/world), ...) and writes them into every rank's outputs (which
- * must then be peer-mapped too). Every rank must make the same calls with the
+ * must then be peer-mapped too). parts_local = 1 (push only): parts[i] is instead
+ * this rank's own slot holding rank i's partial sums of this rank's rows (row
+ * r0 of the slice at offset 0), as dotl_linear_peer leaves them, so only the
+ * results cross NVLink. Every rank must make the same calls with the
  * same rows, D, push and blocks, in the same order. A wait for a peer longer than
  * timeout_ms sets bit 4 of the device error word and ends the call's work; the
  * group's counters then disagree and it must be rebuilt. D % 4 == 0, D <= 2048,
  * world <= 8, all pointers 16-byte aligned.
  */
 int dotl_allreduce_ln(int world, int rank, const float* const* parts, void* const* signals, float* const* x_new,
-                      void* const* normed, int normed_dtype, int push, const float* x, const float* bias,
+                      void* const* normed, int normed_dtype, int push, int parts_local, const float* x, const float* bias,
                       const uint8_t* sum_row_valid, const float* ln_weight, const float* ln_bias, float eps,
                       const uint8_t* normed_row_valid, int64_t rows, int64_t D, int blocks, int timeout_ms,
                       void* stream);

@@ -116,8 +116,8 @@ def test_allreduce_ln_rejects(lib):
     P2 = ctypes.c_void_p * 2
     parts, sigs, outs = P2(16, 32), P2(48, 64), P2(80, 96)
 
-    def call(world=2, rank=0, D=128, dtype=0, timeout=2000, p=parts):
-        return lib.dotl_allreduce_ln(world, rank, p, sigs, None, outs, dtype, 0, 16, None, None, 16, 16,
+    def call(world=2, rank=0, D=128, dtype=0, timeout=2000, p=parts, local=0):
+        return lib.dotl_allreduce_ln(world, rank, p, sigs, None, outs, dtype, 0, local, 16, None, None, 16, 16,
                                      1e-5, None, 8, D, 1, timeout, None)
 
     assert call(world=9) == 1 and "world" in _err(lib)
@@ -128,6 +128,17 @@ def test_allreduce_ln_rejects(lib):
     assert call(timeout=0) == 1 and "timeout_ms" in _err(lib)
     assert call(p=P2(16, None)) == 1 and "NULL" in _err(lib)
     assert call(p=P2(16, 40)) == 1 and "aligned" in _err(lib)
+    assert call(local=1) == 1 and "push" in _err(lib)
+
+
+def test_linear_peer_rejects(lib):
+    P2 = ctypes.c_void_p * 2
+    outs = P2(256, 512)
+    # M must be world x rows_per_rank with rows_per_rank a multiple of 128
+    assert lib.dotl_linear_peer(16, 300, 64, 64, 16, 64, 64, None, 2, outs, 150, 64, None) == 2
+    assert "rows_per_rank" in _err(lib)
+    assert lib.dotl_linear_peer(16, 256, 64, 64, 16, 64, 64, None, 9, outs, 128, 64, None) == 1
+    assert lib.dotl_linear_peer(16, 256, 60, 64, 16, 64, 64, None, 2, outs, 128, 64, None) == 2
 
 
 def test_peer_setup_rejects_and_sizes(lib):

@@ -1,6 +1,7 @@
 """Tensor-parallel layer on 2 GPUs against the oracle (gpu), with each
-all-reduce + add + LayerNorm either fused over peer memory (one-shot and push
-modes of dotl_allreduce_ln) or as NCCL all-reduce + the LayerNorm kernel.
+all-reduce + add + LayerNorm either fused over peer memory (push mode, the
+row-parallel GEMMs scattering their tiles to the row owners where the rows
+allow it, or not; one-shot mode) or as NCCL all-reduce + the LayerNorm kernel.
 
 Runs only where at least two GPUs are visible; the CPU decomposition test in
 test_tensor_parallel_gloo.py covers the sharding everywhere, and
@@ -44,7 +45,8 @@ def _worker(rank, world, port, path, case, mode):
         cfg = O.TransformerConfig(B, S, d, H, Fd, L, causal)
         params = O.init_params(cfg, 21)
         x, mask = O.generate_random_case(cfg, 22, pad, 1.0)
-        tp = TensorParallelTransformer(cfg, params, fused=mode != "nccl", push=mode == "push")
+        tp = TensorParallelTransformer(cfg, params, fused=mode != "nccl", push=mode.startswith("push"),
+                                       scatter=False if mode == "push_noscatter" else None)
         try:
             with torch.inference_mode():
                 out = tp(x.cuda(), mask.cuda() if pad > 0 else None).cpu()
@@ -61,7 +63,7 @@ def _worker(rank, world, port, path, case, mode):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["oneshot", "push", "nccl"])
+@pytest.mark.parametrize("mode", ["push", "push_noscatter", "oneshot", "nccl"])
 @pytest.mark.parametrize("case", [(2, 256, 512, 8, 1024, 1, True, 0.0),
                                   (2, 192, 256, 4, 512, 2, False, 0.5),
                                   (1, 512, 1024, 8, 2048, 1, True, 0.0)])

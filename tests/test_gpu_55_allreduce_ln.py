@@ -192,3 +192,46 @@ def test_rejects(kernels):
         call(parts=[None])
     torch.cuda.synchronize()
     assert torch.isnan(out).all()   # a rejected call enqueues nothing
+
+
+@pytest.mark.parametrize("world", [1, 2, 4])
+def test_gemm_scatters_tiles_to_row_owners(kernels, world):
+    """dotl_linear_peer with every "rank's" receive slot a local buffer: rows
+    [r R, (r+1) R) land in slot r at offset 0, with the bits of dotl_linear."""
+    k = kernels
+    R, K, N = 256, 512, 384
+    g = torch.Generator(device="cuda").manual_seed(world)
+    a = torch.randn(world * R, K, device="cuda", generator=g).half()
+    w = (torch.randn(N, K, device="cuda", generator=g) * K ** -0.5).half()
+    slots = [torch.full((R, N), float("nan"), device="cuda") for _ in range(world)]
+    k.linear_peer(a, w, None, [t.data_ptr() for t in slots], R, N)
+    ref = k.linear_fp16(a, w, torch.zeros(N, device="cuda"))
+    torch.cuda.synchronize()
+    for r in range(world):
+        assert torch.equal(slots[r] + 0.0, ref[r * R:(r + 1) * R] + 0.0), r
+
+
+def test_reduction_from_owner_slots(kernels):
+    """parts_local: the partial sums of this rank's rows come from its own
+    slots (row lo at offset 0), results pushed to every rank's buffers."""
+    k = kernels
+    world, rank, rows, D = 2, 1, 512, 256
+    lo, hi = 256, 512
+    g = torch.Generator(device="cuda").manual_seed(8)
+    x = torch.randn(rows, D, device="cuda", generator=g)
+    slots = [torch.randn(hi - lo, D, device="cuda", generator=g) for _ in range(world)]
+    bias = torch.randn(D, device="cuda", generator=g) * 0.1
+    w, b = torch.ones(D, device="cuda"), torch.zeros(D, device="cuda")
+    blocks, sig = _signals(k, world, rank, True)
+    x_new = [torch.full((rows, D), float("nan"), device="cuda") for _ in range(world)]
+    normed = [torch.full((rows, D), float("nan"), device="cuda", dtype=torch.float16) for _ in range(world)]
+    k.allreduce_ln(world, rank, [t.data_ptr() for t in slots], [s.data_ptr() for s in sig],
+                   [t.data_ptr() for t in x_new], [t.data_ptr() for t in normed], True, True, x, bias, w, b,
+                   1e-5, None, None, rows, D, blocks, 2000, parts_local=True)
+    torch.cuda.synchronize()
+    ref_x = x[lo:hi] + ((slots[0] + slots[1]) + bias)
+    ref_y = torch.nn.functional.layer_norm(ref_x.double(), (D,), eps=1e-5)
+    for i in range(world):
+        assert torch.equal(x_new[i][lo:hi], ref_x)
+        assert (normed[i][lo:hi].double() - ref_y).abs().max().item() < 4e-3
+        assert torch.isnan(x_new[i][:lo]).all()
