@@ -72,10 +72,9 @@ struct FfnSmem {
     static constexpr uint32_t kStageWarpBytes = 4096 + 2048;
     static constexpr uint32_t kOffStage = kOffStats + 2 * 2 * kGemmBM * 8;
     static constexpr uint32_t kOffBar = kOffStage + 8 * kStageWarpBytes;
-    // a_full, a_empty, w_full[S], w_empty[S], acc1_full[2], (unused)[2],
-    // h_full[2], g2_done[2], acc2_full, acc2_empty, stats[2 parity][4 quarters], drain,
-    // resid_full[8 warps]
-    static constexpr int kNumBars = 2 + 2 * kStages + 8 + 2 + 8 + 1 + 8;
+    // a_full, a_empty, w_full[S], w_empty[S], acc1_full[2], h_full[2], g2_done[2],
+    // acc2_full, acc2_empty, stats[2 parity][4 quarters], drain, resid_full[8 warps]
+    static constexpr int kNumBars = 2 + 2 * kStages + 6 + 2 + 8 + 1 + 8;
     static constexpr uint32_t kOffSlot = kOffBar + kNumBars * 8;
     static constexpr uint32_t kOffAbort = kOffSlot + 4;
     static constexpr uint32_t kBytes = kOffAbort + 4;
@@ -93,16 +92,15 @@ struct FfnBars {
     __device__ __forceinline__ uint32_t w_full(int s) const { return bar0 + 8u * (2 + s); }
     __device__ __forceinline__ uint32_t w_empty(int s) const { return bar0 + 8u * (2 + L::kStages + s); }
     __device__ __forceinline__ uint32_t acc1_full(int b) const { return bar0 + 8u * (2 + 2 * L::kStages + b); }
-    __device__ __forceinline__ uint32_t acc1_empty(int b) const { return bar0 + 8u * (4 + 2 * L::kStages + b); }
-    __device__ __forceinline__ uint32_t h_full(int b) const { return bar0 + 8u * (6 + 2 * L::kStages + b); }
-    __device__ __forceinline__ uint32_t g2_done(int b) const { return bar0 + 8u * (8 + 2 * L::kStages + b); }
-    __device__ __forceinline__ uint32_t acc2_full() const { return bar0 + 8u * (10 + 2 * L::kStages); }
-    __device__ __forceinline__ uint32_t acc2_empty() const { return bar0 + 8u * (11 + 2 * L::kStages); }
+    __device__ __forceinline__ uint32_t h_full(int b) const { return bar0 + 8u * (4 + 2 * L::kStages + b); }
+    __device__ __forceinline__ uint32_t g2_done(int b) const { return bar0 + 8u * (6 + 2 * L::kStages + b); }
+    __device__ __forceinline__ uint32_t acc2_full() const { return bar0 + 8u * (8 + 2 * L::kStages); }
+    __device__ __forceinline__ uint32_t acc2_empty() const { return bar0 + 8u * (9 + 2 * L::kStages); }
     __device__ __forceinline__ uint32_t stats(int par, int q) const {
-        return bar0 + 8u * (12 + 2 * L::kStages + par * 4 + q);
+        return bar0 + 8u * (10 + 2 * L::kStages + par * 4 + q);
     }
-    __device__ __forceinline__ uint32_t drain() const { return bar0 + 8u * (20 + 2 * L::kStages); }
-    __device__ __forceinline__ uint32_t resid_full(int w) const { return bar0 + 8u * (21 + 2 * L::kStages + w); }
+    __device__ __forceinline__ uint32_t drain() const { return bar0 + 8u * (18 + 2 * L::kStages); }
+    __device__ __forceinline__ uint32_t resid_full(int w) const { return bar0 + 8u * (19 + 2 * L::kStages + w); }
 };
 
 // The W ring in consumption order: per 128-row block, G1(0), G1(1) [W1 chunk
@@ -149,7 +147,6 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(bars.acc1_full(b), 1);
-            mbar_init(bars.acc1_empty(b), 1);
             mbar_init(bars.h_full(b), 256);
             mbar_init(bars.g2_done(b), 1);
         }
