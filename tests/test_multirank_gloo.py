@@ -107,3 +107,45 @@ def test_settle_runs_the_same_steps_on_every_rank(tmp_path):
                        start_method="spawn", join=True)
     counts = torch.load(path)
     assert counts[0] == counts[1] and counts[0] > 1
+
+
+def _dropout_worker(rank, world, port, result_dir):
+    import datetime
+    import time
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    t = torch.ones(4)
+    dist.all_reduce(t)                       # one collective that everyone joins
+    if rank == 1:
+        # this rank leaves between steps, with nothing in flight
+        with open(os.path.join(result_dir, "left"), "w") as f:
+            f.write("1")
+        os._exit(0)
+    t0 = time.monotonic()
+    err = ""
+    try:
+        dist.all_reduce(t)                   # its partner never joins this one
+    except Exception as exc:  # noqa: BLE001 - any backend error ends the wait
+        err = type(exc).__name__
+    with open(os.path.join(result_dir, "rank0"), "w") as f:
+        f.write(f"{err}\n{time.monotonic() - t0:.2f}")
+    os._exit(0)
+
+
+def test_rank_that_leaves_ends_the_next_collective_with_an_error(tmp_path):
+    """Failure detection on the host: a rank that exits between steps makes the
+    other rank's next collective end with an error within the process group's
+    short timeout instead of waiting forever (no GPU involved)."""
+    ctx = mp.start_processes(_dropout_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2,
+                             start_method="spawn", join=False)
+    import time
+
+    deadline = time.monotonic() + 60
+    while not ctx.join(timeout=1):
+        assert time.monotonic() < deadline, "ranks did not finish"
+    assert (tmp_path / "left").exists()
+    err, secs = (tmp_path / "rank0").read_text().split("\n")
+    assert err, "the surviving rank's collective must fail, not succeed"
+    assert float(secs) < 30
