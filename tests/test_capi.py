@@ -149,3 +149,22 @@ def test_peer_setup_rejects_and_sizes(lib):
     assert lib.dotl_peer_alloc(0, ctypes.byref(p)) == 1
     assert lib.dotl_ipc_open(None, ctypes.byref(p)) == 1
     assert lib.dotl_peer_free(None) == 0 and lib.dotl_ipc_close(None) == 0
+
+
+def test_ffn_rejects(lib):
+    def call(D=256, F=1024, lda=256, mode=0, resid=None, rv=None, normed=64, dtype=1, eps=1e-5, x_out=None):
+        return lib.dotl_ffn(64, 100, D, lda, 64, F, D, 64, 64, F, 64, resid, D, rv, mode, x_out, D, 64, 64,
+                            eps, normed, dtype, D, None, None)
+
+    assert call(D=192) == 2 and "128 or 256" in _err(lib)
+    assert call(F=1000) == 2 and "multiple of 128" in _err(lib)
+    assert call(mode=4) == 1 and "residual mode" in _err(lib)
+    assert call(mode=1) == 1 and "needs resid" in _err(lib)
+    assert call(mode=3, resid=64) == 1 and "row_valid" in _err(lib)
+    assert call(dtype=7) == 1 and "dtype" in _err(lib)
+    assert call(eps=-1.0) == 1 and "eps" in _err(lib)
+    assert call(lda=100) == 2 and "multiples of 8" in _err(lib)
+    assert call(normed=None) == 1 and "NULL" in _err(lib)
+    assert call(x_out=72) == 2 and "x_out" in _err(lib)
+    assert lib.dotl_ffn(None, 0, 256, 256, None, 1024, 256, None, None, 1024, None, None, 256, None, 0,
+                        None, 256, None, None, 1e-5, None, 1, 256, None, None) == 0   # M = 0: nothing to do
