@@ -15,7 +15,12 @@
 //     the result through swizzled smem, so the epilogue of tile i overlaps
 //     the main loop of tile i+1;
 //   * epilogues: bias, bias+GELU (fp16 out, the FFN hidden), bias + residual
-//     with an optional padded-row mask (fp32 out, the residual stream).
+//     with an optional padded-row mask (fp32 out, the residual stream);
+//   * SPLIT2: two CTAs of a cluster split K for long-K problems with too few
+//     tiles, exchanging partial halves through distributed shared memory;
+//   * PEER: each 128-row output tile is TMA-stored into the receive slot of
+//     the tensor-parallel rank that owns those rows (over NVLink), the
+//     reduce-scatter of the row-parallel GEMMs done inside the GEMM.
 //
 // A and W are K-major (rows contiguous along K), which is both nn.Linear's
 // weight layout and the activations' row layout: no transpose anywhere.

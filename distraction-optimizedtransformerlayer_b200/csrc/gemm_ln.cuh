@@ -13,8 +13,10 @@
 // of CS = N / BN CTAs (CS <= 8) shares every 128-row block: CTA r computes
 // columns [r BN, (r+1) BN), so the cluster walks the M blocks together. The
 // epilogue makes two passes over the accumulator:
-//   pass 1: x_new per 32-column chunk (stored by TMA when requested, and
-//           written back into TMEM), with the chunk's exact two-pass mean and
+//   pass 1: x_new per 32-column chunk (the residual block arriving by TMA in
+//           one of two per-warp staging buffers while the previous chunk is
+//           processed; x_new stored by TMA from that buffer when requested,
+//           and written back into TMEM), with the chunk's exact two-pass mean and
 //           M2; chunks, then the CTA's two column halves, merge by Chan et al.'s
 //           pairwise update; each CTA then writes its (mean, M2) for every row
 //           into every peer's shared memory and arrives on the peer's barrier;
