@@ -10,6 +10,7 @@
 
 #include "../../include/dotl.h"
 #include "attention.cuh"
+#include "attn_generic.cuh"
 #include "gemm.cuh"
 #include "gemm_ln.cuh"
 #include "ffn.cuh"
@@ -678,8 +679,9 @@ int dotl_attention(const void* q, const void* k, const void* v, int B, int H, in
     if (out_layout != 0 && out_layout != 1)
         return fail(DOTL_EINVAL, "%s: out_layout must be 0 ([B,H,S,head_dim]) or 1 ([B,S,H*head_dim])", who);
     if (mask_kind < DOTL_MASK_NONE || mask_kind > DOTL_MASK_FULL) return fail(DOTL_EINVAL, "%s: unknown mask kind %d", who, mask_kind);
-    if (head_dim != 32 && head_dim != 64 && head_dim != 128)
-        return fail(DOTL_EUNSUPPORTED, "%s: the tcgen05 kernel covers head_dim 32, 64 and 128, got %d", who, head_dim);
+    const bool tc = head_dim == 32 || head_dim == 64 || head_dim == 128;
+    if (!tc && (head_dim < 8 || head_dim > 256 || head_dim % 8 != 0))
+        return fail(DOTL_EUNSUPPORTED, "%s: head_dim must be a multiple of 8 up to 256, got %d", who, head_dim);
     if (B == 0 || H == 0 || S == 0) return DOTL_OK;
     if (q == nullptr || k == nullptr || v == nullptr || out == nullptr || q_strides == nullptr ||
         k_strides == nullptr || v_strides == nullptr)
@@ -694,6 +696,45 @@ int dotl_attention(const void* q, const void* k, const void* v, int B, int H, in
             if (st[t][d] % 8 != 0 || st[t][d] < 0)
                 return fail(DOTL_EUNSUPPORTED, "%s: q/k/v strides must be non-negative multiples of 8 elements (16 bytes)", who);
     if (static_cast<int64_t>(B) * S > 0x7fffff00LL) return fail(DOTL_EUNSUPPORTED, "%s: B*S must fit in 31 bits", who);
+    if (!tc) {
+        // head dims outside the tcgen05 kernel's tiles: the CUDA-core kernel
+        if (static_cast<int64_t>(B) * H > 65535LL * 65535LL)
+            return fail(DOTL_EUNSUPPORTED, "%s: B*H too large for the generic kernel's grid", who);
+        dotl::AttnGenericParams g;
+        g.q = static_cast<const __half*>(q);
+        g.k = static_cast<const __half*>(k);
+        g.v = static_cast<const __half*>(v);
+        for (int d = 0; d < 3; ++d) {
+            g.qs[d] = q_strides[d];
+            g.ks[d] = k_strides[d];
+            g.vs[d] = v_strides[d];
+        }
+        g.B = B;
+        g.H = H;
+        g.S = S;
+        g.hd = head_dim;
+        g.causal = causal ? 1 : 0;
+        g.scale = scale;
+        g.mask_kind = mask_kind;
+        g.mask = mask;
+        g.ms0 = mask_strides ? mask_strides[0] : 0;
+        g.ms1 = mask_strides ? mask_strides[1] : 0;
+        g.ms2 = mask_strides ? mask_strides[2] : 0;
+        g.ms3 = mask_strides ? mask_strides[3] : 0;
+        g.out = static_cast<__half*>(out);
+        g.out_layout = out_layout;
+        const dim3 grid(static_cast<unsigned>((S + dotl::kGenRows - 1) / dotl::kGenRows),
+                        static_cast<unsigned>(B * H));
+        const dim3 block(dotl::kGenRows * 32);
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        cudaError_t e;
+        if (head_dim <= 32) e = launch_pdl(dotl::attn_generic_kernel<1>, grid, block, 0, s, g);
+        else if (head_dim <= 64) e = launch_pdl(dotl::attn_generic_kernel<2>, grid, block, 0, s, g);
+        else if (head_dim <= 128) e = launch_pdl(dotl::attn_generic_kernel<4>, grid, block, 0, s, g);
+        else e = launch_pdl(dotl::attn_generic_kernel<8>, grid, block, 0, s, g);
+        if (e != cudaSuccess) return fail(DOTL_ECUDA, "%s: launch failed: %s", who, cudaGetErrorString(e));
+        return check_launch(who);
+    }
 
     // Packed tiles run over the flat token axis: every tensor must step from
     // one batch to the next exactly one sequence length further on.

@@ -73,8 +73,9 @@ def test_linear_empty_m_is_ok(lib):
 
 def test_attention_rejects_head_dim(lib):
     st = (ctypes.c_int64 * 3)(0, 0, 0)
-    rc = lib.dotl_attention(16, 16, 16, 1, 1, 8, 48, st, st, st, None, 0, None, 0, 0.1, 16, 0, None)
-    assert rc == 2 and "head_dim" in _err(lib)
+    for hd in (4, 12, 264):
+        rc = lib.dotl_attention(16, 16, 16, 1, 1, 8, hd, st, st, st, None, 0, None, 0, 0.1, 16, 0, None)
+        assert rc == 2 and "head_dim" in _err(lib)
 
 
 def test_attention_rejects_layout_and_mask(lib):

@@ -1,4 +1,5 @@
-"""tcgen05 flash attention against the reference's own attention math (gpu).
+"""Flash attention (tcgen05 for head_dim 32/64/128, the CUDA-core kernel for
+other multiples of 8 up to 256) against the reference's own attention math (gpu).
 
 Cases are the reference's scripts/verify_kernel.py:39-55 set (shapes, causal,
 padded, causal+padded folded into a [B,1,S,S] mask) plus the packed-view
@@ -30,6 +31,14 @@ CASES = [
     ("wide caus+pad", 2, 4, 128, 128, True, True),
     ("odd hd128", 3, 2, 200, 128, True, False),
     ("short packed", 64, 4, 32, 64, False, False),
+    # head dims the tcgen05 tiles do not take: the CUDA-core kernel
+    ("hd 8", 4, 4, 64, 8, False, False),
+    ("hd 8 caus+pad", 3, 4, 70, 8, True, True),
+    ("hd 16 causal", 2, 3, 100, 16, True, False),
+    ("hd 24", 1, 2, 33, 24, False, False),
+    ("hd 48 padded", 2, 2, 90, 48, False, True),
+    ("hd 256", 2, 4, 128, 256, False, False),
+    ("hd 256 caus+pad", 2, 2, 130, 256, True, True),
 ]
 
 TOL = 3e-3
@@ -106,9 +115,10 @@ def test_attention_cases(kernels, case):
         assert (a.float() - p.float()).abs().max().item() <= 1e-3
 
 
-def test_key_mask_with_causal_unfolded(kernels):
+@pytest.mark.parametrize("d", [64, 8, 256])
+def test_key_mask_with_causal_unfolded(kernels, d):
     """A [B,1,1,S] key mask plus is_causal (the model's call), not folded."""
-    b, h, s, d = 3, 4, 256, 64
+    b, h, s = 3, 4, 256
     q, k, v, _, _ = build_case(b, h, s, d, False, False, seed=4)
     lengths = torch.tensor([256, 130, 1], device="cuda")
     valid = torch.arange(s, device="cuda")[None, :] < lengths[:, None]
@@ -129,7 +139,7 @@ def test_fully_masked_rows_are_zero(kernels):
     assert (out.double() - ref).abs().max().item() <= TOL
 
 
-@pytest.mark.parametrize("hd", [8, 16, 256])
+@pytest.mark.parametrize("hd", [4, 12, 264])
 def test_uncovered_head_dims_raise(kernels, hd):
     q = torch.randn(1, 1, 16, hd, device="cuda")
     with pytest.raises(RuntimeError, match="head_dim"):
