@@ -519,15 +519,16 @@ def fused_attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     if impl in (1, 3) or precision in (1, 2, 4):
         raise RuntimeError(
             f"fused_attention_forward: impl={impl} ({_IMPL_NAMES[impl]}), precision="
-            f"{_PREC_NAMES[precision]} is not covered: this build has one attention kernel, "
-            "the tcgen05 tensor-core kernel with fp16 operands (impl 0 or 2, precision 0 or 3)")
+            f"{_PREC_NAMES[precision]} is not covered: this build's attention kernels compute "
+            "with fp16 operands (impl 0 or 2, precision 0 or 3)")
     B, H, S, hd = q.shape
     if scale is None:
         scale = hd ** -0.5
-    if hd not in (32, 64, 128):
+    if hd % 8 or not 8 <= hd <= 256:
         raise RuntimeError(
             f"fused_attention_forward: impl={impl} ({_IMPL_NAMES[impl]}) does not cover "
-            f"dtype={q.dtype}, head_dim={hd}: the tcgen05 kernel takes head_dim 32, 64 or 128")
+            f"dtype={q.dtype}, head_dim={hd}: head_dim must be a multiple of 8 up to 256 "
+            "(32, 64 and 128 on the tcgen05 kernel, the others on the CUDA-core kernel)")
     dtype = q.dtype
 
     def prep(t):
