@@ -11,7 +11,8 @@
 //
 // One warp per query row, the head dims spread over the lanes (hd <= 32 HPL),
 // fp32 scores through an online softmax (running max, running sum, rescaled
-// accumulator), fp16 output. The block's 16 query rows share every key/value
+// accumulator; P rounded to fp16 before it multiplies V, as the tensor-core
+// kernels do), fp16 output. The block's 16 query rows share every key/value
 // tile, staged in shared memory (32 keys at a time, rows zero-padded to
 // 32 HPL) with 16-byte loads. Not a tensor-core kernel: these shapes are small
 // (the largest, dashboard shape 8, is 1 GFLOP per layer).
@@ -97,8 +98,11 @@ __global__ void __launch_bounds__(kGenRows * 32) attn_generic_kernel(const AttnG
             const float corr = __expf(m - m_new);   // 0 on the first allowed key
             const float pj = __expf(s - m_new);
             l = fmaf(l, corr, pj);
+            // P meets V as fp16, the row sum takes the unrounded value: the
+            // arithmetic of the reference's fp16 kernels and of attn_tc_kernel
+            const float ph = __half2float(__float2half_rn(pj));
 #pragma unroll
-            for (int i = 0; i < HPL; ++i) o[i] = fmaf(o[i], corr, pj * __half2float(v_s[j][lane + 32 * i]));
+            for (int i = 0; i < HPL; ++i) o[i] = fmaf(o[i], corr, ph * __half2float(v_s[j][lane + 32 * i]));
             m = m_new;
         }
     }
