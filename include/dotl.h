@@ -152,7 +152,9 @@ int dotl_ffn(const void* a, int64_t M, int64_t D, int64_t lda, const void* w1, i
  *   mask_kind: DOTL_MASK_*; mask strides ms[4] in elements (b, h, query, key).
  *   causal: key j may be attended by query i only if j <= i (combinable).
  *   out: fp16, layout 0 = [B,H,S,head_dim], 1 = [B,S,H*head_dim].
- * Fully masked query rows are written as 0. head_dim in {32, 64, 128}.
+ * Fully masked query rows are written as 0. head_dim 32, 64 or 128 run on the
+ * tcgen05 kernel; other multiples of 8 up to 256 on a CUDA-core flash kernel
+ * (the reference's scalar/wmma shapes, e.g. head_dim 8 and 256).
  */
 int dotl_attention(const void* q, const void* k, const void* v, int B, int H, int S, int head_dim,
                    const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
