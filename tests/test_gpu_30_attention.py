@@ -15,11 +15,12 @@ import torch
 pytestmark = pytest.mark.gpu
 
 # (label, batch, heads, seq_len, head_dim, causal, padded)
+# scripts/verify_kernel.py:39-55, all 15 cases as the reference lists them
 CASES = [
-    ("tiny", 1, 1, 8, 32, False, False),
-    ("tiny causal", 1, 1, 8, 32, True, False),
-    ("tiny padded", 2, 1, 8, 32, False, True),
-    ("tiny causal+pad", 2, 1, 8, 32, True, True),
+    ("tiny", 1, 1, 8, 8, False, False),
+    ("tiny causal", 1, 1, 8, 8, True, False),
+    ("tiny padded", 2, 1, 8, 8, False, True),
+    ("tiny causal+pad", 2, 1, 8, 8, True, True),
     ("default", 8, 8, 128, 64, False, False),
     ("default causal", 8, 8, 128, 64, True, False),
     ("default padded", 8, 8, 128, 64, False, True),
@@ -29,15 +30,19 @@ CASES = [
     ("odd shape", 3, 5, 37, 32, True, True),
     ("wide head_dim", 2, 4, 64, 128, False, False),
     ("wide caus+pad", 2, 4, 128, 128, True, True),
+    ("head_dim 256", 2, 4, 64, 256, False, False),
+    ("head_dim 256 caus", 2, 4, 128, 256, True, True),
+    # further cases of this build: the tcgen05 tiny and odd shapes, packed
+    # short sequences, and more head dims of the CUDA-core kernel
+    ("tiny hd32", 1, 1, 8, 32, False, False),
+    ("tiny hd32 causal+pad", 2, 1, 8, 32, True, True),
     ("odd hd128", 3, 2, 200, 128, True, False),
     ("short packed", 64, 4, 32, 64, False, False),
-    # head dims the tcgen05 tiles do not take: the CUDA-core kernel
     ("hd 8", 4, 4, 64, 8, False, False),
     ("hd 8 caus+pad", 3, 4, 70, 8, True, True),
     ("hd 16 causal", 2, 3, 100, 16, True, False),
     ("hd 24", 1, 2, 33, 24, False, False),
     ("hd 48 padded", 2, 2, 90, 48, False, True),
-    ("hd 256", 2, 4, 128, 256, False, False),
     ("hd 256 caus+pad", 2, 2, 130, 256, True, True),
 ]
 
