@@ -27,7 +27,6 @@ from typing import Optional, Tuple
 import torch
 import torch.nn as nn
 
-from . import config
 from .kernels import (_attention_dispatch, _f32_param, _ffn, _ffn_ok, _layernorm, _linear, _linear_bias,
                       _linear_ln, _linear_ln_ok)
 from .util import _version_or_none
