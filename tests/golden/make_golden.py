@@ -38,6 +38,8 @@ CASES = [
     ("short_seq", 16, 32, 256, 4, 1024, 1, False, 0.0, 13),
     ("hd128_causal", 2, 128, 256, 2, 512, 1, True, 0.0, 14),
     ("two_layer_pad", 2, 64, 128, 4, 256, 2, False, 0.5, 15),
+    ("hd8_two_layer_causal_pad", 3, 40, 32, 4, 64, 2, True, 0.5, 16),
+    ("hd256_causal", 2, 48, 512, 2, 512, 1, True, 0.0, 17),
 ]
 
 
