@@ -23,6 +23,7 @@
 #include <mutex>
 #include <string>
 #include <algorithm>
+#include <atomic>
 #include <utility>
 
 namespace {
@@ -55,27 +56,33 @@ int current_device(int* dev) {
 
 constexpr int kMaxDevices = 64;
 
+// Per-device caches below are filled on first use from whichever host thread
+// gets there first. They hold atomics: two threads may both miss and both
+// fill an entry (each writes the same value; the CUDA calls behind them are
+// idempotent), but no thread reads a torn or racy value.
+using DeviceFlags = std::atomic<bool>[kMaxDevices];
+
 int sm_count(int dev) {
-    static int counts[kMaxDevices] = {0};
+    static std::atomic<int> counts[kMaxDevices];
     if (dev < 0 || dev >= kMaxDevices) return 148;
-    if (counts[dev] == 0) {
-        int n = 0;
+    int n = counts[dev].load(std::memory_order_relaxed);
+    if (n == 0) {
         if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-        counts[dev] = n;
+        counts[dev].store(n, std::memory_order_relaxed);
     }
-    return counts[dev];
+    return n;
 }
 
 // Raises a kernel's dynamic shared memory limit, once per device.
 template <typename Kernel>
-int ensure_smem(Kernel kernel, uint32_t bytes, int dev, bool* done_flags) {
-    if (dev >= 0 && dev < kMaxDevices && done_flags[dev]) return DOTL_OK;
+int ensure_smem(Kernel kernel, uint32_t bytes, int dev, DeviceFlags& done_flags) {
+    if (dev >= 0 && dev < kMaxDevices && done_flags[dev].load(std::memory_order_acquire)) return DOTL_OK;
     const cudaError_t e =
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
     if (e != cudaSuccess)
         return fail(DOTL_ECUDA, "cudaFuncSetAttribute(%u bytes of shared memory) failed: %s", bytes,
                     cudaGetErrorString(e));
-    if (dev >= 0 && dev < kMaxDevices) done_flags[dev] = true;
+    if (dev >= 0 && dev < kMaxDevices) done_flags[dev].store(true, std::memory_order_release);
     return DOTL_OK;
 }
 
@@ -83,15 +90,15 @@ int ensure_smem(Kernel kernel, uint32_t bytes, int dev, bool* done_flags) {
 // launch to grant at least `needed` registers in total; a raise that the
 // launch cannot cover would wait forever, so such a build refuses to launch.
 template <typename Kernel>
-int check_regs(Kernel kernel, int threads, int needed, bool* done_flags, int dev, const char* who) {
-    if (dev >= 0 && dev < kMaxDevices && done_flags[dev]) return DOTL_OK;
+int check_regs(Kernel kernel, int threads, int needed, DeviceFlags& done_flags, int dev, const char* who) {
+    if (dev >= 0 && dev < kMaxDevices && done_flags[dev].load(std::memory_order_acquire)) return DOTL_OK;
     cudaFuncAttributes fa;
     const cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
     if (e != cudaSuccess) return fail(DOTL_ECUDA, "%s: cudaFuncGetAttributes failed: %s", who, cudaGetErrorString(e));
     if (fa.numRegs * threads < needed)
         return fail(DOTL_EUNSUPPORTED, "%s: kernel built with %d registers per thread, its warpgroup split needs %d in total",
                     who, fa.numRegs, needed);
-    if (dev >= 0 && dev < kMaxDevices) done_flags[dev] = true;
+    if (dev >= 0 && dev < kMaxDevices) done_flags[dev].store(true, std::memory_order_release);
     return DOTL_OK;
 }
 
@@ -161,7 +168,7 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap&
     auto kernel = dotl::gemm_tc_kernel<BN, STAGES, OUT_F16, SPLIT2, PEER>;
     static const dotl::GemmPeerOut kNoPeers = {};
     const dotl::GemmPeerOut& po = po_in != nullptr ? *po_in : kNoPeers;
-    static bool done[kMaxDevices] = {false};
+    static DeviceFlags done;
     if (int rc = ensure_smem(kernel, L::kAlloc, dev, done)) return rc;
     const int tiles = p.num_m_tiles * p.num_n_tiles;
     cudaError_t e;
@@ -253,13 +260,13 @@ int launch_gemm_ln(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorM
                    const CUtensorMap& tr, const dotl::GemmLnParams& p, int dev, cudaStream_t stream) {
     using L = dotl::GemmLnSmem<BN, STAGES>;
     auto kernel = dotl::gemm_ln_kernel<BN, STAGES, NORM_F16>;
-    static bool done[kMaxDevices] = {false};
-    static int fit[kMaxDevices][dotl::kLnMaxCluster + 1] = {};
+    static DeviceFlags done;
+    static std::atomic<int> fit[kMaxDevices][dotl::kLnMaxCluster + 1];
     if (int rc = ensure_smem(kernel, L::kAlloc, dev, done)) return rc;
-    int clusters = (dev >= 0 && dev < kMaxDevices) ? fit[dev][p.cs] : 0;
+    int clusters = (dev >= 0 && dev < kMaxDevices) ? fit[dev][p.cs].load(std::memory_order_relaxed) : 0;
     if (clusters == 0) {
         if (int rc = max_clusters(kernel, p.cs, L::kAlloc, &clusters)) return rc;
-        if (dev >= 0 && dev < kMaxDevices) fit[dev][p.cs] = clusters;
+        if (dev >= 0 && dev < kMaxDevices) fit[dev][p.cs].store(clusters, std::memory_order_relaxed);
     }
     if (clusters > p.num_m_tiles) clusters = p.num_m_tiles;
     cudaLaunchConfig_t cfg = {};
@@ -301,8 +308,8 @@ int launch_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap&
                 int dev, cudaStream_t stream) {
     using L = dotl::AttnSmem<HD, STAGES>;
     auto kernel = dotl::attn_tc_kernel<HD, STAGES>;
-    static bool done[kMaxDevices] = {false};
-    static bool regs_ok[kMaxDevices] = {false};
+    static DeviceFlags done;
+    static DeviceFlags regs_ok;
     if (int rc = ensure_smem(kernel, L::kAlloc, dev, done)) return rc;
     if (int rc = check_regs(kernel, dotl::kAttnThreads, dotl::kAttnRegSplit, regs_ok, dev, "dotl_attention")) return rc;
     const int items = p.num_streams * p.num_q_tiles;
@@ -319,7 +326,7 @@ int launch_ffn(const CUtensorMap& ta, const CUtensorMap& tw1, const CUtensorMap&
                const CUtensorMap& tx, const CUtensorMap& tn, const dotl::FfnParams& p, int dev, cudaStream_t stream) {
     using L = dotl::FfnSmem<D>;
     auto kernel = dotl::ffn_kernel<D, NF16>;
-    static bool done[kMaxDevices] = {false};
+    static DeviceFlags done;
     if (int rc = ensure_smem(kernel, L::kAlloc, dev, done)) return rc;
     const int grid = p.num_m_tiles < sm_count(dev) ? p.num_m_tiles : sm_count(dev);
     const cudaError_t e =
@@ -698,8 +705,9 @@ int dotl_attention(const void* q, const void* k, const void* v, int B, int H, in
     if (static_cast<int64_t>(B) * S > 0x7fffff00LL) return fail(DOTL_EUNSUPPORTED, "%s: B*S must fit in 31 bits", who);
     if (!tc) {
         // head dims outside the tcgen05 kernel's tiles: the CUDA-core kernel
-        if (static_cast<int64_t>(B) * H > 65535LL * 65535LL)
-            return fail(DOTL_EUNSUPPORTED, "%s: B*H too large for the generic kernel's grid", who);
+        if (static_cast<int64_t>(B) * H > 65535)
+            return fail(DOTL_EUNSUPPORTED, "%s: B*H=%lld is over the 65535 (batch, head) pairs of the head_dim %d kernel's grid", who,
+                        static_cast<long long>(B) * H, head_dim);
         dotl::AttnGenericParams g;
         g.q = static_cast<const __half*>(q);
         g.k = static_cast<const __half*>(k);

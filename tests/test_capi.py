@@ -78,6 +78,13 @@ def test_attention_rejects_head_dim(lib):
         assert rc == 2 and "head_dim" in _err(lib)
 
 
+def test_attention_rejects_generic_grid_overflow(lib):
+    # head_dim 8 takes the CUDA-core kernel, one grid row per (batch, head)
+    st = (ctypes.c_int64 * 3)(0, 0, 0)
+    rc = lib.dotl_attention(16, 16, 16, 65536, 1, 8, 8, st, st, st, None, 0, None, 0, 0.1, 16, 0, None)
+    assert rc == 2 and "65535" in _err(lib)
+
+
 def test_attention_rejects_layout_and_mask(lib):
     st = (ctypes.c_int64 * 3)(0, 0, 0)
     assert lib.dotl_attention(16, 16, 16, 1, 1, 8, 64, st, st, st, None, 0, None, 0, 0.1, 16, 2, None) == 1
