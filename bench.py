@@ -239,7 +239,8 @@ class _ClockSampler:
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index):
-        self.path = tempfile.mktemp(suffix=".csv")
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
         self.proc = None
         self.gpu_index = gpu_index
 
@@ -254,6 +255,9 @@ class _ClockSampler:
 
     def stop(self):
         if self.proc is None:
+            if getattr(self, "f", None) is not None:
+                self.f.close()
+            os.unlink(self.path)
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
         try:
