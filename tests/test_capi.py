@@ -176,3 +176,45 @@ def test_ffn_rejects(lib):
     assert call(x_out=72) == 2 and "x_out" in _err(lib)
     assert lib.dotl_ffn(None, 0, 256, 256, None, 1024, 256, None, None, 1024, None, None, 256, None, 0,
                         None, 256, None, None, 1e-5, None, 1, 256, None, None) == 0   # M = 0: nothing to do
+
+
+def _prototypes():
+    """name -> parameter declarations, from include/dotl.h."""
+    text = re.sub(r"/\*.*?\*/", " ", open(HEADER).read(), flags=re.S)
+    out = {}
+    for m in re.finditer(r"\b(?:int|const char\s*\*)\s*(dotl_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", text):
+        params = " ".join(m.group(2).split())
+        out[m.group(1)] = [] if params in ("", "void") else [p.strip() for p in params.split(",")]
+    return out
+
+
+def _kind_of_decl(decl):
+    if "*" in decl:
+        return "ptr"
+    if "int64_t" in decl:
+        return "i64"
+    if "float" in decl:
+        return "f32"
+    if "int" in decl:
+        return "i32"
+    raise AssertionError(f"unclassified parameter {decl!r}")
+
+
+def _kind_of_ctype(t):
+    if t in (ctypes.c_void_p, ctypes.c_char_p) or hasattr(t, "_type_") and isinstance(t._type_, type):
+        return "ptr"
+    return {ctypes.c_int64: "i64", ctypes.c_float: "f32", ctypes.c_int: "i32", ctypes.c_uint: "i32"}[t]
+
+
+def test_ctypes_signatures_match_the_header():
+    """Every binding dotl_ops declares has the header's parameter count and
+    kinds (pointer, int64, int, float): a drifted ctypes signature would pass
+    arguments in the wrong registers without any error."""
+    import dotl_ops
+
+    protos = _prototypes()
+    assert set(dotl_ops._SIGNATURES) <= set(protos), set(dotl_ops._SIGNATURES) - set(protos)
+    for name, (argtypes, _restype) in dotl_ops._SIGNATURES.items():
+        want = [_kind_of_decl(d) for d in protos[name]]
+        got = [_kind_of_ctype(t) for t in argtypes]
+        assert got == want, f"{name}: ctypes {got} != header {want}"
