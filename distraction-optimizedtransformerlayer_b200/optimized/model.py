@@ -43,6 +43,22 @@ class OptimizedTransformer(nn.Module):
         self._graph_denied: set = set()
         self._chunk_rows: Dict[Tuple, int] = {}
         self._device_budget: Optional[int] = None
+        # A captured graph reads the fp16 weight copies it was captured with.
+        # Reloading the weights (load_state_dict) or moving the model (to,
+        # cuda, half, ...) therefore drops this model's graphs, and the next
+        # forward captures again from the new weights. Upstream keeps replaying
+        # and reads a stale QKV concatenation (graphs.py:356-363 there: "weights
+        # never move after copy_model_weights"); every GEMM weight here is a
+        # cached fp16 copy, so the graphs are dropped instead.
+        self.register_load_state_dict_post_hook(OptimizedTransformer._drop_graphs_after_load)
+
+    @staticmethod
+    def _drop_graphs_after_load(module: "OptimizedTransformer", incompatible_keys) -> None:
+        module.release_graphs()
+
+    def _apply(self, fn, *args, **kwargs):
+        self.release_graphs()
+        return super()._apply(fn, *args, **kwargs)
 
     def _mask_is_trivial(self, mask: Optional[torch.Tensor]) -> bool:
         """True when every position is valid (model.py:68-93 upstream): one
@@ -166,7 +182,11 @@ class OptimizedTransformer(nn.Module):
         return runner
 
     def release_graphs(self) -> None:
-        """Free every captured graph of this model (before process-group teardown)."""
-        for runner in self._graphs.values():
+        """Free every captured graph of this model (before process-group
+        teardown, after new weights, before a move)."""
+        graphs = self.__dict__.get("_graphs")
+        if not graphs:
+            return
+        for runner in graphs.values():
             runner.release()
-        self._graphs.clear()
+        graphs.clear()

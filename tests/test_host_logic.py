@@ -173,3 +173,34 @@ def test_attention_refuses_uncovered_requests_on_host():
         dotl_ops.fused_attention_forward(q, q, q, impl=9)
     with pytest.raises(RuntimeError, match="CUDA"):
         dotl_ops.fused_attention_forward(q, q, q)
+
+
+class _FakeRunner:
+    def __init__(self):
+        self.released = False
+
+    def release(self):
+        self.released = True
+
+
+def test_reloading_or_moving_weights_drops_captured_graphs():
+    """A graph bakes in the fp16 weight copies: load_state_dict and module
+    moves drop the model's graphs so the next forward captures the new weights."""
+    from optimized import OptimizedTransformer
+
+    cfg = O.TransformerConfig(2, 16, 64, 4, 128, 1, True)
+    params = O.init_params(cfg, 1)
+    model = OptimizedTransformer(cfg)
+    model.load_state_dict(params, strict=True)          # no graphs yet: nothing to drop
+    r = _FakeRunner()
+    model._graphs[("key",)] = r
+    model.load_state_dict(O.init_params(cfg, 2), strict=True)
+    assert r.released and not model._graphs
+    r2 = _FakeRunner()
+    model._graphs[("key",)] = r2
+    model.float()                                       # any _apply (to, cuda, half, ...)
+    assert r2.released and not model._graphs
+    r3 = _FakeRunner()
+    model._graphs[("key",)] = r3
+    model.eval()                                        # mode switches keep them
+    assert not r3.released and model._graphs
