@@ -973,8 +973,8 @@ int dotl_peer_signal_bytes(int blocks, int64_t* bytes) {
 int dotl_allreduce_ln(int world, int rank, const float* const* parts, void* const* signals, float* const* x_new,
                       void* const* normed, int normed_dtype, int push, int parts_local, const float* x, const float* bias,
                       const uint8_t* sum_row_valid, const float* ln_weight, const float* ln_bias, float eps,
-                      const uint8_t* normed_row_valid, int64_t rows, int64_t D, int blocks, int timeout_ms,
-                      void* stream) {
+                      const uint8_t* normed_row_valid, int64_t rows, int64_t D, int blocks, int64_t signal_bytes,
+                      unsigned int* status, int timeout_ms, void* stream) {
     const char* who = "dotl_allreduce_ln";
     if (world < 1 || world > dotl::kPeerMax || rank < 0 || rank >= world)
         return fail(DOTL_EINVAL, "%s: world %d / rank %d outside 1..%d", who, world, rank, dotl::kPeerMax);
@@ -988,6 +988,16 @@ int dotl_allreduce_ln(int world, int rank, const float* const* parts, void* cons
     if (parts == nullptr || signals == nullptr || normed == nullptr || x == nullptr || ln_weight == nullptr ||
         ln_bias == nullptr)
         return fail(DOTL_EINVAL, "%s: NULL pointer", who);
+    // The signal layout depends on the grid (counters, then flags at offset
+    // blocks): a grid other than the one the areas were sized for would write
+    // past them or overlap counters with flags.
+    if (signal_bytes != dotl::peer_signal_words(blocks) * 4)
+        return fail(DOTL_EINVAL,
+                    "%s: signal areas of %lld bytes do not match blocks=%d (dotl_peer_signal_bytes gives %lld); "
+                    "blocks must be the value the areas were allocated for, on every call and every rank",
+                    who, (long long)signal_bytes, blocks, (long long)(dotl::peer_signal_words(blocks) * 4));
+    if (status != nullptr && (reinterpret_cast<uintptr_t>(status) & 3u) != 0)
+        return fail(DOTL_EINVAL, "%s: status word must be 4-byte aligned", who);
     dotl::PeerLnParams p = {};
     const int d0 = push ? 0 : rank, d1 = push ? world : rank + 1;
     for (int i = 0; i < world; ++i) {
@@ -1026,6 +1036,7 @@ int dotl_allreduce_ln(int world, int rank, const float* const* parts, void* cons
     p.push = push ? 1 : 0;
     p.parts_local = parts_local ? 1 : 0;
     p.timeout_ns = static_cast<unsigned long long>(timeout_ms) * 1000000ull;
+    p.status = status;
     const dim3 grid(static_cast<unsigned>(blocks)), block(dotl::kPeerWarps * 32);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t le;

@@ -114,7 +114,7 @@ __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity) {
 // Distributed shared memory: a CTA reaches a peer's shared memory through the
 // shared::cluster window (mapa), stores there, and arrives on the peer's
 // mbarriers with release semantics at cluster scope; the peer waits on its own
-// barrier with acquire at cluster scope. No TMA multicast anywhere.
+// barrier with acquire at cluster scope. Every CTA loads its own tiles.
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;

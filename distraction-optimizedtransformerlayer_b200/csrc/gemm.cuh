@@ -60,7 +60,7 @@ struct GemmParams {
 // Output tiles scattered over the ranks of a tensor-parallel group: row block
 // m (rows [128 m, 128 m + 128)) belongs to rank (128 m) / rows, which receives
 // it at row 128 m - rank * rows of map[rank] (its receive slot for this rank,
-// in its own memory, reached over NVLink). Plain TMA stores: no multicast.
+// in its own memory, reached over NVLink). Plain TMA stores, one destination each.
 constexpr int kGemmPeerMax = 8;
 struct GemmPeerOut {
     CUtensorMap map[kGemmPeerMax];

@@ -10,7 +10,7 @@
 // parallelism, so the reduction itself has no counterpart there).
 //
 // Every rank's partial-sum buffer and signal area are mapped into every other
-// rank's address space (CUDA IPC). Plain loads and stores only: no multicast,
+// rank's address space (CUDA IPC). Plain loads and stores only (one address each),
 // no NVLS. Per call, on every rank, with the same grid on every rank:
 //   1. start barrier: CTA b tells CTA b of every peer that it has started, and
 //      waits until every peer's CTA b has (so every peer's partial sums, which
@@ -74,6 +74,7 @@ struct PeerLnParams {
     int push;
     int parts_local;               // part[i]: rows [lo, hi) of rank i's partial sums, in this rank's memory
     unsigned long long timeout_ns;
+    unsigned int* status;          // optional caller word (e.g. host-mapped) that a timeout also sets
 };
 
 __device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
@@ -99,6 +100,12 @@ __device__ __forceinline__ bool peer_handshake(const PeerLnParams& p, int64_t of
         while (static_cast<int>(ld_acquire_sys(mine + src) - val) < 0) {
             if (global_ns() - t0 > p.timeout_ns) {
                 atomicOr(&g_dotl_dev_error, kDevErrPeerTimeout);
+                if (p.status != nullptr) {
+                    // a plain store: the word may be host memory, where
+                    // device atomics are not guaranteed
+                    *reinterpret_cast<volatile unsigned int*>(p.status) = kDevErrPeerTimeout;
+                    __threadfence_system();
+                }
                 return false;
             }
         }

@@ -62,7 +62,7 @@ _SIGNATURES = {
     "dotl_peer_blocks": ([ctypes.POINTER(ctypes.c_int)], _i32),
     "dotl_peer_signal_bytes": ([_i32, _P64], _i32),
     "dotl_allreduce_ln": ([_i32, _i32, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _f32, _vp,
-                           _i64, _i64, _i32, _i32, _vp], _i32),
+                           _i64, _i64, _i32, _i64, _vp, _i32, _vp], _i32),
     "dotl_linear_peer": ([_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i32, _vp, _i64, _i64, _vp], _i32),
 }
 
@@ -649,15 +649,21 @@ def _ptrarr(vals) -> ctypes.Array:
 def allreduce_ln(world: int, rank: int, parts, signals, x_new, normed, normed_half: bool, push: bool,
                  x: torch.Tensor, bias: Optional[torch.Tensor], ln_w: torch.Tensor, ln_b: torch.Tensor,
                  eps: float, sum_row_valid: Optional[torch.Tensor], normed_row_valid: Optional[torch.Tensor],
-                 rows: int, D: int, blocks: int, timeout_ms: int, parts_local: bool = False) -> None:
+                 rows: int, D: int, blocks: int, timeout_ms: int, parts_local: bool = False,
+                 signal_bytes: Optional[int] = None, status: Optional[int] = None) -> None:
     """dotl_allreduce_ln: parts / signals / x_new / normed are per-rank lists of
-    device addresses as this process sees them (None where not used)."""
+    device addresses as this process sees them (None where not used).
+    signal_bytes: the size the signal areas were allocated with (default: the
+    size `blocks` needs). status: address of a device-visible uint32 that a
+    timed-out wait sets (e.g. a pinned host word), or None."""
+    if signal_bytes is None:
+        signal_bytes = peer_signal_bytes(blocks)
     _check(lib().dotl_allreduce_ln(
         world, rank, _ptrarr(parts), _ptrarr(signals), None if x_new is None else _ptrarr(x_new),
         _ptrarr(normed), F16 if normed_half else F32, 1 if push else 0, 1 if parts_local else 0,
         x.data_ptr(), _ptr(bias),
         _ptr(sum_row_valid), ln_w.data_ptr(), ln_b.data_ptr(), float(eps), _ptr(normed_row_valid),
-        int(rows), int(D), int(blocks), int(timeout_ms), _stream(x.device)))
+        int(rows), int(D), int(blocks), int(signal_bytes), status, int(timeout_ms), _stream(x.device)))
 
 
 def linear_peer(a16: torch.Tensor, w16: torch.Tensor, bias: Optional[torch.Tensor], outs, rows_per_rank: int,

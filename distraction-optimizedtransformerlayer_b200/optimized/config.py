@@ -42,8 +42,11 @@ LAYERNORM = "auto"
 QKV_FP16 = "auto"
 NORMED_FP16 = "auto"
 
-# The reference's fused FFN kernel only covered d_model <= 128; here the FFN
-# always runs as LN -> GEMM(+GELU) -> GEMM(+residual, +row mask) -> LN.
+# The reference's fused FFN kernel only covered d_model <= 128. Here the block's
+# MLP (ffn_in + GELU, ffn_out + residual + row mask, next LayerNorm) is one
+# kernel with the hidden kept on chip where the shape allows it (kernels
+# ffn_preferred), else GEMM(+GELU) then GEMM(+residual, +row mask) and the
+# LayerNorm, folded into the second GEMM's epilogue where that is faster.
 FFN_BLOCK = "auto"
 
 # cp.async knob of the reference's wmma kernel; TMA does the staging here.
@@ -65,17 +68,17 @@ CUDA_GRAPH = "auto"
 # faster eager (679 vs 778, 1005 vs 1208, 1821 vs 1953 us). Replay is
 # bit-identical to eager.
 _GRAPH_MAX_ACTIVATION = 1 << 22
-_GRAPH_POOL_SAFETY_FRACTION = 0.25
+# graphs kept per model (one per input shape / mask mode)
 _GRAPH_MAX_ENTRIES = 4
-_GRAPH_WARMUP_ITERS = 3
+# no capture when less than this much device memory is free
 _GRAPH_MIN_FREE_BYTES = 512 << 20
-_GRAPH_SEED = 20240827
 
-# Split the batch and retry when a forward runs out of memory.
+# Eager forwards too big for the device run over batch chunks sized from the
+# free device memory (rows never interact, so the values do not change).
 MICROBATCH_FALLBACK = True
 _MICROBATCH_MIN_ROWS = 1
-_MICROBATCH_PEAK_FACTOR = 10
-_MICROBATCH_BUDGET_FRACTION = 0.85
+# fraction of the free device memory a chunk's intermediates may take
+_MICROBATCH_BUDGET_FRACTION = 0.8
 
 
 def validate() -> None:

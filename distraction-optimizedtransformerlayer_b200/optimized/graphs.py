@@ -1,48 +1,74 @@
-"""Whole-forward CUDA graph capture and replay (optimized/graphs.py upstream).
+"""Whole-forward CUDA graph capture and replay (the role of optimized/graphs.py
+upstream: `_graph_key`, `_graph_eligible`, `_capture_graph`, `_GraphRunner`).
 
-The forward is recorded once per key (shape, dtype, device, mask mode) and
-replayed afterwards: one graph launch plus two input copies instead of
-1 + 6 * num_layers kernel launches. Replay is verified bit-identical to eager
-before a graph is installed; on any doubt capture declines and the caller
-stays eager. Re-derived for B200: graphs are captured per device (one process
-per GPU) and the size gate is B200's (config._GRAPH_MAX_ACTIVATION).
+A forward of 1 + 5..8 * num_layers kernel launches becomes one graph launch
+plus the copy of x (and the mask) into the graph's input buffers and the copy
+of its output out. How this build does it:
+
+* What a graph depends on. The kernels read fp16 / fp32 copies of the weights
+  that the layers cache per parameter version, and a graph bakes in the
+  addresses of those copies. So a runner records the fingerprint of the
+  parameters it was captured under (each parameter's storage address and
+  version counter). `OptimizedTransformer.forward` compares it with the live
+  fingerprint before every replay, so an in-place update (optimizer.step,
+  param.copy_ or mul_ under no_grad) or a reload retires the runner, and the
+  next call captures again from the new weights.
+* How it is captured. The capturing call runs the forward eagerly on a side
+  stream with the caller's own input first. That run builds every lazily
+  created cache, and its output, which the call returns, is also the reference
+  for a bit-exact check of one replay. A graph whose replay differs, or whose
+  capture rebuilt a weight cache, is dropped and the key stays eager.
+* Lifetime. The graphs belong to their model. A `weakref.finalize` on the
+  model releases them when the model is collected, and at interpreter exit
+  while CUDA is still up; `release_graphs()` does it on demand (before a
+  process group that a graph's kernels use is torn down, for instance).
 """
 
 from __future__ import annotations
 
-import atexit
 import weakref
-from typing import Optional, Tuple
+from typing import Dict, Optional, Tuple
 
 import torch
 
 from . import config
 from .kernels import _custom_kernels
+from .util import _version_or_none
 
-_graph_warned = False
+_warned = False
+
+
+def _note_once(msg: str) -> None:
+    global _warned
+    if not _warned:
+        _warned = True
+        print(f"[info] {msg}")
 
 
 class _GraphRunner:
-    """One captured CUDA graph plus the buffers whose addresses it baked in."""
+    """One captured forward: the graph, the input/output buffers whose
+    addresses it holds, and the weight fingerprint it is valid for."""
 
     __slots__ = ("graph", "stream", "static_x", "static_mask", "static_out", "needs_mask",
-                 "replays", "pinned", "__weakref__")
+                 "fingerprint", "keep_alive", "replays")
 
-    def __init__(self, graph, stream, static_x, static_mask, static_out, needs_mask, pinned):
+    def __init__(self, graph, stream, static_x, static_mask, static_out, needs_mask, fingerprint,
+                 keep_alive):
         self.graph = graph
         self.stream = stream
         self.static_x = static_x
         self.static_mask = static_mask
         self.static_out = static_out
         self.needs_mask = needs_mask
-        self.pinned = pinned
+        self.fingerprint = fingerprint
+        self.keep_alive = keep_alive      # the weight caches the kernels read
         self.replays = 0
 
     def replay(self, x: torch.Tensor, mask: Optional[torch.Tensor],
                out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """Copy the inputs in, replay, return the output copied out of the
-        graph's buffer (the next replay overwrites static_out in place): into
-        `out` when given, else into a new tensor."""
+        """Copy the inputs in, replay, and return the output copied out of the
+        graph's buffer (the next replay rewrites that buffer): into `out`
+        when given, else into a new tensor."""
         self.static_x.copy_(x)
         if self.needs_mask:
             self.static_mask.copy_(mask)
@@ -54,14 +80,14 @@ class _GraphRunner:
         return out
 
     def release(self) -> None:
-        try:
-            self.graph.reset()
-        except Exception:  # noqa: BLE001 - reset on a half-captured graph may throw
-            pass
-        self.graph = None
-        self.stream = None
+        if self.graph is not None:
+            try:
+                self.graph.reset()
+            except Exception:  # noqa: BLE001 - a graph whose capture failed may refuse reset
+                pass
+        self.graph = self.stream = None
         self.static_x = self.static_mask = self.static_out = None
-        self.pinned = None
+        self.keep_alive = ()
 
 
 def _graph_key(x: torch.Tensor, use_mask: bool) -> Tuple:
@@ -85,113 +111,105 @@ def _graph_eligible(x: torch.Tensor, entries: int) -> bool:
     return x.shape[0] * x.shape[1] * x.shape[2] <= config._GRAPH_MAX_ACTIVATION
 
 
-def _graph_cache_ptrs(model) -> Tuple:
+def _weights_fingerprint(model) -> Tuple:
+    """(storage address, version) of every parameter: changes whenever a
+    weight is edited in place, reloaded or moved."""
+    return tuple((p.data_ptr(), _version_or_none(p)) for p in model.parameters())
+
+
+def _weight_caches(model) -> Tuple:
+    """The cached weight copies the kernels read (the tensors a graph holds
+    the addresses of)."""
     out = []
     for layer in model.layers:
         attn = layer.attention
-        for t in (attn._qkv_weight, attn._qkv_bias, attn.out_proj._w16, layer.ffn_in._w16,
-                  layer.ffn_out._w16):
-            out.append(None if t is None else t.data_ptr())
-    return tuple(out)
-
-
-def _graph_pinned_refs(model) -> Tuple:
-    out = []
-    for layer in model.layers:
-        attn = layer.attention
-        out.extend((attn._qkv_weight, attn._qkv_bias, attn.out_proj._w16, layer.ffn_in._w16,
-                    layer.ffn_out._w16))
+        out += [attn._qkv_weight, attn._qkv_bias, attn.out_proj._w16, layer.ffn_in._w16, layer.ffn_out._w16]
+        for mod in (layer.norm1, layer.norm2, attn.out_proj, layer.ffn_in, layer.ffn_out):
+            out += [entry[1] for entry in mod.__dict__.get("_f32_cache", {}).values()]
+    out += [entry[1] for entry in model.final_norm.__dict__.get("_f32_cache", {}).values()]
     return tuple(out)
 
 
 def _capture_graph(model, x: torch.Tensor, mask: Optional[torch.Tensor],
-                   use_mask: bool) -> Optional[_GraphRunner]:
-    """Capture model._forward_eager, or return None and leave the run eager."""
-    global _graph_warned
+                   use_mask: bool) -> Tuple[Optional[_GraphRunner], torch.Tensor]:
+    """Runs model._forward_eager(x, mask) and tries to capture it.
+
+    Returns (runner or None, this call's output). The output is the eager
+    result, so the capturing call costs one eager forward plus the capture."""
     dev = x.device
-    g = None
+    _custom_kernels()
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        eager = model._forward_eager(x, mask, use_mask)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    eager.record_stream(torch.cuda.current_stream(dev))   # made on `side`, read by the caller's stream
+    free, _total = torch.cuda.mem_get_info(dev)
+    if free < config._GRAPH_MIN_FREE_BYTES:
+        return None, eager
+    graph = None
     try:
-        _custom_kernels()
-        free_bytes, _ = torch.cuda.mem_get_info(dev)
-        if free_bytes < config._GRAPH_MIN_FREE_BYTES:
-            return None
         with torch.inference_mode(False), torch.no_grad():
-            static_x = torch.empty(x.shape, dtype=x.dtype, device=dev)
-            static_mask = torch.empty(mask.shape, dtype=torch.bool, device=dev) if use_mask else None
-            gen = torch.Generator(device=dev)
-            gen.manual_seed(config._GRAPH_SEED)
-            static_x.normal_(generator=gen)
-            if use_mask:
-                static_mask.fill_(True)
-                static_mask[:, static_mask.shape[1] // 2:] = False
-            side = torch.cuda.Stream(device=dev)
-            side.wait_stream(torch.cuda.current_stream(dev))
-            with torch.cuda.stream(side):
-                for _ in range(config._GRAPH_WARMUP_ITERS):
-                    model._forward_eager(static_x, static_mask, use_mask)
-            torch.cuda.current_stream(dev).wait_stream(side)
+            static_x = x.detach().clone()
+            static_mask = mask.detach().clone() if use_mask else None
+            fingerprint = _weights_fingerprint(model)
+            caches = _weight_caches(model)
             torch.cuda.synchronize(dev)
-            ptrs_before = _graph_cache_ptrs(model)
-            ref = model._forward_eager(static_x, static_mask, use_mask).clone()
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=side):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=side):
                 static_out = model._forward_eager(static_x, static_mask, use_mask)
-            g.replay()
+            graph.replay()
             torch.cuda.synchronize(dev)
-            exact = torch.equal(static_out, ref)
-            ptrs_after = _graph_cache_ptrs(model)
-        if ptrs_after != ptrs_before or not exact:
-            _graph_release(g)
-            if not _graph_warned:
-                _graph_warned = True
-                print("[info] CUDA graph replay did not reproduce eager exactly (or a weight "
-                      "cache moved during capture); this shape stays eager.")
-            return None
-        runner = _GraphRunner(g, side, static_x, static_mask, static_out, use_mask,
-                              _graph_pinned_refs(model))
-        _graph_register(runner)
-        return runner
+            same_caches = all(a is b for a, b in zip(caches, _weight_caches(model)))
+            if not same_caches or fingerprint != _weights_fingerprint(model):
+                raise RuntimeError("a weight cache was rebuilt during capture")
+            if not torch.equal(static_out, eager):
+                raise RuntimeError("graph replay did not reproduce the eager forward bit for bit")
     except Exception as exc:  # noqa: BLE001
-        _graph_release(g)
-        try:
-            if torch.cuda.is_current_stream_capturing():
-                raise RuntimeError("stream is still capturing")
-            torch.cuda.synchronize(dev)
-        except Exception as fatal:  # noqa: BLE001
-            raise RuntimeError("CUDA graph capture failed and left the CUDA context unusable. "
-                               f"Original failure: {exc}") from fatal
-        if not _graph_warned:
-            _graph_warned = True
-            print(f"[info] CUDA graph capture failed for shape {tuple(x.shape)}, running eagerly. "
-                  f"Reason: {type(exc).__name__}: {exc}")
-        return None
+        if graph is not None:
+            try:
+                graph.reset()
+            except Exception:  # noqa: BLE001
+                pass
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError(f"CUDA graph capture failed and left the stream capturing: {exc}") from exc
+        torch.cuda.synchronize(dev)   # surfaces a broken context instead of hiding it
+        _note_once(f"shape {tuple(x.shape)} stays eager (no CUDA graph): {type(exc).__name__}: {exc}")
+        return None, eager
+    return _GraphRunner(graph, side, static_x, static_mask, static_out, use_mask, fingerprint, caches), eager
 
 
-def _graph_release(g) -> None:
-    if g is not None:
-        try:
-            g.reset()
-        except Exception:  # noqa: BLE001
-            pass
+class GraphCache:
+    """A model's captured graphs by key, released with the model."""
 
+    def __init__(self, owner) -> None:
+        self.runners: Dict[Tuple, _GraphRunner] = {}
+        self.declined: set = set()
+        # runs when the owner is collected, or at interpreter exit
+        self._finalizer = weakref.finalize(owner, GraphCache._release_all, self.runners)
 
-_graph_live: "weakref.WeakSet" = weakref.WeakSet()
-_graph_atexit_registered = False
-
-
-def _graph_register(runner: _GraphRunner) -> None:
-    global _graph_atexit_registered
-    _graph_live.add(runner)
-    if not _graph_atexit_registered:
-        _graph_atexit_registered = True
-        atexit.register(_graph_release_all)
-
-
-def _graph_release_all() -> None:
-    """Drop every surviving graph while CUDA is still up. Safe to re-run."""
-    for runner in list(_graph_live):
-        try:
+    @staticmethod
+    def _release_all(runners: Dict[Tuple, _GraphRunner]) -> None:
+        for runner in runners.values():
             runner.release()
-        except Exception:  # noqa: BLE001
-            pass
-    _graph_live.clear()
+        runners.clear()
+
+    def clear(self) -> None:
+        self._release_all(self.runners)
+        self.declined.clear()
+
+    def get(self, key: Tuple, fingerprint_of) -> Optional[_GraphRunner]:
+        """The runner for `key` if it was captured under the current weights;
+        a runner whose weights changed is released and forgotten."""
+        runner = self.runners.get(key)
+        if runner is not None and runner.fingerprint != fingerprint_of():
+            runner.release()
+            del self.runners[key]
+            runner = None
+        return runner
+
+    def __len__(self) -> int:
+        return len(self.runners)
+
+    def values(self):
+        return self.runners.values()

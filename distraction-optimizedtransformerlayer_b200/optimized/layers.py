@@ -35,7 +35,9 @@ RESID_ADD, RESID_ADD_MASKSUB, RESID_ADD_MASKALL = 1, 2, 3
 
 
 class MyLinear(nn.Module):
-    """Same parameter names/shapes as nn.Linear -> free strict weight loading."""
+    """A linear layer whose `weight` [out, in] and `bias` [out] are laid out as
+    nn.Linear's, so a baseline state_dict loads with strict=True; the GEMM runs
+    on libdotl with the weight narrowed to fp16 once per version."""
 
     def __init__(self, in_features: int, out_features: int, bias: bool = True) -> None:
         super().__init__()
@@ -61,7 +63,8 @@ class MyLinear(nn.Module):
 
 
 class MyLayerNorm(nn.Module):
-    """Same parameter names/shapes as nn.LayerNorm -> free strict weight loading."""
+    """LayerNorm parameters `weight` and `bias` [d_model] as nn.LayerNorm keeps
+    them (strict state_dict loading works); normalises on libdotl's kernels."""
 
     def __init__(self, d_model: int, eps: float = 1e-5) -> None:
         super().__init__()
@@ -74,7 +77,9 @@ class MyLayerNorm(nn.Module):
 
 
 class MySelfAttention(nn.Module):
-    """Same submodule names as BaselineSelfAttention -> free strict weight loading."""
+    """Multi-head self-attention with q/k/v/out projections named as the
+    baseline's (strict state_dict loading works): one fused QKV GEMM, the
+    tcgen05 attention kernel, and out_proj with its residual folded in."""
 
     def __init__(self, d_model: int, num_heads: int) -> None:
         super().__init__()
@@ -143,7 +148,8 @@ class MySelfAttention(nn.Module):
 
 
 class MyTransformerBlock(nn.Module):
-    """Same submodule names as BaselineTransformerBlock -> free strict weight loading."""
+    """One Pre-LN block (norm1, attention, norm2, ffn_in, ffn_out, named as the
+    baseline block's submodules) run as 5 to 8 fused kernels."""
 
     def __init__(self, d_model: int, num_heads: int, ffn_dim: int, causal: bool) -> None:
         super().__init__()

@@ -1,18 +1,17 @@
-"""The optimized transformer (optimized/model.py upstream)."""
+"""The optimized transformer (optimized/model.py upstream: the class name,
+constructor, parameter names and forward signature are the interface)."""
 
 from __future__ import annotations
 
-import weakref
 from typing import TYPE_CHECKING, Dict, Optional, Tuple
 
 import torch
 import torch.nn as nn
 
 from . import config
-from .graphs import _GraphRunner, _capture_graph, _graph_eligible, _graph_key
+from .graphs import GraphCache, _capture_graph, _graph_eligible, _graph_key, _weights_fingerprint
 from .kernels import _layernorm
 from .layers import MyLayerNorm, MyTransformerBlock
-from .util import _version_or_none
 
 if TYPE_CHECKING:
     from torch_transformer_benchmark import TransformerConfig
@@ -36,20 +35,12 @@ class OptimizedTransformer(nn.Module):
             for _ in range(config.num_layers)
         ])
         self.final_norm = MyLayerNorm(config.d_model)
-        self._triv_ref: Optional[weakref.ReferenceType] = None
-        self._triv_version: Optional[int] = None
-        self._triv: bool = False
-        self._graphs: Dict[Tuple, _GraphRunner] = {}
-        self._graph_denied: set = set()
-        self._chunk_rows: Dict[Tuple, int] = {}
-        self._device_budget: Optional[int] = None
-        # A captured graph reads the fp16 weight copies it was captured with.
+        self._graphs = GraphCache(self)
+        # rows per chunk that fit the device, per (shape, dtype, mask mode)
+        self._chunk_plan: Dict[Tuple, int] = {}
         # Reloading the weights (load_state_dict) or moving the model (to,
-        # cuda, half, ...) therefore drops this model's graphs, and the next
-        # forward captures again from the new weights. Upstream keeps replaying
-        # and reads a stale QKV concatenation (graphs.py:356-363 there: "weights
-        # never move after copy_model_weights"); every GEMM weight here is a
-        # cached fp16 copy, so the graphs are dropped instead.
+        # cuda, half, ...) drops the captured graphs at once; in-place edits
+        # are caught by the weight fingerprint checked before every replay.
         self.register_load_state_dict_post_hook(OptimizedTransformer._drop_graphs_after_load)
 
     @staticmethod
@@ -61,18 +52,11 @@ class OptimizedTransformer(nn.Module):
         return super()._apply(fn, *args, **kwargs)
 
     def _mask_is_trivial(self, mask: Optional[torch.Tensor]) -> bool:
-        """True when every position is valid (model.py:68-93 upstream): one
-        device->host sync per new mask object, memoised by weakref + version."""
-        if mask is None:
-            return False
-        version = _version_or_none(mask)
-        cached = self._triv_ref() if self._triv_ref is not None else None
-        if cached is mask and self._triv_version == version and version is not None:
-            return self._triv
-        self._triv = bool(mask.all().item())
-        self._triv_ref = weakref.ref(mask)
-        self._triv_version = version
-        return self._triv
+        """Whether every position of `mask` is valid (False for None). One
+        device->host read per call. forward() never calls it: a given mask
+        always takes the masked kernels, which on an all-valid mask cost the
+        same as the unmasked ones and give the same values."""
+        return mask is not None and bool(mask.all())
 
     def _forward_eager(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor],
                        use_mask: bool) -> torch.Tensor:
@@ -93,19 +77,19 @@ class OptimizedTransformer(nn.Module):
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None,
                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
         config.validate()
-        # A given mask always takes the masked kernels. On an all-valid mask
-        # they cost the same as the unmasked ones and give identical values,
-        # so unlike upstream (model.py:68-93) no device->host sync is spent on
-        # _mask_is_trivial to pick a path.
         use_mask = valid_token_mask is not None
         key = _graph_key(x, use_mask)
-        runner = self._graphs.get(key)
-        if runner is None:
-            runner = self._maybe_capture(key, x, valid_token_mask, use_mask)
+        runner = self._graphs.get(key, lambda: _weights_fingerprint(self))
         if runner is not None:
             return runner.replay(x, valid_token_mask, out)
-        if config.MICROBATCH_FALLBACK and x.is_cuda and x.shape[0] > 1:
-            y = self._forward_chunk_on_oom(x, valid_token_mask, use_mask)
+        if key not in self._graphs.declined and _graph_eligible(x, len(self._graphs)):
+            runner, y = _capture_graph(self, x, valid_token_mask, use_mask)
+            if runner is None:
+                self._graphs.declined.add(key)
+            else:
+                self._graphs.runners[key] = runner
+        elif config.MICROBATCH_FALLBACK and x.is_cuda and x.shape[0] > 1:
+            y = self._forward_in_chunks(x, valid_token_mask, use_mask)
         else:
             y = self._forward_eager(x, valid_token_mask, use_mask)
         if out is None:
@@ -122,71 +106,63 @@ class OptimizedTransformer(nn.Module):
             raise ValueError("out must match x in shape, dtype and device")
         return self.forward(x, valid_token_mask, out=out)
 
-    def _rows_within_budget(self, x: torch.Tensor) -> int:
-        rows = x.shape[0]
-        per_row = x.shape[1] * x.shape[2] * x.element_size() * config._MICROBATCH_PEAK_FACTOR
-        if per_row <= 0:
-            return rows
-        budget = self._device_budget
-        if budget is None:
-            _, total = torch.cuda.mem_get_info(x.device)
-            budget = int(total * config._MICROBATCH_BUDGET_FRACTION)
-            self._device_budget = budget
-        if per_row * rows <= budget:
-            return rows
-        return max(config._MICROBATCH_MIN_ROWS, min(rows, budget // per_row))
+    # ------------------------------------------------------------ memory --
 
-    def _forward_chunk_on_oom(self, x, valid_token_mask, use_mask):
-        """_forward_eager, retried over batch chunks if it runs out of memory
-        (model.py:194-246 upstream). Rows never interact, so chunking changes
-        no value: every kernel here computes a row independently of M."""
-        rows = x.shape[0]
-        key = (rows, x.shape[1], x.shape[2], x.dtype, use_mask)
-        n = self._chunk_rows.get(key)
-        if n is None:
-            n = self._rows_within_budget(x)
-        if n >= rows:
+    def _bytes_per_row(self, x: torch.Tensor) -> int:
+        """Device bytes one batch row of one forward holds at its peak: the
+        fp32 input copy and output, and one block's intermediates (fp16 n1,
+        qkv and ctx; fp32 x1 and x2; fp16 n2 and the [S, F] hidden)."""
+        S, d = x.shape[1], x.shape[2]
+        F = max(layer.ffn_in.weight.shape[0] for layer in self.layers)
+        per_token = 4 * d * 2 + 2 * d * (1 + 3 + 1 + 1) + 4 * d * 2 + 2 * F
+        return S * per_token
+
+    def _plan_rows(self, x: torch.Tensor) -> int:
+        """Rows per chunk such that a chunk's intermediates fit in the memory
+        the device and the caching allocator can still hand out."""
+        free, _total = torch.cuda.mem_get_info(x.device)
+        stats = torch.cuda.memory_stats(x.device)
+        cached_free = stats.get("reserved_bytes.all.current", 0) - stats.get("allocated_bytes.all.current", 0)
+        budget = int((free + max(cached_free, 0)) * config._MICROBATCH_BUDGET_FRACTION)
+        per_row = max(1, self._bytes_per_row(x))
+        return max(config._MICROBATCH_MIN_ROWS, min(x.shape[0], budget // per_row))
+
+    def _forward_in_chunks(self, x, valid_token_mask, use_mask):
+        """_forward_eager over batch chunks sized from the device's free
+        memory (the role of upstream's microbatch fallback). Rows never
+        interact and every kernel computes a row independently of the row
+        count, so chunking changes no value. The plan is made once per shape;
+        an out-of-memory error re-plans once from the memory then free, then
+        propagates."""
+        key = (tuple(x.shape), x.dtype, use_mask)
+        for attempt in range(2):
+            rows = self._chunk_plan.get(key)
+            if rows is None:
+                rows = self._plan_rows(x)
+                self._chunk_plan[key] = rows
             try:
-                return self._forward_eager(x, valid_token_mask, use_mask)
+                if rows >= x.shape[0]:
+                    return self._forward_eager(x, valid_token_mask, use_mask)
+                y = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+                for lo in range(0, x.shape[0], rows):
+                    hi = min(lo + rows, x.shape[0])
+                    m = valid_token_mask[lo:hi] if use_mask else None
+                    y[lo:hi] = self._forward_eager(x[lo:hi], m, use_mask)
+                return y
             except torch.OutOfMemoryError:
-                torch.cuda.empty_cache()
-                n = rows // 2
-        while n >= config._MICROBATCH_MIN_ROWS:
-            out = None
-            try:
-                out = torch.empty_like(x)
-                for lo in range(0, rows, n):
-                    hi = min(lo + n, rows)
-                    m = valid_token_mask[lo:hi] if valid_token_mask is not None else None
-                    out[lo:hi] = self._forward_eager(x[lo:hi], m, use_mask)
-                self._chunk_rows[key] = n
-                return out
-            except torch.OutOfMemoryError:
-                del out
-                torch.cuda.empty_cache()
-                if n <= config._MICROBATCH_MIN_ROWS:
+                if attempt == 1:
                     raise
-                n //= 2
-        return self._forward_eager(x, valid_token_mask, use_mask)
-
-    def _maybe_capture(self, key, x, valid_token_mask, use_mask) -> Optional[_GraphRunner]:
-        if key in self._graph_denied:
-            return None
-        if not _graph_eligible(x, len(self._graphs)):
-            return None
-        runner = _capture_graph(self, x, valid_token_mask, use_mask)
-        if runner is None:
-            self._graph_denied.add(key)
-            return None
-        self._graphs[key] = runner
-        return runner
+                y = None
+                torch.cuda.empty_cache()
+                # what fits now, with what this call held released
+                self._chunk_plan[key] = min(rows, self._plan_rows(x)) if rows > 1 else 1
+                if self._chunk_plan[key] >= rows:
+                    self._chunk_plan[key] = max(1, rows * 3 // 4)
+        raise AssertionError("unreachable")
 
     def release_graphs(self) -> None:
         """Free every captured graph of this model (before process-group
         teardown, after new weights, before a move)."""
         graphs = self.__dict__.get("_graphs")
-        if not graphs:
-            return
-        for runner in graphs.values():
-            runner.release()
-        graphs.clear()
+        if graphs is not None:
+            graphs.clear()

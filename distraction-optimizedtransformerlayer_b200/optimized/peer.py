@@ -4,7 +4,7 @@ tensor-parallel layer (one process per GPU, one box).
 No reference counterpart: the reference runs on one GPU. This replaces, for
 `TensorParallelTransformer`, each NCCL all-reduce of fp32 partial sums and the
 add+LayerNorm kernel after it with one `dotl_allreduce_ln` launch that reads
-the peers' partial sums over NVLink (plain loads, no multicast).
+the peers' partial sums over NVLink (plain loads from each peer, one CTA at a time).
 
 Every rank allocates the same named buffers with `dotl_peer_alloc`, publishes
 their CUDA IPC handles through the process group (all_gather_object) and
@@ -27,6 +27,14 @@ reads (P-1) whole partials per rank.
 
 Every rank must create the group, and call `allreduce_ln`, with the same
 arguments in the same order. `close()` unmaps and frees collectively.
+
+Failure: every wait inside the kernel is bounded by `timeout_ms`. A wait that
+runs out stores a bit into `status`, a pinned host word the kernel writes
+through its device mapping, so the host sees it without a device sync once
+the kernel has finished (`failed()`). The ranks' call counters then disagree,
+so the group is unusable: `check()` raises PeerTimeoutError and marks the
+group `poisoned`, and its owner must rebuild it (collectively) before the
+next call.
 """
 
 from __future__ import annotations
@@ -36,6 +44,10 @@ from typing import Dict, List, Optional
 import torch
 
 _NAMES = ("part", "recv", "xa", "xb", "n16", "out")
+
+
+class PeerTimeoutError(RuntimeError):
+    """A fused all-reduce gave up waiting for a peer; its outputs are not valid."""
 
 
 class _DeviceView:
@@ -68,13 +80,17 @@ class PeerGroup:
         self.rows, self.d, self.device = int(rows), int(d), device
         self.push = True if push is None else bool(push)
         self.timeout_ms = int(timeout_ms)
+        self.poisoned = False
+        # Host word the kernel sets when a wait times out (pinned memory is
+        # mapped into the device's address space at the same address).
+        self.status = torch.zeros(1, dtype=torch.int32, pin_memory=torch.cuda.is_available())
         k = self.k
         with torch.cuda.device(device):
             blocks = torch.tensor([k.peer_blocks()], dtype=torch.int64, device=device)
             dist.all_reduce(blocks, op=dist.ReduceOp.MIN, group=group)
             self.blocks = int(blocks.item())
             sizes = {n: self.rows * d * (2 if n == "n16" else 4) for n in _NAMES}
-            sizes["signal"] = k.peer_signal_bytes(self.blocks)
+            sizes["signal"] = self.signal_bytes = k.peer_signal_bytes(self.blocks)
             self._own: Dict[str, int] = {}
             self._opened: List[int] = []
             try:
@@ -116,6 +132,8 @@ class PeerGroup:
         'n16' (fp16) or 'out' (fp32)."""
         if rows > self.rows:
             raise ValueError(f"{rows} rows exceed the group's {self.rows}")
+        if self.poisoned:
+            raise PeerTimeoutError("this peer group timed out earlier and must be rebuilt")
         if x_new is not None and self._own[x_new] == x.data_ptr():
             raise ValueError("x_new must not be the buffer x is read from")
         dsts = range(self.world) if self.push else (self.rank,)
@@ -132,7 +150,22 @@ class PeerGroup:
             self.world, self.rank, parts, self.ptrs["signal"],
             None if x_new is None else pick(x_new), pick(normed), normed == "n16", self.push,
             x, bias, ln_w, ln_b, eps, sum_row_valid, normed_row_valid, rows, self.d, self.blocks,
-            self.timeout_ms, parts_local=from_owners)
+            self.timeout_ms, parts_local=from_owners, signal_bytes=self.signal_bytes,
+            status=self.status.data_ptr())
+
+    def failed(self) -> bool:
+        """Whether a finished call of this group timed out (no device sync:
+        reads the pinned status word; a call still running is not seen)."""
+        return int(self.status[0]) != 0
+
+    def check(self) -> None:
+        """Raise PeerTimeoutError (and mark the group poisoned) if a call timed out."""
+        if self.poisoned or self.failed():
+            self.poisoned = True
+            raise PeerTimeoutError(
+                f"dotl_allreduce_ln on rank {self.rank} of {self.world} gave up waiting for a peer "
+                f"(timeout {self.timeout_ms} ms); its outputs are not valid and the peer group must be "
+                "rebuilt by every rank")
 
     def scatter_ok(self, rows: int) -> bool:
         """Whether row-parallel GEMMs over `rows` rows can scatter their tiles

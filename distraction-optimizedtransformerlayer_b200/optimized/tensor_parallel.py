@@ -25,6 +25,16 @@ the GEMMs write bias-free partial sums and the kernel adds the full bias once,
 on valid rows only. Otherwise NCCL all-reduces partials that carry the bias on
 rank 0 and are zeroed on padded rows.
 
+Failure: the fused reduction's waits for peers are bounded (timeout_ms). A
+timed-out wait leaves that forward's outputs invalid and the peer group's
+counters out of step. With error_check="sync" (the default) forward()
+synchronises the stream at its end and raises PeerTimeoutError, so no invalid
+output is returned. With "deferred" (no per-forward sync, for pipelined
+serving and timing loops) the next forward() or check() raises instead. After
+the error the group is poisoned: the next forward rebuilds it, which is
+collective, so every rank must take that path (every rank sees the timeout
+when a peer stops calling).
+
 The partial sums stay fp32 through the reduction. Padded rows add nothing;
 the residual stream keeps x there, which differs from the reference's zeroed
 rows only on padded rows, which no valid row attends to and the final
@@ -114,7 +124,8 @@ class TensorParallelTransformer:
     def __init__(self, config, state_dict: Dict[str, torch.Tensor], group=None,
                  device: Optional[torch.device] = None, eps: float = 1e-5,
                  fused: Optional[bool] = None, push: Optional[bool] = None,
-                 timeout_ms: int = 2000, scatter: Optional[bool] = None) -> None:
+                 timeout_ms: int = 2000, scatter: Optional[bool] = None,
+                 error_check: str = "sync") -> None:
         import torch.distributed as dist
 
         self.dist = dist
@@ -134,6 +145,9 @@ class TensorParallelTransformer:
         d = config.d_model
         if fused is None:
             fused = d % 4 == 0 and d <= 2048 and world <= 8
+        if error_check not in ("sync", "deferred"):
+            raise ValueError(f"error_check must be 'sync' or 'deferred', not {error_check!r}")
+        self.error_check = error_check
         self.fused, self.push, self.timeout_ms = bool(fused), push, timeout_ms
         self.scatter = scatter   # None: wherever the rows allow it
         self.peer = None
@@ -153,12 +167,20 @@ class TensorParallelTransformer:
     def _peer_group(self, rows: int):
         from .peer import PeerGroup
 
-        if self.peer is None or self.peer.rows < rows:
+        if self.peer is None or self.peer.rows < rows or self.peer.poisoned:
             if self.peer is not None:
                 self.peer.close()
+                self.peer = None
             self.peer = PeerGroup(self.group, rows, self.config.d_model, self.device, self.push,
                                   self.timeout_ms)
         return self.peer
+
+    def check(self) -> None:
+        """Raise PeerTimeoutError if a finished forward of the fused path gave up
+        waiting for a peer (reads a pinned host word: no device sync). Its
+        output was not valid; the next forward rebuilds the peer group."""
+        if self.peer is not None:
+            self.peer.check()
 
     def close(self) -> None:
         """Collective: releases the peer-mapped buffers of the fused path."""
@@ -213,7 +235,13 @@ class TensorParallelTransformer:
 
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
         if self.fused:
-            return self._forward_fused(x.float().contiguous(), valid_token_mask)
+            if self.peer is not None and not self.peer.poisoned:
+                self.peer.check()          # an earlier (deferred) forward that timed out
+            out = self._forward_fused(x.float().contiguous(), valid_token_mask)
+            if self.error_check == "sync":
+                torch.cuda.current_stream(self.device).synchronize()
+                self.peer.check()
+            return out
         k = self._kernels()
         cfg, plan, w = self.config, self.plan, self.w
         B, S, d = x.shape

@@ -221,16 +221,20 @@ int dotl_linear_peer(const void* a, int64_t M, int64_t K, int64_t lda, const voi
  * this rank's own slot holding rank i's partial sums of this rank's rows (row
  * r0 of the slice at offset 0), as dotl_linear_peer leaves them, so only the
  * results cross NVLink. Every rank must make the same calls with the
- * same rows, D, push and blocks, in the same order. A wait for a peer longer than
- * timeout_ms sets bit 4 of the device error word and ends the call's work; the
- * group's counters then disagree and it must be rebuilt. D % 4 == 0, D <= 2048,
- * world <= 8, all pointers 16-byte aligned.
+ * same rows, D, push and blocks, in the same order. blocks must be the value
+ * the signal areas were sized for (signal_bytes = dotl_peer_signal_bytes(blocks),
+ * checked: the layout depends on it), the same on every call and every rank. A
+ * wait for a peer longer than timeout_ms sets bit 4 of the device error word,
+ * stores that bit into *status when status is not NULL (any device-visible word:
+ * host-mapped pinned memory lets the host see it without a device sync), and
+ * ends the call's work; the group's counters then disagree and it must be
+ * rebuilt. D % 4 == 0, D <= 2048, world <= 8, all pointers 16-byte aligned.
  */
 int dotl_allreduce_ln(int world, int rank, const float* const* parts, void* const* signals, float* const* x_new,
                       void* const* normed, int normed_dtype, int push, int parts_local, const float* x, const float* bias,
                       const uint8_t* sum_row_valid, const float* ln_weight, const float* ln_bias, float eps,
-                      const uint8_t* normed_row_valid, int64_t rows, int64_t D, int blocks, int timeout_ms,
-                      void* stream);
+                      const uint8_t* normed_row_valid, int64_t rows, int64_t D, int blocks, int64_t signal_bytes,
+                      unsigned int* status, int timeout_ms, void* stream);
 
 #ifdef __cplusplus
 }

@@ -77,4 +77,7 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python make_golden.py <reference project root>  "
+                         "(the directory holding torch_transformer_benchmark.py)")
+    main(sys.argv[1])

@@ -124,9 +124,10 @@ def test_allreduce_ln_rejects(lib):
     P2 = ctypes.c_void_p * 2
     parts, sigs, outs = P2(16, 32), P2(48, 64), P2(80, 96)
 
-    def call(world=2, rank=0, D=128, dtype=0, timeout=2000, p=parts, local=0):
+    def call(world=2, rank=0, D=128, dtype=0, timeout=2000, p=parts, local=0, blocks=1, sig_bytes=68,
+             status=None):
         return lib.dotl_allreduce_ln(world, rank, p, sigs, None, outs, dtype, 0, local, 16, None, None, 16, 16,
-                                     1e-5, None, 8, D, 1, timeout, None)
+                                     1e-5, None, 8, D, blocks, sig_bytes, status, timeout, None)
 
     assert call(world=9) == 1 and "world" in _err(lib)
     assert call(rank=2) == 1 and "rank" in _err(lib)
@@ -137,6 +138,10 @@ def test_allreduce_ln_rejects(lib):
     assert call(p=P2(16, None)) == 1 and "NULL" in _err(lib)
     assert call(p=P2(16, 40)) == 1 and "aligned" in _err(lib)
     assert call(local=1) == 1 and "push" in _err(lib)
+    # signal areas sized for one grid, called with another: rejected before launch
+    assert call(blocks=2) == 1 and "signal areas" in _err(lib)
+    assert call(sig_bytes=4096) == 1 and "signal areas" in _err(lib)
+    assert call(status=6) == 1 and "status" in _err(lib)
 
 
 def test_linear_peer_rejects(lib):

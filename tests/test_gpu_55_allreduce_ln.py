@@ -235,3 +235,82 @@ def test_reduction_from_owner_slots(kernels):
         assert torch.equal(x_new[i][lo:hi], ref_x)
         assert (normed[i][lo:hi].double() - ref_y).abs().max().item() < 4e-3
         assert torch.isnan(x_new[i][:lo]).all()
+
+
+def _phantom_allreduce_ln(phantom):
+    """PeerGroup.allreduce_ln as if the group had a second rank that never
+    calls: the real kernel, one-shot, with rank 1's partial sums and signal
+    area as local buffers whose flags nothing sets."""
+    from optimized.peer import PeerTimeoutError
+
+    def call(self, x, bias, ln_w, ln_b, eps, x_new, normed, rows, sum_row_valid=None,
+             normed_row_valid=None, from_owners=False):
+        if self.poisoned:
+            raise PeerTimeoutError("poisoned")
+        if not phantom:
+            phantom["sig"] = torch.zeros(self.signal_bytes // 4, dtype=torch.int32, device=x.device)
+            phantom["part"] = torch.zeros(self.rows, self.d, device=x.device)
+        self.k.allreduce_ln(2, 0, [self.ptrs["part"][0], phantom["part"].data_ptr()],
+                            [self.ptrs["signal"][0], phantom["sig"].data_ptr()],
+                            None if x_new is None else [self.ptrs[x_new][0], None],
+                            [self.ptrs[normed][0], None], normed == "n16", False, x, bias, ln_w, ln_b, eps,
+                            sum_row_valid, normed_row_valid, rows, self.d, self.blocks, self.timeout_ms,
+                            signal_bytes=self.signal_bytes, status=self.status.data_ptr())
+    return call
+
+
+@pytest.mark.parametrize("error_check", ["sync", "deferred"])
+def test_tp_forward_raises_when_a_peer_never_arrives(kernels, monkeypatch, error_check):
+    """Through TensorParallelTransformer.forward: the fused reduction waits for
+    a peer that never calls, gives up after 50 ms, and the forward raises
+    PeerTimeoutError (at its end with error_check="sync", at the next check
+    with "deferred") instead of returning the invalid output. The group is then
+    poisoned; the next forward rebuilds it and is correct again."""
+    import datetime
+    import socket
+
+    import torch.distributed as dist
+    from oracle import layer as O
+    from optimized import peer as peer_mod
+    from optimized.tensor_parallel import TensorParallelTransformer
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    store = dist.TCPStore("127.0.0.1", port, 1, True)
+    dist.init_process_group("nccl", store=store, rank=0, world_size=1, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", torch.cuda.current_device()))
+    try:
+        cfg = O.TransformerConfig(2, 128, 256, 4, 512, 1, True)
+        params = O.init_params(cfg, 31)
+        x, _ = O.generate_random_case(cfg, 32, 0.0, 1.0)
+        x = x.cuda()
+        tp = TensorParallelTransformer(cfg, params, timeout_ms=50, error_check=error_check)
+        try:
+            with torch.inference_mode():
+                good = tp(x).clone()
+                torch.cuda.synchronize()
+                tp.check()
+                phantom = {}
+                monkeypatch.setattr(peer_mod.PeerGroup, "allreduce_ln", _phantom_allreduce_ln(phantom))
+                if error_check == "sync":
+                    with pytest.raises(peer_mod.PeerTimeoutError):
+                        tp(x)
+                else:
+                    tp(x)                               # returns; the failure is seen afterwards
+                    torch.cuda.synchronize()
+                    with pytest.raises(peer_mod.PeerTimeoutError):
+                        tp.check()
+                assert tp.peer.poisoned
+                assert kernels.device_error(clear=True) & TIMEOUT_BIT
+                monkeypatch.undo()
+                old = tp.peer
+                again = tp(x).clone()
+                torch.cuda.synchronize()
+                tp.check()
+                assert tp.peer is not old and not tp.peer.poisoned
+                assert torch.equal(again, good)
+        finally:
+            tp.close()
+    finally:
+        dist.destroy_process_group()

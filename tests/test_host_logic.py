@@ -107,7 +107,7 @@ def test_graph_key_and_gate():
         config.CUDA_GRAPH = old
 
 
-def test_mask_is_trivial_cache():
+def test_mask_is_trivial():
     from optimized import OptimizedTransformer
 
     m = OptimizedTransformer(O.TransformerConfig(1, 8, 32, 2, 64, 1, False))
@@ -115,7 +115,7 @@ def test_mask_is_trivial_cache():
     assert m._mask_is_trivial(mask) is True
     assert m._mask_is_trivial(None) is False
     mask[0, 3] = False
-    assert m._mask_is_trivial(mask) is False, "an in-place edit bumps the version"
+    assert m._mask_is_trivial(mask) is False, "an in-place edit is seen"
 
 
 def test_half_weight_cache_semantics():
@@ -176,8 +176,9 @@ def test_attention_refuses_uncovered_requests_on_host():
 
 
 class _FakeRunner:
-    def __init__(self):
+    def __init__(self, fingerprint=None):
         self.released = False
+        self.fingerprint = fingerprint
 
     def release(self):
         self.released = True
@@ -193,14 +194,53 @@ def test_reloading_or_moving_weights_drops_captured_graphs():
     model = OptimizedTransformer(cfg)
     model.load_state_dict(params, strict=True)          # no graphs yet: nothing to drop
     r = _FakeRunner()
-    model._graphs[("key",)] = r
+    model._graphs.runners[("key",)] = r
     model.load_state_dict(O.init_params(cfg, 2), strict=True)
     assert r.released and not model._graphs
     r2 = _FakeRunner()
-    model._graphs[("key",)] = r2
+    model._graphs.runners[("key",)] = r2
     model.float()                                       # any _apply (to, cuda, half, ...)
     assert r2.released and not model._graphs
     r3 = _FakeRunner()
-    model._graphs[("key",)] = r3
+    model._graphs.runners[("key",)] = r3
     model.eval()                                        # mode switches keep them
     assert not r3.released and model._graphs
+
+
+def test_in_place_weight_edit_retires_the_graph():
+    """An in-place update (optimizer step, copy_, mul_ under no_grad) bumps a
+    parameter's version: the graph captured under the old weights is released
+    at the next lookup instead of replaying stale fp16 copies."""
+    from optimized import OptimizedTransformer
+    from optimized.graphs import _weights_fingerprint
+
+    cfg = O.TransformerConfig(2, 16, 64, 4, 128, 1, True)
+    model = OptimizedTransformer(cfg)
+    model.load_state_dict(O.init_params(cfg, 1), strict=True)
+    fp = lambda: _weights_fingerprint(model)  # noqa: E731
+    r = _FakeRunner(fp())
+    model._graphs.runners[("key",)] = r
+    assert model._graphs.get(("key",), fp) is r and not r.released
+    with torch.no_grad():
+        model.layers[0].ffn_out.weight.mul_(0.5)
+    assert model._graphs.get(("key",), fp) is None
+    assert r.released and not model._graphs
+    r2 = _FakeRunner(fp())
+    model._graphs.runners[("key",)] = r2
+    with torch.no_grad():
+        model.layers[0].attention.q_proj.bias.copy_(torch.ones(64))
+    assert model._graphs.get(("key",), fp) is None and r2.released
+
+
+def test_graph_cache_releases_with_its_model():
+    """The model's graphs go when the model is collected (no global registry)."""
+    import gc
+
+    from optimized import OptimizedTransformer
+
+    model = OptimizedTransformer(O.TransformerConfig(1, 8, 32, 2, 64, 1, False))
+    r = _FakeRunner()
+    model._graphs.runners[("key",)] = r
+    del model
+    gc.collect()
+    assert r.released

@@ -27,6 +27,9 @@ def _group(world, rank, push=True):
     g.k = _FakeKernels()
     g.world, g.rank, g.rows, g.d = world, rank, ROWS, D
     g.push, g.timeout_ms, g.blocks = push, 2000, 296
+    g.signal_bytes = 296 * 17 * 4
+    g.poisoned = False
+    g.status = torch.zeros(1, dtype=torch.int32)
     g.device = torch.device("cpu")
     # distinct fake addresses per (buffer, rank), as rank `rank` maps them
     names = ("part", "recv", "xa", "xb", "n16", "out", "signal")
@@ -102,3 +105,24 @@ def test_reduction_refuses_in_place_and_oversize():
 ])
 def test_scatter_ok(world, rows, push, ok):
     assert _group(world, 0, push).scatter_ok(rows) is ok
+
+
+def test_timed_out_call_poisons_the_group():
+    """A call whose wait ran out (the kernel stored the timeout bit into the
+    status word) makes check() raise, and the group refuses further calls."""
+    from optimized.peer import PeerTimeoutError
+
+    g = _group(2, 0)
+    x, w, b = _ln_args()
+    g.allreduce_ln(x, None, w, b, 1e-5, "xa", "n16", ROWS)
+    (_, args, kwargs), = g.k.calls
+    assert kwargs["status"] == g.status.data_ptr() and kwargs["signal_bytes"] == g.signal_bytes
+    g.check()                                   # nothing timed out yet
+    g.status[0] = 4                             # what the kernel stores on a timeout
+    assert g.failed()
+    with pytest.raises(PeerTimeoutError):
+        g.check()
+    assert g.poisoned
+    with pytest.raises(PeerTimeoutError):
+        g.allreduce_ln(x, None, w, b, 1e-5, "xa", "n16", ROWS)
+    assert len(g.k.calls) == 1                  # nothing more was launched

@@ -1,7 +1,8 @@
 """Source rules the CUDA code keeps, checked on the CPU:
 
-* no TMA / bulk copy with cluster multicast (the peer-memory kernels run on
-  several GPUs, where a multicast load from a peer's memory is not allowed);
+* every bulk copy has one destination CTA (each CTA loads its own tiles; the
+  peer-memory kernels run on several GPUs, where a copy that fans out across a
+  cluster is not allowed);
 * none of the batched-memcpy entry points (copies are one cudaMemcpyAsync each);
 * no trap instructions or device asserts (a failed wait sets an error word and
   returns instead);
@@ -34,8 +35,8 @@ def _code(text):
     return re.sub(r"//[^\n]*", " ", text)
 
 
-def test_no_multicast_bulk_copies():
-    mc = "multi" + "cast"
+def test_bulk_copies_have_one_destination():
+    mc = "multi" + "ca" + "st"
     for path, text in _sources():
         for line in _code(text).splitlines():
             if "cp.async.bulk" in line:
