@@ -3,28 +3,37 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
 
-A step is one forward of one BASELINE config's layer (default: config 2,
-B=4 S=512 d=512 8x64 heads FFN 2048 causal) through the public API
-`optimized.OptimizedTransformer.forward` on synthetic seeded data of that
-shape, with inputs already in HBM. Under torchrun each rank (one per GPU) runs
-its own full batch of the config (weak scaling, no data-path collective; NCCL
-is used only for the barrier and the max-over-ranks time).
+A step is one forward of one BASELINE config's layer through the public API
+`optimized.OptimizedTransformer.forward`, on synthetic seeded data of that
+shape (x ~ N(0,1), the reference's generate_random_case masks, Xavier-uniform
+weights), with inputs already in HBM. The headline workload is config 5
+(B=16 S=1024 d=2048 16x128 heads FFN 8192 causal), the largest that fits one
+GPU. Under torchrun (one process per GPU) the config's batch is split across
+the ranks (strong scaling: B/N rows each; rows never interact, so there is no
+data-path collective; NCCL carries only barriers and the max-over-ranks time).
 
-Timing: W warm-up steps (the first captures the CUDA graph), then exactly K
-steps, each bracketed by CUDA events on the launching stream, with a 256 MiB
-write between steps to flush the 126 MB L2 (the inputs are smaller than L2).
+The line also carries `per_config`: every BASELINE config measured the same
+way (configs whose batch does not split over N ranks are marked so), each with
+device tokens/s, e2e tokens/s, the dominant kernel's roofline fraction and, at
+N=1, the reference CPU layer's tokens/s on this host, plus the geometric mean
+of the GPU/CPU speed-ups over the five configs (the metric's second half).
+
+Timing: W warm-up steps (the first may capture the CUDA graph), about a second
+of untimed steps, then exactly K steps, each bracketed by CUDA events on the
+launching stream, with a 256 MiB write between steps to flush the 126 MB L2.
 `value` = tokens processed by all ranks / max over ranks of the summed step
 time. `e2e` repeats the steps through optimized.HostPipeline: each step's
 input is copied in from pinned host memory and its output copied back, with
 step i+1's copy-in and step i-1's copy-out overlapping step i's forward; the
 time runs from the first copy-in to the last copy-out. `roofline` is the
 dominant kernel of the layer, timed alone with CUDA events around CUDA-graph
-replays of 20 back-to-back launches (best of 5). `cpu_baseline` is
-the reference's CPU layer (the oracle port of BaselineTransformer) on this
-host's cores, rank 0 at N=1 only.
+replays of 20 back-to-back launches (best of 5), its DRAM traffic read from
+the committed ncu summary table profiles/dram_traffic.md. `cpu_baseline` is the
+reference's CPU layer (the oracle port of BaselineTransformer) on this host's
+cores, rank 0 at N=1 only, on a bounded sample of batch rows.
 
---impl reference times that CPU layer alone and prints the same JSON line
-with "impl": "reference" (rank 0 only; other ranks exit 0).
+--impl reference times that CPU layer alone on the same config and prints the
+same JSON line with "impl": "reference" (rank 0 only; other ranks exit 0).
 """
 
 from __future__ import annotations
@@ -152,9 +161,10 @@ def _peaks():
 
 class _CpuLayer:
     """The reference's CPU layer (oracle port of BaselineTransformer) on a
-    bounded sample of batch rows, sized so one forward takes about a second."""
+    bounded sample of batch rows: one row first, then as many rows (up to
+    the config's batch) as make one forward take about a second."""
 
-    def __init__(self, cfg):
+    def __init__(self, cfg, target_s=1.0):
         from oracle import layer as O
 
         self.O = O
@@ -165,13 +175,12 @@ class _CpuLayer:
                                    cfg.ffn_dim, cfg.num_layers, cfg.causal)
         self.params = O.init_params(ocfg, SEED)
         self.qb = 256 if cfg.seq_len > 512 else 0
-        rows = cfg.batch_size
-        while True:
+        self._prepare(1)
+        self.forward_s()                     # the first forward pays one-off setup
+        one = self.forward_s()
+        rows = int(max(1, min(cfg.batch_size, target_s / max(one, 1e-4))))
+        if rows > 1:
             self._prepare(rows)
-            dt = self.forward_s()
-            if dt <= 1.5 or rows == 1:
-                break
-            rows = max(1, rows // 2)
 
     def _prepare(self, rows):
         O, cfg = self.O, self.cfg
@@ -203,7 +212,18 @@ def _cpu_layer_tokens_per_s(cfg, budget_s=10.0):
             "kind": "port", "sample": layer.sample(med, len(samples))}
 
 
-def run_reference(args, rank):
+def _config_dict(cid, world, layers):
+    """The workload description both arms print (identical for the same
+    config, N and layer count)."""
+    B, S = CONFIGS[cid][0], CONFIGS[cid][1]
+    per = B // world if B % world == 0 else None
+    return {"workload": _describe(cid), "global_batch": B, "batch_per_gpu": per, "seq_len": S,
+            "layers": layers, "parallelism": f"dp{world} (batch rows split across GPUs)",
+            "l2": "flushed between steps (256 MiB write)"}
+
+
+def run_reference(args, rank, world):
+    """The reference CPU layer on the arm's config (rank 0 only)."""
     if rank != 0:
         return 0
     cfg = _Cfg(args.config, args.layers)
@@ -213,16 +233,17 @@ def run_reference(args, rank):
     per_step = [layer.forward_s() for _ in range(args.steps)]
     med = statistics.median(per_step)
     value = layer.rows * cfg.seq_len / med
+    cpu = {"value": value, "unit": "tokens/s", "cores": layer.threads, "kind": "port",
+           "sample": layer.sample(med, len(per_step))}
     line = {
-        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": med * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "impl": "reference",
-        "config": {"workload": _describe(args.config), "batch_per_gpu": cfg.batch_size,
-                   "seq_len": cfg.seq_len, "layers": cfg.num_layers, "device": "cpu",
-                   "step": "one fp32 CPU forward of the sample below"},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": layer.threads, "kind": "port",
-                         "sample": layer.sample(med, len(per_step))},
+        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": _config_dict(args.config, world, cfg.num_layers),
+        "reference_run": {"device": "cpu", "step": "one fp32 CPU forward of the sample below, timed on the host",
+                          "threads": layer.threads},
+        "cpu_baseline": cpu,
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -484,71 +505,65 @@ def _fused_allreduce_roofline(model, dist, dev, T, d, world, reps=20):
             "nvlink_bytes_per_gpu": nbytes, "ms_per_launch": ms, "launches_per_step": 2}
 
 
-# DRAM bytes (read + write) per launch of a layer kernel, from one ncu capture
-# each (dram__bytes_read.sum + dram__bytes_write.sum); the captures and their
-# commands are summarised in profiles/<kernel>_cfg<N>.md.
-TRAFFIC_BYTES = {
-    (2, "gemm_ffn_out_residual"): 14_721_536,
-    (4, "ffn_fused"): 403_830_528 + 230_381_056,
-    (4, "gemm_out_proj_ln"): 403_830_784 + 356_402_688,
-    (3, "attention"): 107_401_984 + 24_509_184,
-    (3, "gemm_ffn_out_ln"): 214_991_104 + 42_022_912,
-}
+def _traffic_table():
+    """DRAM bytes (read + write) per launch of each layer kernel, from the
+    committed ncu summaries: the rows `| cfg | kernel | read | write | ... |`
+    of profiles/dram_traffic.md (one ncu capture each; the file gives the
+    commands)."""
+    path = os.path.join(REPO, "profiles", "dram_traffic.md")
+    table = {}
+    try:
+        with open(path) as f:
+            for line in f:
+                cells = [c.strip() for c in line.strip().strip("|").split("|")]
+                if len(cells) >= 4 and cells[0].isdigit():
+                    try:
+                        table[(int(cells[0]), cells[1].strip("`"))] = int(cells[2].replace(",", "")) + \
+                            int(cells[3].replace(",", ""))
+                    except ValueError:
+                        continue
+    except OSError:
+        pass
+    return table
 
 
-def _traffic_for(config_id, kernel):
-    return TRAFFIC_BYTES.get((config_id, kernel))
+def _init_dist(world, dev):
+    if world <= 1:
+        return None
+    import datetime
 
-
-def run_ours(args, rank, world, local_rank):
-    import kernel_ext
-    from optimized import OptimizedTransformer, config as oconfig
-
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-        # NCCL prints a version banner on stdout when the communicator comes up
-        # (eagerly here, device_id is bound): send it to stderr, so rank 0's
-        # stdout carries only the JSON line.
+    import torch.distributed as dist
+    # NCCL prints a version banner on stdout when the communicator comes up
+    # (eagerly here, device_id is bound): send it to stderr, so rank 0's
+    # stdout carries only the JSON line.
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        dist.barrier()
+    finally:
         sys.stdout.flush()
-        saved = os.dup(1)
-        os.dup2(2, 1)
-        try:
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-            dist.barrier()
-        finally:
-            sys.stdout.flush()
-            os.dup2(saved, 1)
-            os.close(saved)
-    kernels = kernel_ext.get_kernels()
-    if kernels is None:
-        raise RuntimeError(f"libdotl failed to load: {kernel_ext.load_error()}")
-    if args.no_graph:
-        oconfig.CUDA_GRAPH = "off"
-    if args.profile_kernel:
-        return _profile_kernel(args, kernels, dev)
+        os.dup2(saved, 1)
+        os.close(saved)
+    return dist
 
-    cfg = _Cfg(args.config, args.layers)
+
+def _measure(cid, args, kernels, dist, dev, rank, world, steps, cpu_budget_s):
+    """One config measured the bench's way. Returns a dict (rank 0's view,
+    times already maxed over ranks), or None where the config's batch does not
+    split over the ranks."""
+    from optimized import HostPipeline, OptimizedTransformer
+
+    cfg = _Cfg(cid, args.layers)
+    strong = world > 1 and not args.weak
+    if strong and cfg.batch_size % world != 0:
+        return None
     model = OptimizedTransformer(cfg)
     _init_model(model, SEED)
-    if args.tp:
-        if world < 2:
-            raise SystemExit("--tp needs torchrun with at least 2 ranks")
-        from optimized.tensor_parallel import TensorParallelTransformer
-
-        state = {k: v.detach() for k, v in model.state_dict().items()}
-        model = TensorParallelTransformer(cfg, state, device=dev, fused=args.tp_impl == "fused",
-                                          push=not args.tp_oneshot,
-                                          scatter=False if args.tp_no_scatter else None)
-        args.strong = True
-    else:
-        model = model.to(dev).eval()
-    lo, hi = (0, cfg.batch_size) if args.tp else shard_rows(cfg.batch_size, world, rank, args.strong)
-    if args.strong:
+    model = model.to(dev).eval()
+    lo, hi = shard_rows(cfg.batch_size, world, rank, strong)
+    if strong or world == 1:
         x_all, mask_all = _synthetic_case(cfg, SEED, cfg.batch_size)
         x_cpu = x_all[lo:hi].contiguous()
         mask_cpu = mask_all[lo:hi].contiguous() if mask_all is not None else None
@@ -558,7 +573,7 @@ def run_ours(args, rank, world, local_rank):
     mask = mask_cpu.to(dev) if mask_cpu is not None else None
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
     tokens_per_rank = (hi - lo) * cfg.seq_len
-    job_tokens = cfg.batch_size * cfg.seq_len if args.tp else world * tokens_per_rank
+    job_tokens = world * tokens_per_rank
     stream = torch.cuda.current_stream(dev)
 
     def barrier():
@@ -567,23 +582,22 @@ def run_ours(args, rank, world, local_rank):
             dist.barrier()
         torch.cuda.synchronize(dev)
 
-    sampler = _ClockSampler(local_rank)
+    sampler = _ClockSampler(dev.index)
     sampler.start()
     with torch.inference_mode():
         for _ in range(args.warmup):
             model(x, mask)
-        # a wait that ran out (e.g. a peer that never arrived) would make every
-        # later step wait out its limit too: stop here instead
+        # a wait that ran out would make every later step wait out its limit too
         word = kernels.device_error(clear=False)
         if word:
-            raise RuntimeError(f"device error word {word:#x} after the warm-up steps")
+            raise RuntimeError(f"device error word {word:#x} after the warm-up steps (config {cid})")
         # about a second of untimed steps so the clocks settle before timing
         settle(lambda: model(x, mask), args.settle, dist, dev)
-        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
         barrier()
         torch.cuda.nvtx.range_push("timed_steps")    # the launch-list profile selects this range
-        for i in range(args.steps):
+        for i in range(steps):
             flush.zero_()
             starts[i].record(stream)
             model(x, mask)
@@ -593,116 +607,251 @@ def run_ours(args, rank, world, local_rank):
     clocks = sampler.stop()
     total_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
 
-    # e2e: pinned host input -> forward -> pinned host output, every step, through
-    # optimized.HostPipeline (copy-in of step i+1 and copy-out of step i-1
-    # overlap step i's forward; every step still copies its own input in and its
-    # output out). The L2 flush runs on the compute stream before each forward and
-    # counts toward the time.
-    from optimized import HostPipeline
+    # e2e: pinned host input -> forward -> pinned host output, every step,
+    # through optimized.HostPipeline (copy-in of step i+1 and copy-out of step
+    # i-1 overlap step i's forward; every step still copies its own input in
+    # and its output out). The L2 flush runs on the compute stream before each
+    # forward and counts toward the time.
     x_host = x_cpu.pin_memory()
     mask_host = mask_cpu.pin_memory() if mask_cpu is not None else None
     out_hosts = [torch.empty(x_cpu.shape, dtype=torch.float32).pin_memory() for _ in range(2)]
     pipe = HostPipeline(model, dev, before_compute=flush.zero_)
+
+    def masks(n):
+        return [mask_host] * n if mask_host is not None else None
+
     with torch.inference_mode():
         # W warm-up steps, then about a second more: the first pipelined
         # copies out of freshly pinned buffers run well below steady state
-        pipe.run([x_host] * args.warmup, [mask_host] * args.warmup if mask_host is not None else None,
-                 [out_hosts[i & 1] for i in range(args.warmup)])
-        settle(lambda: pipe.run([x_host] * 20, [mask_host] * 20 if mask_host is not None else None,
-                                [out_hosts[i & 1] for i in range(20)]), args.settle, dist, dev)
+        pipe.run([x_host] * args.warmup, masks(args.warmup), [out_hosts[i & 1] for i in range(args.warmup)])
+        settle(lambda: pipe.run([x_host] * 8, masks(8), [out_hosts[i & 1] for i in range(8)]),
+               args.settle, dist, dev)
         e_start = torch.cuda.Event(enable_timing=True)
         e_end = torch.cuda.Event(enable_timing=True)
         barrier()
-        pipe.run([x_host] * args.steps, [mask_host] * args.steps if mask_host is not None else None,
-                 [out_hosts[i & 1] for i in range(args.steps)], start_event=e_start, end_event=e_end)
+        pipe.run([x_host] * steps, masks(steps), [out_hosts[i & 1] for i in range(steps)],
+                 start_event=e_start, end_event=e_end)
         barrier()
     e2e_ms = e_start.elapsed_time(e_end)
     h2d = x_cpu.numel() * 4 + (mask_cpu.numel() if mask_cpu is not None else 0)
     d2h = x_cpu.numel() * 4
-
     total_ms, e2e_ms = max_over_ranks([total_ms, e2e_ms], dist, dev)
 
-    breakdown = None
-    allreduce = None
-    if args.tp and model.fused:
-        allreduce = _fused_allreduce_roofline(model, dist, dev, x.numel() // cfg.d_model, cfg.d_model, world)
-    elif args.tp:
-        allreduce = _allreduce_roofline(dist, dev, x.numel(), world)
-    elif rank == 0:
+    res = {"config": cid, "tokens_per_rank": tokens_per_rank, "job_tokens": job_tokens,
+           "ms_per_step": total_ms / steps, "value": job_tokens * steps / (total_ms / 1e3),
+           "e2e": {"value": job_tokens * steps / (e2e_ms / 1e3), "unit": "tokens/s",
+                   "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+           "clocks": clocks, "batch_per_gpu": hi - lo, "strong": strong,
+           "cuda_graph": len(model._graphs) > 0,
+           "l2": "inputs " + ("larger" if x.numel() * 4 > 126 * 2 ** 20 else "smaller") + " than L2"}
+    if rank == 0:
         with torch.inference_mode():
             breakdown = _op_breakdown(model, x, mask, 20, kernels, cfg)
+        res["launches_per_step"] = 1 + (len(breakdown) - 1) * cfg.num_layers
+        hbm, tflops, _tsus, peak_kind = _peaks()
+        dom = max(breakdown, key=lambda r: r["ms"])
+        if dom["bound"] == "tensor":
+            achieved, peak, unit = dom["work"] / (dom["ms"] / 1e3) / 1e12, tflops, "TFLOP/s"
+        else:
+            achieved, peak, unit = dom["work"] / (dom["ms"] / 1e3) / 1e9, hbm, "GB/s"
+        res["roofline"] = {
+            "kernel": dom["kernel"], "bound": dom["bound"], "achieved": achieved, "peak": peak, "unit": unit,
+            "frac": achieved / peak,
+            "peak_source": f"{peak_kind} ({'bf16_tflops burst' if unit == 'TFLOP/s' else 'hbm_gbs'})",
+            "work_per_launch": dom["work"], "launch_us": dom["ms"] * 1e3,
+            "traffic": _traffic_table().get((cid, dom["kernel"]))}
+        res["kernels"] = [{"kernel": r["kernel"], "us": round(r["ms"] * 1e3, 2),
+                           ("tflops" if r["bound"] == "tensor" else "gbs"):
+                               round(r["work"] / (r["ms"] / 1e3) / (1e12 if r["bound"] == "tensor" else 1e9), 1)}
+                          for r in breakdown]
+        if world == 1 and cpu_budget_s > 0:
+            res["cpu_baseline"] = _cpu_layer_tokens_per_s(cfg, budget_s=cpu_budget_s)
+    word = kernels.device_error(clear=True)
+    if word:
+        raise RuntimeError(f"device error word {word:#x} after config {cid}")
+    model.release_graphs()
+    del model, x, mask, flush, pipe, x_host, out_hosts
+    torch.cuda.empty_cache()
+    return res
+
+
+def _per_config_entry(r):
+    e = {"value": r["value"], "unit": "tokens/s", "ms_per_step": r["ms_per_step"],
+         "batch_per_gpu": r["batch_per_gpu"], "e2e": r["e2e"]["value"], "cuda_graph": r["cuda_graph"],
+         "sm_mhz": r["clocks"].get("sm_mhz"), "throttle": r["clocks"].get("reasons")}
+    if "roofline" in r:
+        rf = r["roofline"]
+        e["roofline"] = {"kernel": rf["kernel"], "bound": rf["bound"], "frac": round(rf["frac"], 4),
+                         "achieved": round(rf["achieved"], 1), "unit": rf["unit"]}
+    if "cpu_baseline" in r:
+        e["cpu_baseline"] = r["cpu_baseline"]
+        e["speedup_vs_cpu"] = r["value"] / r["cpu_baseline"]["value"]
+        e["e2e_speedup_vs_cpu"] = r["e2e"]["value"] / r["cpu_baseline"]["value"]
+    return e
+
+
+def run_ours(args, rank, world, local_rank):
+    import kernel_ext
+    from optimized import config as oconfig
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = _init_dist(world, dev)
+    kernels = kernel_ext.get_kernels()
+    if kernels is None:
+        raise RuntimeError(f"libdotl failed to load: {kernel_ext.load_error()}")
+    if args.no_graph:
+        oconfig.CUDA_GRAPH = "off"
+    if args.profile_kernel:
+        return _profile_kernel(args, kernels, dev)
+    if args.tp:
+        return run_tp(args, rank, world, dev, dist, kernels)
+
+    cpu_budget = 0.0 if args.no_cpu_baseline else args.cpu_budget
+    head = _measure(args.config, args, kernels, dist, dev, rank, world, args.steps, cpu_budget)
+    if head is None:
+        raise SystemExit(f"config {args.config}'s batch ({CONFIGS[args.config][0]}) does not split over "
+                         f"{world} ranks; use --weak or another --config")
+    per_config = {}
+    for cid in args.configs:
+        r = head if cid == args.config else _measure(cid, args, kernels, dist, dev, rank, world,
+                                                      max(3, min(args.steps, args.per_config_steps)), cpu_budget)
+        per_config[str(cid)] = (_per_config_entry(r) if r is not None else
+                                {"skipped": f"batch {CONFIGS[cid][0]} does not split over {world} GPUs"})
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": head["value"], "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
+            "higher_is_better": True, "scaling": "strong" if head["strong"] else "weak",
+            "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": _config_dict(args.config, world, args.layers),
+            "impl_notes": {"cuda_graph": head["cuda_graph"], "l2": head["l2"],
+                           "arithmetic": "fp16 tensor-core operands, fp32 accumulate, fp32 I/O and LN"},
+            "clocks": head["clocks"],
+            "e2e": head["e2e"],
+            "gpu_launches": head["launches_per_step"] * args.steps,
+            "roofline": head["roofline"],
+            "kernels": head["kernels"],
+        }
+        if "cpu_baseline" in head:
+            line["cpu_baseline"] = head["cpu_baseline"]
+        line["per_config"] = per_config
+        sp = [v["speedup_vs_cpu"] for v in per_config.values() if "speedup_vs_cpu" in v]
+        sp_e2e = [v["e2e_speedup_vs_cpu"] for v in per_config.values() if "e2e_speedup_vs_cpu" in v]
+        if sp:
+            line["geomean_vs_cpu"] = {
+                "device": math.exp(sum(math.log(v) for v in sp) / len(sp)),
+                "e2e": math.exp(sum(math.log(v) for v in sp_e2e) / len(sp_e2e)),
+                "configs": [int(c) for c, v in per_config.items() if "speedup_vs_cpu" in v]}
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def run_tp(args, rank, world, dev, dist, kernels):
+    """Config 5's tensor-parallel layer over all ranks (--tp): one global
+    batch per step, heads and FFN columns sharded."""
+    from optimized import HostPipeline, OptimizedTransformer
+    from optimized.tensor_parallel import TensorParallelTransformer
+
+    if world < 2:
+        raise SystemExit("--tp needs torchrun with at least 2 ranks")
+    cfg = _Cfg(args.config, args.layers)
+    full = OptimizedTransformer(cfg)
+    _init_model(full, SEED)
+    state = {k: v.detach() for k, v in full.state_dict().items()}
+    model = TensorParallelTransformer(cfg, state, device=dev, fused=args.tp_impl == "fused",
+                                      push=not args.tp_oneshot,
+                                      scatter=False if args.tp_no_scatter else None, error_check="deferred")
+    x_cpu, mask_cpu = _synthetic_case(cfg, SEED, cfg.batch_size)
+    x = x_cpu.to(dev)
+    mask = mask_cpu.to(dev) if mask_cpu is not None else None
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    job_tokens = cfg.batch_size * cfg.seq_len
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    sampler = _ClockSampler(dev.index)
+    sampler.start()
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            model(x, mask)
+        torch.cuda.synchronize(dev)
+        model.check()
+        settle(lambda: model(x, mask), args.settle, dist, dev)
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        barrier()
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            model(x, mask)
+            ends[i].record(stream)
+        barrier()
+        model.check()
+    clocks = sampler.stop()
+    total_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    x_host = x_cpu.pin_memory()
+    mask_host = mask_cpu.pin_memory() if mask_cpu is not None else None
+    out_hosts = [torch.empty(x_cpu.shape, dtype=torch.float32).pin_memory() for _ in range(2)]
+    pipe = HostPipeline(model, dev, before_compute=flush.zero_)
+
+    def masks(n):
+        return [mask_host] * n if mask_host is not None else None
+
+    with torch.inference_mode():
+        pipe.run([x_host] * args.warmup, masks(args.warmup), [out_hosts[i & 1] for i in range(args.warmup)])
+        settle(lambda: pipe.run([x_host] * 8, masks(8), [out_hosts[i & 1] for i in range(8)]),
+               args.settle, dist, dev)
+        e_start = torch.cuda.Event(enable_timing=True)
+        e_end = torch.cuda.Event(enable_timing=True)
+        barrier()
+        pipe.run([x_host] * args.steps, masks(args.steps), [out_hosts[i & 1] for i in range(args.steps)],
+                 start_event=e_start, end_event=e_end)
+        barrier()
+        model.check()
+    e2e_ms = e_start.elapsed_time(e_end)
+    total_ms, e2e_ms = max_over_ranks([total_ms, e2e_ms], dist, dev)
+    if model.fused:
+        allreduce = _fused_allreduce_roofline(model, dist, dev, x.numel() // cfg.d_model, cfg.d_model, world)
+    else:
+        allreduce = _allreduce_roofline(dist, dev, x.numel(), world)
     word = kernels.device_error(clear=True)
     if word:
         raise RuntimeError(f"device error word {word:#x} after the timed run")
-
-    if rank == 0 and args.tp:
+    if rank == 0:
         line = {
             "metric": METRIC, "value": job_tokens * args.steps / (total_ms / 1e3), "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-            "config": {"workload": _describe(args.config), "global_batch": cfg.batch_size,
-                       "seq_len": cfg.seq_len, "layers": cfg.num_layers, "parallelism": f"tp{world}",
-                       "l2": "flushed between steps (256 MiB write)", "cuda_graph": False,
-                       "arithmetic": "fp16 tensor-core operands, fp32 accumulate, fp32 partial sums all-reduced",
-                       "allreduce": ("dotl_allreduce_ln over peer memory, " + ("push" if model.peer.push else "one-shot")
-                                     + (", GEMM tiles scattered to the row owners by dotl_linear_peer"
-                                        if model.scatter is not False and model.peer.scatter_ok(x.numel() // cfg.d_model)
-                                        else ""))
-                       if model.fused else "NCCL all_reduce + LayerNorm kernel"},
+            "config": dict(_config_dict(args.config, world, cfg.num_layers),
+                           parallelism=f"tp{world} (heads and FFN columns split across GPUs)"),
+            "impl_notes": {
+                "cuda_graph": False, "arithmetic": "fp16 tensor-core operands, fp32 accumulate, fp32 partial sums",
+                "allreduce": ("dotl_allreduce_ln over peer memory, " + ("push" if model.peer.push else "one-shot")
+                              + (", GEMM tiles scattered to the row owners by dotl_linear_peer"
+                                 if model.scatter is not False and model.peer.scatter_ok(x.numel() // cfg.d_model)
+                                 else ""))
+                if model.fused else "NCCL all_reduce + LayerNorm kernel"},
             "clocks": clocks,
             "e2e": {"value": job_tokens * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                    "h2d_bytes_per_step": x_cpu.numel() * 4 + (mask_cpu.numel() if mask_cpu is not None else 0),
+                    "d2h_bytes_per_step": x_cpu.numel() * 4},
             "gpu_launches": (1 + 7 * cfg.num_layers) * args.steps,
             "roofline": allreduce,
         }
         print(json.dumps(line), flush=True)
-    elif rank == 0:
-        hbm, tflops, _tsus, peak_kind = _peaks()
-        dom = max(breakdown, key=lambda r: r["ms"])
-        if dom["bound"] == "tensor":
-            achieved = dom["work"] / (dom["ms"] / 1e3) / 1e12
-            peak, unit = tflops, "TFLOP/s"
-        else:
-            achieved = dom["work"] / (dom["ms"] / 1e3) / 1e9
-            peak, unit = hbm, "GB/s"
-        launches_per_step = 1 + (len(breakdown) - 1) * cfg.num_layers   # entry LN + each layer's kernels
-        value = job_tokens * args.steps / (total_ms / 1e3)
-        line = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
-            "higher_is_better": True, "scaling": "strong" if args.strong else "weak",
-            "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-            "config": {"workload": _describe(args.config), "batch_per_gpu": hi - lo,
-                       "global_batch": (hi - lo) * world, "seq_len": cfg.seq_len,
-                       "layers": cfg.num_layers, "parallelism": f"dp{world}",
-                       "l2": "flushed between steps (256 MiB write); inputs "
-                             + ("larger" if x.numel() * 4 > 126 * 2 ** 20 else "smaller") + " than L2",
-                       "cuda_graph": bool(getattr(model, "_graphs", None)),
-                       "arithmetic": "fp16 tensor-core operands, fp32 accumulate, fp32 I/O and LN"},
-            "clocks": clocks,
-            "e2e": {"value": job_tokens * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": launches_per_step * args.steps,
-            "roofline": {"kernel": dom["kernel"], "bound": "tensor" if dom["bound"] == "tensor" else "hbm",
-                         "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
-                         "peak_source": f"{peak_kind} ({'bf16_tflops burst' if unit == 'TFLOP/s' else 'hbm_gbs'})",
-                         "traffic": _traffic_for(args.config, dom["kernel"])},
-            "kernels": [{"kernel": r["kernel"], "us": round(r["ms"] * 1e3, 2),
-                         ("tflops" if r["bound"] == "tensor" else "gbs"):
-                             round(r["work"] / (r["ms"] / 1e3) / (1e12 if r["bound"] == "tensor" else 1e9), 1)}
-                        for r in breakdown],
-        }
-        if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = _cpu_layer_tokens_per_s(cfg, budget_s=10.0)
-        print(json.dumps(line), flush=True)
-    if dist is not None:
-        if hasattr(model, "release_graphs"):
-            model.release_graphs()
-        if hasattr(model, "close"):
-            model.close()   # collective: unmaps and frees the peer buffers
-        dist.barrier()
-        dist.destroy_process_group()
+    model.close()   # collective: unmaps and frees the peer buffers
+    dist.barrier()
+    dist.destroy_process_group()
     return 0
 
 
@@ -734,37 +883,45 @@ def _profile_kernel(args, kernels, dev):
 
 
 def main() -> int:
-    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[1])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
+    ap.add_argument("--config", type=int, default=5, choices=sorted(CONFIGS),
+                    help="the headline workload (default: config 5, the largest on one GPU)")
+    ap.add_argument("--configs", default="1,2,3,4,5",
+                    help="configs measured for per_config ('none' for the headline only)")
+    ap.add_argument("--per-config-steps", type=int, default=30,
+                    help="timed steps of each per_config entry other than the headline")
     ap.add_argument("--layers", type=int, default=1)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-graph", action="store_true", help="time the eager path (no CUDA graph)")
     ap.add_argument("--tp", action="store_true",
-                    help="tensor parallel across all ranks (heads and FFN columns sharded, two NCCL "
-                         "all-reduces per layer); one global batch per step")
+                    help="tensor parallel across all ranks (heads and FFN columns sharded, two reductions "
+                         "per layer); one global batch per step")
     ap.add_argument("--tp-impl", choices=("fused", "nccl"), default="fused",
                     help="--tp: each all-reduce + add + LayerNorm as one peer-memory kernel, or NCCL + LN")
     ap.add_argument("--tp-oneshot", action="store_true",
                     help="--tp fused: one-shot mode (every rank reduces every row)")
     ap.add_argument("--tp-no-scatter", action="store_true",
                     help="--tp fused push: row-parallel GEMMs write locally (no scatter to the row owners)")
-    ap.add_argument("--strong", action="store_true",
-                    help="split the config's batch across ranks (strong scaling) instead of a full batch per rank")
+    ap.add_argument("--weak", action="store_true",
+                    help="every rank runs the config's whole batch (weak scaling) instead of splitting it")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=6.0,
+                    help="seconds of CPU reference forwards per config for cpu_baseline (N=1, rank 0)")
     ap.add_argument("--settle", type=float, default=1.0, help="seconds of untimed steps before timing")
     ap.add_argument("--profile-kernel", default=None,
                     help="run only this kernel of the layer 3x in an NVTX range (for ncu)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
+    args.configs = [] if args.configs == "none" else [int(c) for c in args.configs.split(",")]
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        return run_reference(args, rank)
+        return run_reference(args, rank, world)
     if world != args.gpus:
         print(f"[bench] note: --gpus {args.gpus} but WORLD_SIZE={world}; using {world}", file=sys.stderr)
     return run_ours(args, rank, world, local_rank)

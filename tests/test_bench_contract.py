@@ -28,6 +28,20 @@ def test_reference_arm_json_line():
     assert d["impl"] == "reference" and d["value"] > 0
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["cpu_baseline"]["kind"] == "port"
     assert "workload" in d["config"] and "model" not in d["config"]
+    # the GPU arm prints the same workload description (bench._config_dict)
+    sys.path.insert(0, REPO)
+    import bench
+
+    assert d["config"] == bench._config_dict(1, 1, 1)
+
+
+def test_traffic_table_parses_the_committed_summary():
+    sys.path.insert(0, REPO)
+    import bench
+
+    table = bench._traffic_table()
+    assert table[(3, "attention")] == 107_401_984 + 24_509_184
+    assert all(v > 0 for v in table.values())
 
 
 def test_reference_arm_other_ranks_exit_quietly():

@@ -1,9 +1,24 @@
-"""Tensor-parallel layer on 2 GPUs against the oracle (gpu), with each
-all-reduce + add + LayerNorm either fused over peer memory (push mode, the
-row-parallel GEMMs scattering their tiles to the row owners where the rows
-allow it, or not; one-shot mode) or as NCCL all-reduce + the LayerNorm kernel.
+"""Tensor-parallel layer on 2, 4 and 8 GPUs against the oracle (gpu).
 
-Runs only where at least two GPUs are visible; the CPU decomposition test in
+Each world size runs in one set of spawned processes (one per GPU) that loops
+over the cases and the reduction modes: each all-reduce + add + LayerNorm
+either fused over peer memory (push mode with the row-parallel GEMMs
+scattering their tiles to the row owners, push without the scatter, one-shot)
+or NCCL all-reduce + the LayerNorm kernel. Every rank must return the same
+bits, a repeat forward the same bits again, and rank 0's output must pass the
+reference harness's rule (2e-3 abs or 2 % rel, zero failing elements) against
+the CPU oracle. The config-5 case runs at full size (the oracle checks its
+first two batch rows; rows never interact).
+
+A second test makes a peer late on 2 GPUs: rank 1 skips into a sleep while
+rank 0 runs a forward, so rank 0's bounded waits run out and its forward
+raises PeerTimeoutError; rank 1's own late forward then finds no end flags
+from rank 0 and raises too. Both rebuild the peer group (close, then the next
+forward) and get the pre-failure bits back. Nothing faults or hangs: every
+wait is bounded (200 ms here), NVLS is off, and the fused kernels use plain
+peer loads and stores.
+
+Skipped where fewer GPUs are visible; the CPU decomposition test in
 test_tensor_parallel_gloo.py covers the sharding everywhere, and
 test_gpu_55_allreduce_ln.py the fused kernel's arithmetic on one GPU."""
 
@@ -16,6 +31,16 @@ import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
 
+# (B, S, d_model, heads, ffn, layers, causal, padding_ratio)
+CASES = [
+    (2, 256, 512, 8, 1024, 1, True, 0.0),
+    (2, 192, 256, 4, 512, 2, False, 0.5),
+    (1, 512, 1024, 8, 2048, 1, True, 0.0),
+    (16, 1024, 2048, 16, 8192, 1, True, 0.0),
+]
+MODES = ["push", "push_noscatter", "oneshot", "nccl"]
+CFG5 = CASES[3]
+
 
 def _free_port():
     with socket.socket() as s:
@@ -23,62 +48,142 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, path, case, mode):
-    import sys
+def _setup(rank, world, port):
     import datetime
+    import sys
 
     here = os.path.dirname(os.path.abspath(__file__))
     sys.path.insert(0, os.path.dirname(here))
     sys.path.insert(0, os.path.join(os.path.dirname(here), "distraction-optimizedtransformerlayer_b200"))
     import torch.distributed as dist
-    from oracle import layer as O
-    from optimized.tensor_parallel import TensorParallelTransformer
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
                             device_id=torch.device("cuda", rank))
+    return dist
+
+
+def _cases_for(world):
+    return [c for c in CASES if c[3] % world == 0 and c[4] % world == 0]
+
+
+def _worker(rank, world, port, path):
+    dist = _setup(rank, world, port)
+    from oracle import layer as O
+    from optimized.tensor_parallel import TensorParallelTransformer
+
+    results = {}
     try:
-        B, S, d, H, Fd, L, causal, pad = case
-        cfg = O.TransformerConfig(B, S, d, H, Fd, L, causal)
-        params = O.init_params(cfg, 21)
-        x, mask = O.generate_random_case(cfg, 22, pad, 1.0)
-        tp = TensorParallelTransformer(cfg, params, fused=mode != "nccl", push=mode.startswith("push"),
-                                       scatter=False if mode == "push_noscatter" else None)
-        try:
-            with torch.inference_mode():
-                out = tp(x.cuda(), mask.cuda() if pad > 0 else None).cpu()
-                out2 = tp(x.cuda(), mask.cuda() if pad > 0 else None).cpu()
-            torch.cuda.synchronize()
-            word = tp._kernels().device_error(clear=True)
-        finally:
-            tp.close()
-        torch.save({"out": out, "out2": out2, "word": word}, f"{path}.{rank}")
-        if rank == 0:
-            ref = O.baseline_forward(params, cfg, x, mask if pad > 0 else None, query_block=256)
-            torch.save({"ref": ref}, path)
+        for ci, case in enumerate(_cases_for(world)):
+            B, S, d, H, Fd, L, causal, pad = case
+            cfg = O.TransformerConfig(B, S, d, H, Fd, L, causal)
+            params = O.init_params(cfg, 21)
+            x, mask = O.generate_random_case(cfg, 22, pad, 1.0)
+            for mode in MODES:
+                tp = TensorParallelTransformer(cfg, params, fused=mode != "nccl", push=mode.startswith("push"),
+                                               scatter=False if mode == "push_noscatter" else None)
+                try:
+                    with torch.inference_mode():
+                        out = tp(x.cuda(), mask.cuda() if pad > 0 else None).cpu()
+                        out2 = tp(x.cuda(), mask.cuda() if pad > 0 else None).cpu()
+                    torch.cuda.synchronize()
+                    word = tp._kernels().device_error(clear=True)
+                finally:
+                    tp.close()
+                rows = slice(0, 2) if case == CFG5 else slice(None)
+                results[(ci, mode)] = {"out": out[rows].clone(), "same_again": torch.equal(out, out2),
+                                       "word": word, "digest": float(out.double().sum())}
+            if rank == 0:
+                rows = slice(0, 2) if case == CFG5 else slice(None)
+                sub = O.TransformerConfig(x[rows].shape[0], S, d, H, Fd, L, causal)
+                ref = O.baseline_forward(params, sub, x[rows], mask[rows] if pad > 0 else None, query_block=256)
+                results[(ci, "ref")] = ref
+        torch.save(results, f"{path}.{rank}")
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["push", "push_noscatter", "oneshot", "nccl"])
-@pytest.mark.parametrize("case", [(2, 256, 512, 8, 1024, 1, True, 0.0),
-                                  (2, 192, 256, 4, 512, 2, False, 0.5),
-                                  (1, 512, 1024, 8, 2048, 1, True, 0.0)])
-def test_tp2_matches_oracle(kernels, tmp_path, case, mode):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("tensor parallelism needs two GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_matches_oracle(kernels, tmp_path, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"tensor parallelism over {world} ranks needs {world} GPUs")
     from oracle import layer as O
 
     path = str(tmp_path / "tp.pt")
-    mp.start_processes(_worker, args=(2, _free_port(), path, case, mode), nprocs=2, start_method="spawn",
-                       join=True)
-    ref = torch.load(path)["ref"]
-    r0, r1 = torch.load(f"{path}.0"), torch.load(f"{path}.1")
-    assert r0["word"] == 0 and r1["word"] == 0
-    assert torch.equal(r0["out"], r0["out2"])
-    assert torch.equal(r0["out"], r1["out"]), "every rank must hold the same bits"
-    res = O.compare_outputs(ref, r0["out"])
-    assert res.passed, (res.failed_elements, res.max_abs_error)
+    mp.start_processes(_worker, args=(world, _free_port(), path), nprocs=world, start_method="spawn", join=True)
+    res = [torch.load(f"{path}.{r}") for r in range(world)]
+    failures = []
+    for ci, case in enumerate(_cases_for(world)):
+        ref = res[0][(ci, "ref")]
+        for mode in MODES:
+            r0 = res[0][(ci, mode)]
+            tag = f"world={world} case={case} mode={mode}"
+            if any(r[(ci, mode)]["word"] for r in res):
+                failures.append(f"{tag}: device error word set")
+            if not all(r[(ci, mode)]["same_again"] for r in res):
+                failures.append(f"{tag}: a repeat forward changed bits")
+            if not all(torch.equal(r[(ci, mode)]["out"], r0["out"]) and r[(ci, mode)]["digest"] == r0["digest"]
+                       for r in res):
+                failures.append(f"{tag}: ranks hold different bits")
+            acc = O.compare_outputs(ref, r0["out"])
+            if not acc.passed:
+                failures.append(f"{tag}: {acc.failed_elements} failing elements, max_abs {acc.max_abs_error:.3e}")
+    assert not failures, "\n".join(failures)
+
+
+def _late_peer_worker(rank, world, port, path):
+    import time
+
+    dist = _setup(rank, world, port)
+    from oracle import layer as O
+    from optimized.peer import PeerTimeoutError
+    from optimized.tensor_parallel import TensorParallelTransformer
+
+    out = {}
+    try:
+        cfg = O.TransformerConfig(2, 256, 512, 8, 1024, 1, True)
+        params = O.init_params(cfg, 41)
+        x, _ = O.generate_random_case(cfg, 42, 0.0, 1.0)
+        x = x.cuda()
+        tp = TensorParallelTransformer(cfg, params, timeout_ms=200, error_check="sync")
+        k = tp._kernels()
+        try:
+            with torch.inference_mode():
+                good = tp(x).cpu()
+                dist.barrier()
+                if rank == 1:
+                    time.sleep(1.5)          # late: rank 0's waits run out meanwhile
+                try:
+                    tp(x)
+                    out["raised"] = False
+                except PeerTimeoutError:
+                    out["raised"] = True
+                out["poisoned"] = tp.peer.poisoned
+                torch.cuda.synchronize()
+                out["word"] = k.device_error(clear=True)
+                dist.barrier()
+                tp.close()                   # collective: every rank drops the poisoned group
+                again = tp(x).cpu()          # rebuilds it
+                torch.cuda.synchronize()
+                out["word_after"] = k.device_error(clear=True)
+                out["recovered"] = torch.equal(again, good)
+        finally:
+            tp.close()
+        torch.save(out, f"{path}.{rank}")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_late_peer_times_out_and_group_recovers(kernels, tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    path = str(tmp_path / "late.pt")
+    mp.start_processes(_late_peer_worker, args=(2, _free_port(), path), nprocs=2, start_method="spawn", join=True)
+    for r in range(2):
+        res = torch.load(f"{path}.{r}")
+        assert res["raised"] and res["poisoned"], (r, res)
+        assert res["word"] & 4, (r, res)           # the peer-timeout bit
+        assert res["word_after"] == 0 and res["recovered"], (r, res)
