@@ -42,6 +42,12 @@ MODES = ["push", "push_noscatter", "oneshot", "nccl"]
 CFG5 = CASES[3]
 
 
+def _modes_for(world):
+    # the no-scatter push variant differs from push only in where the GEMMs
+    # write; two ranks cover it
+    return MODES if world == 2 else ["push", "oneshot", "nccl"]
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -82,7 +88,7 @@ def _worker(rank, world, port, path):
             cfg = O.TransformerConfig(B, S, d, H, Fd, L, causal)
             params = O.init_params(cfg, 21)
             x, mask = O.generate_random_case(cfg, 22, pad, 1.0)
-            for mode in MODES:
+            for mode in _modes_for(world):
                 tp = TensorParallelTransformer(cfg, params, fused=mode != "nccl", push=mode.startswith("push"),
                                                scatter=False if mode == "push_noscatter" else None)
                 try:
@@ -118,7 +124,7 @@ def test_tp_matches_oracle(kernels, tmp_path, world):
     failures = []
     for ci, case in enumerate(_cases_for(world)):
         ref = res[0][(ci, "ref")]
-        for mode in MODES:
+        for mode in _modes_for(world):
             r0 = res[0][(ci, mode)]
             tag = f"world={world} case={case} mode={mode}"
             if any(r[(ci, mode)]["word"] for r in res):
