@@ -65,6 +65,8 @@ struct AttnParams {
     void* out;
     int out_layout;      // 0: [B,H,S,hd]; 1: [B,S,H*hd]
     int head_inner;      // bit t (q=0,k=1,v=2): tensor map dims are {hd, H, rows, B}
+    int64_t out_lo;      // 0, or the element offset from `out` of a plane receiving
+                         // fp16(o - fp16(o)) (the fp16 pair of the three-product GEMM mode)
 };
 
 // Loads one 128-row box of `map` at (col, row, head, batch), in whichever
@@ -469,7 +471,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 if (grp == 0 && q_ok) {
                     __half* op = out_row();
 #pragma unroll
-                    for (int i = 0; i < HD; i += 8) *reinterpret_cast<uint4*>(op + i) = make_uint4(0, 0, 0, 0);
+                    for (int i = 0; i < HD; i += 8) {
+                        *reinterpret_cast<uint4*>(op + i) = make_uint4(0, 0, 0, 0);
+                        if (p.out_lo != 0) *reinterpret_cast<uint4*>(op + p.out_lo + i) = make_uint4(0, 0, 0, 0);
+                    }
                 }
                 continue;
             }
@@ -702,18 +707,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 if (two) tmem_ld_32x32b_x16(t_o0 + HD + cc, o1);
                 tmem_ld_wait16(o0);
                 if (two) tmem_ld_wait16(o1);
-                uint32_t w[8];
+                uint32_t w[8], wl[8];
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const float v0 = two ? fmaf(__uint_as_float(o0[2 * i]), a0, __uint_as_float(o1[2 * i]) * a1)
                                          : __uint_as_float(o0[2 * i]) * a0;
                     const float v1 = two ? fmaf(__uint_as_float(o0[2 * i + 1]), a0, __uint_as_float(o1[2 * i + 1]) * a1)
                                          : __uint_as_float(o0[2 * i + 1]) * a0;
-                    w[i] = pack_half2(v0, v1);
+                    split_half2(v0, v1, w[i], wl[i]);
                 }
                 if (q_ok) {
                     *reinterpret_cast<uint4*>(op + cc) = make_uint4(w[0], w[1], w[2], w[3]);
                     *reinterpret_cast<uint4*>(op + cc + 8) = make_uint4(w[4], w[5], w[6], w[7]);
+                    if (p.out_lo != 0) {
+                        *reinterpret_cast<uint4*>(op + p.out_lo + cc) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
+                        *reinterpret_cast<uint4*>(op + p.out_lo + cc + 8) = make_uint4(wl[4], wl[5], wl[6], wl[7]);
+                    }
                 }
             }
             tc_fence_before();

@@ -40,6 +40,7 @@ struct AttnGenericParams {
     int64_t ms0, ms1, ms2, ms3;
     __half* out;
     int out_layout;
+    int64_t out_lo;                // 0, or the element offset of the fp16 pair's lo plane
 };
 
 template <int HPL>
@@ -113,7 +114,12 @@ __global__ void __launch_bounds__(kGenRows * 32) attn_generic_kernel(const AttnG
 #pragma unroll
     for (int i = 0; i < HPL; ++i) {
         const int d = lane + 32 * i;
-        if (d < p.hd) p.out[base + d] = __float2half_rn(o[i] * inv);
+        if (d < p.hd) {
+            const float y = o[i] * inv;
+            const __half hi = __float2half_rn(y);
+            p.out[base + d] = hi;
+            if (p.out_lo != 0) p.out[p.out_lo + base + d] = __float2half_rn(y - __half2float(hi));
+        }
     }
 }
 

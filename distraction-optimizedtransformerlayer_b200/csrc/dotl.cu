@@ -257,7 +257,8 @@ int max_clusters(Kernel kernel, int cs, uint32_t smem, int* out) {
 
 template <int BN, int STAGES, bool NORM_F16>
 int launch_gemm_ln(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tn,
-                   const CUtensorMap& tr, const dotl::GemmLnParams& p, int dev, cudaStream_t stream) {
+                   const CUtensorMap& tr, const CUtensorMap& tnl, const dotl::GemmLnParams& p, int dev,
+                   cudaStream_t stream) {
     using L = dotl::GemmLnSmem<BN, STAGES>;
     auto kernel = dotl::gemm_ln_kernel<BN, STAGES, NORM_F16>;
     static DeviceFlags done;
@@ -283,7 +284,7 @@ int launch_gemm_ln(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorM
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tw, tx, tn, tr, p);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tw, tx, tn, tr, tnl, p);
     if (e != cudaSuccess) return fail(DOTL_ECUDA, "dotl_linear_ln: launch failed: %s", cudaGetErrorString(e));
     return check_launch("dotl_linear_ln");
 }
@@ -405,11 +406,13 @@ int dotl_layernorm(const float* x, const float* sub, const float* weight, const 
     const char* who = sub ? "fused_add_layernorm" : "fused_layernorm";
     if (rows < 0 || D <= 0) return fail(DOTL_EINVAL, "%s: bad shape rows=%lld D=%lld", who, (long long)rows, (long long)D);
     if (D > 2048) return fail(DOTL_EUNSUPPORTED, "%s: last dimension %lld is over the 2048 this kernel holds in registers", who, (long long)D);
-    if (normed_dtype != DOTL_F32 && normed_dtype != DOTL_F16)
-        return fail(DOTL_EINVAL, "%s: normed dtype must be DOTL_F32 or DOTL_F16", who);
+    if (normed_dtype != DOTL_F32 && normed_dtype != DOTL_F16 && normed_dtype != DOTL_F16X2)
+        return fail(DOTL_EINVAL, "%s: normed dtype must be DOTL_F32, DOTL_F16 or DOTL_F16X2", who);
     if (rows == 0) return DOTL_OK;
     if (x == nullptr || weight == nullptr || bias == nullptr || normed == nullptr)
         return fail(DOTL_EINVAL, "%s: NULL pointer", who);
+    // DOTL_F16X2: the lo plane follows the hi plane ([rows, D] each)
+    const int64_t lo_plane = normed_dtype == DOTL_F16X2 ? rows * D : 0;
     if (sub != nullptr && x_new == nullptr) return fail(DOTL_EINVAL, "%s: sub given without x_new", who);
     const bool vec = (D % 128 == 0) && aligned16(x) && aligned16(weight) && aligned16(bias) && aligned16(normed) &&
                      (sub == nullptr || (aligned16(sub) && aligned16(x_new)));
@@ -422,12 +425,12 @@ int dotl_layernorm(const float* x, const float* sub, const float* weight, const 
     cudaError_t le = cudaSuccess;
 #define DOTL_LN(EPL, VEC)                                                                                      \
     do {                                                                                                       \
-        if (normed_dtype == DOTL_F16)                                                                          \
+        if (normed_dtype != DOTL_F32)                                                                          \
             le = launch_pdl(dotl::ln_rows_kernel<EPL, VEC, __half>, grid, block, 0, s, x, sub, weight, bias,  \
-                            x_new, static_cast<__half*>(normed), row_valid, rows, Di, eps);                    \
+                            x_new, static_cast<__half*>(normed), row_valid, rows, Di, eps, lo_plane);          \
         else                                                                                                   \
             le = launch_pdl(dotl::ln_rows_kernel<EPL, VEC, float>, grid, block, 0, s, x, sub, weight, bias,   \
-                            x_new, static_cast<float*>(normed), row_valid, rows, Di, eps);                     \
+                            x_new, static_cast<float*>(normed), row_valid, rows, Di, eps, int64_t{0});         \
     } while (0)
 
     if (vec) {
@@ -452,7 +455,7 @@ int dotl_layernorm(const float* x, const float* sub, const float* weight, const 
 
 int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,
                 const float* bias, int act, const float* resid, int64_t ldr, const uint8_t* row_valid, int resid_mode,
-                void* out, int out_dtype, int64_t ldo, int tile_n, void* stream) {
+                void* out, int out_dtype, int64_t ldo, int tile_n, int operands, void* stream) {
     const char* who = act ? "linear_gelu" : "linear_bias";
     if (M < 0 || N <= 0 || K <= 0) return fail(DOTL_EINVAL, "%s: bad shape M=%lld N=%lld K=%lld", who, (long long)M, (long long)N, (long long)K);
     if (M > (int64_t)0x7fffffff - 256 || N > 0x7fffffff || K > 0x7fffffff)
@@ -460,7 +463,11 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
     if (act != 0 && act != 1) return fail(DOTL_EINVAL, "%s: act must be 0 (none) or 1 (GELU)", who);
     if (resid_mode < DOTL_RESID_NONE || resid_mode > DOTL_MASK_ROWS)
         return fail(DOTL_EINVAL, "%s: unknown residual mode %d", who, resid_mode);
-    if (out_dtype != DOTL_F32 && out_dtype != DOTL_F16) return fail(DOTL_EINVAL, "%s: out dtype must be DOTL_F32 or DOTL_F16", who);
+    if (out_dtype != DOTL_F32 && out_dtype != DOTL_F16 && out_dtype != DOTL_F16X2)
+        return fail(DOTL_EINVAL, "%s: out dtype must be DOTL_F32, DOTL_F16 or DOTL_F16X2", who);
+    if (operands != DOTL_F16 && operands != DOTL_F16X2)
+        return fail(DOTL_EINVAL, "%s: operands must be DOTL_F16 or DOTL_F16X2", who);
+    const bool x3 = operands == DOTL_F16X2;
     if (M == 0) return DOTL_OK;
     if (a == nullptr || w == nullptr || bias == nullptr || out == nullptr) return fail(DOTL_EINVAL, "%s: NULL pointer", who);
     if (K % 8 != 0 || lda % 8 != 0 || ldw % 8 != 0 || lda < K || ldw < K)
@@ -481,7 +488,8 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
 
     int dev;
     if (int rc = current_device(&dev)) return rc;
-    const int64_t nkb = (K + dotl::kGemmBK - 1) / dotl::kGemmBK;
+    // the k loop's length; the three-product mode runs three passes of K
+    const int64_t nkb = (x3 ? 3 : 1) * ((K + dotl::kGemmBK - 1) / dotl::kGemmBK);
     const int64_t mt = (M + dotl::kGemmBM - 1) / dotl::kGemmBM;
     int bn = tile_n;
     bool split2 = false;
@@ -503,15 +511,22 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
     if (bn != 64 && bn != 128 && bn != 256)
         return fail(DOTL_EINVAL, "%s: tile_n must be 0, 64, 128, 256 or -128 (split K)", who);
 
+    // DOTL_F16X2 operands: one map over both planes of each (lo rows below hi)
     CUtensorMap ta, tw;
-    const cuuint64_t adims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+    const cuuint64_t adims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(x3 ? 2 * M : M)};
     const cuuint64_t astr[1] = {static_cast<cuuint64_t>(lda) * 2};
     if (int rc = encode_f16_map(&ta, a, 2, adims, astr, dotl::kGemmBK, dotl::kGemmBM, who)) return rc;
-    const cuuint64_t wdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
+    const cuuint64_t wdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(x3 ? 2 * N : N)};
     const cuuint64_t wstr[1] = {static_cast<cuuint64_t>(ldw) * 2};
     if (int rc = encode_f16_map(&tw, w, 2, wdims, wstr, dotl::kGemmBK, static_cast<uint32_t>(bn), who)) return rc;
     CUtensorMap to;
-    if (int rc = encode_out_map(&to, out, M, N, ldo, out_dtype, who)) return rc;
+    const int store_dtype = out_dtype == DOTL_F16X2 ? DOTL_F16 : out_dtype;
+    if (int rc = encode_out_map(&to, out, M, N, ldo, store_dtype, who)) return rc;
+    // DOTL_F16X2 out: the lo plane, M rows of ldo below the hi plane
+    dotl::GemmPeerOut lo_out = {};
+    if (out_dtype == DOTL_F16X2)
+        if (int rc = encode_out_map(&lo_out.map[0], static_cast<__half*>(out) + M * ldo, M, N, ldo, DOTL_F16, who))
+            return rc;
 
     dotl::GemmParams p;
     p.M = static_cast<int>(M);
@@ -527,18 +542,24 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
     p.act = act;
     p.out = out;
     p.ldo = ldo;
+    p.x3_nkb = x3 ? static_cast<int>((K + dotl::kGemmBK - 1) / dotl::kGemmBK) : 0;
+    p.a_lo_row = x3 ? static_cast<int>(M) : 0;
+    p.w_lo_row = x3 ? static_cast<int>(N) : 0;
+    p.out_lo = out_dtype == DOTL_F16X2 ? 1 : 0;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const bool f16 = store_dtype == DOTL_F16;
+    const dotl::GemmPeerOut* po = &lo_out;
     if (split2)
-        return out_dtype == DOTL_F16 ? launch_gemm<128, 5, true, true>(ta, tw, to, p, dev, s)
-                                     : launch_gemm<128, 5, false, true>(ta, tw, to, p, dev, s);
+        return f16 ? launch_gemm<128, 5, true, true>(ta, tw, to, p, dev, s, po)
+                   : launch_gemm<128, 5, false, true>(ta, tw, to, p, dev, s, po);
     if (bn == 256)
-        return out_dtype == DOTL_F16 ? launch_gemm<256, 4, true>(ta, tw, to, p, dev, s)
-                                     : launch_gemm<256, 4, false>(ta, tw, to, p, dev, s);
+        return f16 ? launch_gemm<256, 4, true>(ta, tw, to, p, dev, s, po)
+                   : launch_gemm<256, 4, false>(ta, tw, to, p, dev, s, po);
     if (bn == 64)
-        return out_dtype == DOTL_F16 ? launch_gemm<64, 7, true>(ta, tw, to, p, dev, s)
-                                     : launch_gemm<64, 7, false>(ta, tw, to, p, dev, s);
-    return out_dtype == DOTL_F16 ? launch_gemm<128, 5, true>(ta, tw, to, p, dev, s)
-                                 : launch_gemm<128, 5, false>(ta, tw, to, p, dev, s);
+        return f16 ? launch_gemm<64, 7, true>(ta, tw, to, p, dev, s, po)
+                   : launch_gemm<64, 7, false>(ta, tw, to, p, dev, s, po);
+    return f16 ? launch_gemm<128, 5, true>(ta, tw, to, p, dev, s, po)
+               : launch_gemm<128, 5, false>(ta, tw, to, p, dev, s, po);
 }
 
 int dotl_linear_peer(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,
@@ -592,7 +613,8 @@ int dotl_linear_peer(const void* a, int64_t M, int64_t K, int64_t lda, const voi
 int dotl_linear_ln(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,
                    const float* bias, const float* resid, int64_t ldr, const uint8_t* row_valid, int resid_mode,
                    float* out, int64_t ldo, const float* ln_weight, const float* ln_bias, float eps, void* normed,
-                   int normed_dtype, int64_t ldn, const uint8_t* normed_row_valid, int tile_n, void* stream) {
+                   int normed_dtype, int64_t ldn, const uint8_t* normed_row_valid, int tile_n, int operands,
+                   void* stream) {
     const char* who = "linear_add_layernorm";
     if (M < 0 || N <= 0 || K <= 0) return fail(DOTL_EINVAL, "%s: bad shape M=%lld N=%lld K=%lld", who, (long long)M, (long long)N, (long long)K);
     if (M > (int64_t)0x7fffffff - 256 || N > 0x7fffffff || K > 0x7fffffff)
@@ -600,7 +622,11 @@ int dotl_linear_ln(const void* a, int64_t M, int64_t K, int64_t lda, const void*
     if (resid_mode != DOTL_RESID_NONE && resid_mode != DOTL_RESID_ADD && resid_mode != DOTL_RESID_ADD_MASKSUB &&
         resid_mode != DOTL_RESID_ADD_MASKALL)
         return fail(DOTL_EINVAL, "%s: residual mode %d is not one of NONE, ADD, ADD_MASKSUB, ADD_MASKALL", who, resid_mode);
-    if (normed_dtype != DOTL_F32 && normed_dtype != DOTL_F16) return fail(DOTL_EINVAL, "%s: normed dtype must be DOTL_F32 or DOTL_F16", who);
+    if (normed_dtype != DOTL_F32 && normed_dtype != DOTL_F16 && normed_dtype != DOTL_F16X2)
+        return fail(DOTL_EINVAL, "%s: normed dtype must be DOTL_F32, DOTL_F16 or DOTL_F16X2", who);
+    if (operands != DOTL_F16 && operands != DOTL_F16X2)
+        return fail(DOTL_EINVAL, "%s: operands must be DOTL_F16 or DOTL_F16X2", who);
+    const bool x3 = operands == DOTL_F16X2;
     if (!(eps >= 0.0f)) return fail(DOTL_EINVAL, "%s: eps must be >= 0", who);
     if (M == 0) return DOTL_OK;
     if (a == nullptr || w == nullptr || bias == nullptr || ln_weight == nullptr || ln_bias == nullptr || normed == nullptr)
@@ -632,18 +658,23 @@ int dotl_linear_ln(const void* a, int64_t M, int64_t K, int64_t lda, const void*
         return fail(DOTL_EUNSUPPORTED, "%s: N=%lld is not tile_n=%d times a cluster size of at most %d", who,
                     (long long)N, bn, dotl::kLnMaxCluster);
 
-    CUtensorMap ta, tw, tx, tn;
-    const cuuint64_t adims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+    CUtensorMap ta, tw, tx, tn, tnl;
+    const cuuint64_t adims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(x3 ? 2 * M : M)};
     const cuuint64_t astr[1] = {static_cast<cuuint64_t>(lda) * 2};
     if (int rc = encode_f16_map(&ta, a, 2, adims, astr, dotl::kGemmBK, dotl::kGemmBM, who)) return rc;
-    const cuuint64_t wdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
+    const cuuint64_t wdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(x3 ? 2 * N : N)};
     const cuuint64_t wstr[1] = {static_cast<cuuint64_t>(ldw) * 2};
     if (int rc = encode_f16_map(&tw, w, 2, wdims, wstr, dotl::kGemmBK, static_cast<uint32_t>(bn), who)) return rc;
+    const int nstore = normed_dtype == DOTL_F16X2 ? DOTL_F16 : normed_dtype;
     // with out == NULL the x map points at `normed` and is never used
     if (int rc = encode_out_map(&tx, out != nullptr ? static_cast<void*>(out) : normed, M, N,
-                                out != nullptr ? ldo : ldn, out != nullptr ? DOTL_F32 : normed_dtype, who))
+                                out != nullptr ? ldo : ldn, out != nullptr ? DOTL_F32 : nstore, who))
         return rc;
-    if (int rc = encode_out_map(&tn, normed, M, N, ldn, normed_dtype, who)) return rc;
+    if (int rc = encode_out_map(&tn, normed, M, N, ldn, nstore, who)) return rc;
+    // DOTL_F16X2 normed: the lo plane, M rows of ldn below the hi plane
+    tnl = tn;
+    if (normed_dtype == DOTL_F16X2)
+        if (int rc = encode_out_map(&tnl, static_cast<__half*>(normed) + M * ldn, M, N, ldn, DOTL_F16, who)) return rc;
     // residual in as 32 x 32 fp32 blocks (without a residual the map is unused)
     CUtensorMap tr = tn;
     if (resid_mode != DOTL_RESID_NONE)
@@ -665,27 +696,35 @@ int dotl_linear_ln(const void* a, int64_t M, int64_t K, int64_t lda, const void*
     p.ln_b = ln_bias;
     p.eps = eps;
     p.norm_row_valid = normed_row_valid;
+    p.x3_nkb = x3 ? static_cast<int>((K + dotl::kGemmBK - 1) / dotl::kGemmBK) : 0;
+    p.a_lo_row = x3 ? static_cast<int>(M) : 0;
+    p.w_lo_row = x3 ? static_cast<int>(N) : 0;
+    p.norm_lo = normed_dtype == DOTL_F16X2 ? 1 : 0;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const bool f16 = normed_dtype == DOTL_F16;
+    const bool f16 = nstore == DOTL_F16;
     if (bn == 256)
-        return f16 ? launch_gemm_ln<256, 3, true>(ta, tw, tx, tn, tr, p, dev, s)
-                   : launch_gemm_ln<256, 3, false>(ta, tw, tx, tn, tr, p, dev, s);
+        return f16 ? launch_gemm_ln<256, 3, true>(ta, tw, tx, tn, tr, tnl, p, dev, s)
+                   : launch_gemm_ln<256, 3, false>(ta, tw, tx, tn, tr, tnl, p, dev, s);
     if (bn == 128)
-        return f16 ? launch_gemm_ln<128, 4, true>(ta, tw, tx, tn, tr, p, dev, s)
-                   : launch_gemm_ln<128, 4, false>(ta, tw, tx, tn, tr, p, dev, s);
-    return f16 ? launch_gemm_ln<64, 6, true>(ta, tw, tx, tn, tr, p, dev, s)
-               : launch_gemm_ln<64, 6, false>(ta, tw, tx, tn, tr, p, dev, s);
+        return f16 ? launch_gemm_ln<128, 4, true>(ta, tw, tx, tn, tr, tnl, p, dev, s)
+                   : launch_gemm_ln<128, 4, false>(ta, tw, tx, tn, tr, tnl, p, dev, s);
+    return f16 ? launch_gemm_ln<64, 6, true>(ta, tw, tx, tn, tr, tnl, p, dev, s)
+               : launch_gemm_ln<64, 6, false>(ta, tw, tx, tn, tr, tnl, p, dev, s);
 }
 
 int dotl_attention(const void* q, const void* k, const void* v, int B, int H, int S, int head_dim,
                    const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, const uint8_t* mask,
                    int mask_kind, const int64_t* mask_strides, int causal, float scale, void* out, int out_layout,
-                   void* stream) {
+                   int out_dtype, void* stream) {
     const char* who = "fused_attention_forward";
     if (B < 0 || H < 0 || S < 0) return fail(DOTL_EINVAL, "%s: negative shape", who);
     if (out_layout != 0 && out_layout != 1)
         return fail(DOTL_EINVAL, "%s: out_layout must be 0 ([B,H,S,head_dim]) or 1 ([B,S,H*head_dim])", who);
     if (mask_kind < DOTL_MASK_NONE || mask_kind > DOTL_MASK_FULL) return fail(DOTL_EINVAL, "%s: unknown mask kind %d", who, mask_kind);
+    if (out_dtype != DOTL_F16 && out_dtype != DOTL_F16X2)
+        return fail(DOTL_EINVAL, "%s: out dtype must be DOTL_F16 or DOTL_F16X2", who);
+    // DOTL_F16X2: the lo plane follows the hi plane (B*H*S*head_dim elements each)
+    const int64_t out_lo = out_dtype == DOTL_F16X2 ? static_cast<int64_t>(B) * H * S * head_dim : 0;
     const bool tc = head_dim == 32 || head_dim == 64 || head_dim == 128;
     if (!tc && (head_dim < 8 || head_dim > 256 || head_dim % 8 != 0))
         return fail(DOTL_EUNSUPPORTED, "%s: head_dim must be a multiple of 8 up to 256, got %d", who, head_dim);
@@ -731,6 +770,7 @@ int dotl_attention(const void* q, const void* k, const void* v, int B, int H, in
         g.ms3 = mask_strides ? mask_strides[3] : 0;
         g.out = static_cast<__half*>(out);
         g.out_layout = out_layout;
+        g.out_lo = out_lo;
         const dim3 grid(static_cast<unsigned>((S + dotl::kGenRows - 1) / dotl::kGenRows),
                         static_cast<unsigned>(B * H));
         const dim3 block(dotl::kGenRows * 32);
@@ -745,11 +785,12 @@ int dotl_attention(const void* q, const void* k, const void* v, int B, int H, in
     }
 
     // Packed tiles run over the flat token axis: every tensor must step from
-    // one batch to the next exactly one sequence length further on.
-    bool packed = true;
+    // one batch to the next exactly one sequence length further on. Only
+    // sequences shorter than a tile are packed; longer ones get tiles of their
+    // own, so a row's key tiles start at its sequence's first key whatever the
+    // batch size, and a batch row gives the same bits alone or in a batch.
+    bool packed = S < dotl::kAttnTile;
     for (int t = 0; t < 3; ++t) packed = packed && (st[t][0] == static_cast<int64_t>(S) * st[t][2]);
-    // Per-sequence tiles when the sequences already fill 128-row tiles.
-    if (S % dotl::kAttnTile == 0) packed = false;
 
     dotl::AttnParams p;
     p.B = B;
@@ -769,6 +810,7 @@ int dotl_attention(const void* q, const void* k, const void* v, int B, int H, in
     p.ms3 = mask_strides ? mask_strides[3] : 0;
     p.out = out;
     p.out_layout = out_layout;
+    p.out_lo = out_lo;
 
     const uint32_t box_cols = head_dim < 64 ? static_cast<uint32_t>(head_dim) : 64u;
     const void* bases[3] = {q, k, v};

@@ -489,6 +489,18 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// The fp16 pair of (a, b) for the three-product GEMM mode: hi = fp16(v) and
+// lo = fp16(v - hi), both round to nearest even, so hi + lo carries v to about
+// 22 bits (a product a w then splits into a_hi w_hi + a_lo w_hi + a_hi w_lo,
+// dropping only a_lo w_lo).
+__device__ __forceinline__ void split_half2(float a, float b, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(a - hf.x, b - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
 // max(a, b, c) in one instruction (three-input max.f32, sm_100).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
     float d;

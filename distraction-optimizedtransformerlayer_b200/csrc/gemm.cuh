@@ -20,7 +20,13 @@
 //     tiles, exchanging partial halves through distributed shared memory;
 //   * PEER: each 128-row output tile is TMA-stored into the receive slot of
 //     the tensor-parallel rank that owns those rows (over NVLink), the
-//     reduce-scatter of the row-parallel GEMMs done inside the GEMM.
+//     reduce-scatter of the row-parallel GEMMs done inside the GEMM;
+//   * three-product mode (runtime, X3Pass): A and W each come as an fp16 pair
+//     of planes (hi = fp16(v), lo = fp16(v - hi)), and the k loop runs three
+//     passes into one accumulator, A_hi W_hi + A_lo W_hi + A_hi W_lo, which
+//     carries the operands to about 22 bits instead of 11 (for stacks of
+//     layers whose error would otherwise pass the harness's bound). The fp16
+//     epilogue can likewise write its output as such a pair.
 //
 // A and W are K-major (rows contiguous along K), which is both nn.Linear's
 // weight layout and the activations' row layout: no transpose anywhere.
@@ -55,6 +61,20 @@ struct GemmParams {
     int act;                 // 0 = none, 1 = exact GELU
     void* out;               // [M, ldo], fp16 or fp32
     int64_t ldo;
+    int x3_nkb;              // three-product mode: k-blocks per pass (0: one fp16 pass)
+    int a_lo_row, w_lo_row;  // three-product mode: rows of the lo planes in the A and W maps
+    int out_lo;              // fp16 out: also store the lo half through po.map[0]
+};
+
+// The three passes of the three-product mode: k-block kb of the combined loop
+// reads A plane (pass == 1 ? lo : hi) and W plane (pass == 2 ? lo : hi) at
+// k-block kb mod nkb. The planes sit in one tensor map each, the lo plane
+// a_lo / w_lo rows below the hi plane. A tile that reaches past the hi plane's
+// last row reads lo rows (or zeros) into accumulator rows or columns that are
+// never stored.
+struct X3Pass {
+    int nkb;                 // 0: a single pass
+    int a_lo, w_lo;
 };
 
 // Output tiles scattered over the ranks of a tensor-parallel group: row block
@@ -123,7 +143,7 @@ struct GemmBars {
 template <int BN, int STAGES>
 __device__ __forceinline__ void gemm_produce(const CUtensorMap* tmap_a, const CUtensorMap* tmap_w, uint32_t sbase,
                                              GemmBars<STAGES> bars, volatile int* abort_flag, const TileSched& ts,
-                                             int kb0, int kb1) {
+                                             int kb0, int kb1, X3Pass x3 = {0, 0, 0}) {
     using L = GemmSmem<BN, STAGES>;
     int stage = 0;
     uint32_t phase = 0;
@@ -135,10 +155,15 @@ __device__ __forceinline__ void gemm_produce(const CUtensorMap* tmap_a, const CU
         for (int kb = kb0; kb < kb1; ++kb) {
             if (!mbar_wait(bars.empty(stage), phase ^ 1u, abort_flag)) goto producer_done;
             mbar_arrive_expect_tx(bars.full(stage), L::kStageBytes);
-            tma_load_2d(sbase + L::kOffA + stage * kGemmATileBytes, tmap_a, bars.full(stage), kb * kGemmBK,
-                        m_blk * kGemmBM);
-            tma_load_2d(sbase + L::kOffB + stage * L::kBTileBytes, tmap_w, bars.full(stage), kb * kGemmBK,
-                        n_blk * BN);
+            int ka = kb, arow = m_blk * kGemmBM, wrow = n_blk * BN;
+            if (x3.nkb > 0) {
+                const int pass = kb / x3.nkb;
+                ka = kb - pass * x3.nkb;
+                if (pass == 1) arow += x3.a_lo;
+                if (pass == 2) wrow += x3.w_lo;
+            }
+            tma_load_2d(sbase + L::kOffA + stage * kGemmATileBytes, tmap_a, bars.full(stage), ka * kGemmBK, arow);
+            tma_load_2d(sbase + L::kOffB + stage * L::kBTileBytes, tmap_w, bars.full(stage), ka * kGemmBK, wrow);
             issued_phase[stage] = static_cast<int>(phase);
             if (++stage == STAGES) {
                 stage = 0;
@@ -264,7 +289,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint32_t tmem_base = *tmem_slot;
 
     const int num_tiles = p.num_m_tiles * p.num_n_tiles;
-    const int num_kb = (p.K + kGemmBK - 1) / kGemmBK;
+    const int num_kb = p.x3_nkb > 0 ? 3 * p.x3_nkb : (p.K + kGemmBK - 1) / kGemmBK;
+    const X3Pass x3{p.x3_nkb, p.a_lo_row, p.w_lo_row};
 
     const int cta_unit = SPLIT2 ? static_cast<int>(blockIdx.x) / 2 : static_cast<int>(blockIdx.x);
     const int units = SPLIT2 ? static_cast<int>(gridDim.x) / 2 : static_cast<int>(gridDim.x);
@@ -272,7 +298,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int kb0 = SPLIT2 ? static_cast<int>(rank) * (num_kb / 2) : 0;
     const int kb1 = SPLIT2 ? (rank == 0 ? num_kb / 2 : num_kb) : num_kb;
     if (warp == 0 && lane == 0) {
-        gemm_produce<BN, STAGES>(&tmap_a, &tmap_w, sbase, bars, abort_flag, ts, kb0, kb1);
+        gemm_produce<BN, STAGES>(&tmap_a, &tmap_w, sbase, bars, abort_flag, ts, kb0, kb1, x3);
     } else if (warp == 1 && lane == 0) {
         gemm_mma<BN, STAGES>(sbase, tmem_base, bars, abort_flag, ts, kb0, kb1);
     } else if (warp >= 2) {
@@ -428,9 +454,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 // the buffer, so before writing a half wait until the store that
                 // last read it is done: it is at most the one before the newest.
                 if (nc < p.N) {
-                    const uint32_t sb = OUT_F16 ? (nstore & 1u) * 2048u : 0u;
+                    // with the lo half the chunk takes both halves of the buffer
+                    const bool lo_out = OUT_F16 && p.out_lo != 0;
+                    const uint32_t sb = (OUT_F16 && !lo_out) ? (nstore & 1u) * 2048u : 0u;
                     if (lane == 0) {
-                        if constexpr (OUT_F16) bulk_wait_read<1>();
+                        if (OUT_F16 && !lo_out) bulk_wait_read<1>();
                         else bulk_wait_read<0>();
                     }
                     __syncwarp();
@@ -439,12 +467,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         // 64 B rows, 64B swizzle: granule q of row r at q ^ ((r >> 1) & 3)
 #pragma unroll
                         for (int q = 0; q < 4; ++q) {
-                            uint4 w;
-                            w.x = pack_half2(v[8 * q], v[8 * q + 1]);
-                            w.y = pack_half2(v[8 * q + 2], v[8 * q + 3]);
-                            w.z = pack_half2(v[8 * q + 4], v[8 * q + 5]);
-                            w.w = pack_half2(v[8 * q + 6], v[8 * q + 7]);
+                            uint4 w, l;
+                            split_half2(v[8 * q], v[8 * q + 1], w.x, l.x);
+                            split_half2(v[8 * q + 2], v[8 * q + 3], w.y, l.y);
+                            split_half2(v[8 * q + 4], v[8 * q + 5], w.z, l.z);
+                            split_half2(v[8 * q + 6], v[8 * q + 7], w.w, l.w);
                             *reinterpret_cast<uint4*>(srow + ((q ^ ((lane >> 1) & 3)) << 4)) = w;
+                            if (lo_out) *reinterpret_cast<uint4*>(srow + 2048 + ((q ^ ((lane >> 1) & 3)) << 4)) = l;
                         }
                     } else {
                         // 128 B rows, 128B swizzle: granule q of row r at q ^ (r & 7)
@@ -458,6 +487,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     __syncwarp();
                     if (lane == 0) {
                         tma_store_2d(omap, stage_addr + sb, nc, orow + quarter * 32);
+                        if (OUT_F16 && lo_out) tma_store_2d(&po.map[0], stage_addr + 2048, nc, orow + quarter * 32);
                         bulk_commit();
                     }
                     ++nstore;

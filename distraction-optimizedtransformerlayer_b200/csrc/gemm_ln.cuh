@@ -52,6 +52,9 @@ struct GemmLnParams {
     const float* ln_b;           // [N]
     float eps;
     const uint8_t* norm_row_valid;   // rows with 0 get normed = 0, or null
+    int x3_nkb;                  // three-product mode (X3Pass): k-blocks per pass, 0 = one pass
+    int a_lo_row, w_lo_row;
+    int norm_lo;                 // fp16 normed: also store its lo half through tmap_nl
 };
 
 template <int BN, int STAGES>
@@ -93,7 +96,8 @@ template <int BN, int STAGES, bool NORM_F16>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_ln_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
                    const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_n,
-                   const __grid_constant__ CUtensorMap tmap_r, const GemmLnParams p) {
+                   const __grid_constant__ CUtensorMap tmap_r, const __grid_constant__ CUtensorMap tmap_nl,
+                   const GemmLnParams p) {
     using L = GemmLnSmem<BN, STAGES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -146,13 +150,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    const int num_kb = (p.K + kGemmBK - 1) / kGemmBK;
+    const int num_kb = p.x3_nkb > 0 ? 3 * p.x3_nkb : (p.K + kGemmBK - 1) / kGemmBK;
+    const X3Pass x3{p.x3_nkb, p.a_lo_row, p.w_lo_row};
     const int cluster_id = static_cast<int>(blockIdx.x) / cs;
     const int num_clusters = static_cast<int>(gridDim.x) / cs;
     const TileSched ts{cluster_id, num_clusters, p.num_m_tiles, 1, static_cast<int>(rank)};
 
     if (warp == 0 && lane == 0) {
-        gemm_produce<BN, STAGES>(&tmap_a, &tmap_w, sbase, bars, abort_flag, ts, 0, num_kb);
+        gemm_produce<BN, STAGES>(&tmap_a, &tmap_w, sbase, bars, abort_flag, ts, 0, num_kb, x3);
     } else if (warp == 1 && lane == 0) {
         gemm_mma<BN, STAGES>(sbase, tmem_base, bars, abort_flag, ts, 0, num_kb);
     } else if (warp >= 2) {
@@ -346,14 +351,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 __syncwarp();
                 uint8_t* srow = stage_ptr + lane * (NORM_F16 ? 64 : 128);
                 if constexpr (NORM_F16) {
+                    // the lo half of the fp16 pair (three-product mode) goes
+                    // to the second half of the 4 KB buffer
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
-                        uint4 w;
-                        w.x = pack_half2(v[8 * q], v[8 * q + 1]);
-                        w.y = pack_half2(v[8 * q + 2], v[8 * q + 3]);
-                        w.z = pack_half2(v[8 * q + 4], v[8 * q + 5]);
-                        w.w = pack_half2(v[8 * q + 6], v[8 * q + 7]);
+                        uint4 w, l;
+                        split_half2(v[8 * q], v[8 * q + 1], w.x, l.x);
+                        split_half2(v[8 * q + 2], v[8 * q + 3], w.y, l.y);
+                        split_half2(v[8 * q + 4], v[8 * q + 5], w.z, l.z);
+                        split_half2(v[8 * q + 6], v[8 * q + 7], w.w, l.w);
                         *reinterpret_cast<uint4*>(srow + ((q ^ ((lane >> 1) & 3)) << 4)) = w;
+                        if (p.norm_lo) *reinterpret_cast<uint4*>(srow + 2048 + ((q ^ ((lane >> 1) & 3)) << 4)) = l;
                     }
                 } else {
 #pragma unroll
@@ -366,6 +374,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 __syncwarp();
                 if (lane == 0) {
                     tma_store_2d(&tmap_n, stage_addr, nc, m_blk * kGemmBM + quarter * 32);
+                    if (NORM_F16 && p.norm_lo) tma_store_2d(&tmap_nl, stage_addr + 2048, nc, m_blk * kGemmBM + quarter * 32);
                     bulk_commit();
                 }
                 g_cur = g_next;

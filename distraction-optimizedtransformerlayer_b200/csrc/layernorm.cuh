@@ -41,12 +41,15 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 // EPL = elements per lane (D <= 32 * EPL). VEC4: D % 128 == 0 and every row
 // 16-byte aligned, so each lane moves float4 chunks at (i * 32 + lane) * 4.
+// lo_plane (fp16 output only): 0, or the element offset from `normed` of a
+// second plane that receives fp16(v - fp16(v)), the low half of the fp16 pair
+// the three-product GEMM mode reads.
 template <int EPL, bool VEC4, typename NormT>
 __global__ void __launch_bounds__(kLnWarpsPerBlock * 32)
     ln_rows_kernel(const float* __restrict__ x, const float* __restrict__ sub,
                    const float* __restrict__ w, const float* __restrict__ b,
                    float* __restrict__ x_new, NormT* __restrict__ normed,
-                   const uint8_t* __restrict__ row_valid, int64_t rows, int D, float eps) {
+                   const uint8_t* __restrict__ row_valid, int64_t rows, int D, float eps, int64_t lo_plane) {
     pdl_wait();
     pdl_launch_dependents();
     const int lane = threadIdx.x & 31;
@@ -132,10 +135,12 @@ __global__ void __launch_bounds__(kLnWarpsPerBlock * 32)
                     *reinterpret_cast<float4*>(reinterpret_cast<float*>(normed) + base + c) =
                         make_float4(o0, o1, o2, o3);
                 } else {
-                    uint2 h;
-                    h.x = pack_half2(o0, o1);
-                    h.y = pack_half2(o2, o3);
+                    uint2 h, l;
+                    split_half2(o0, o1, h.x, l.x);
+                    split_half2(o2, o3, h.y, l.y);
                     *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(normed) + base + c) = h;
+                    if (lo_plane != 0)
+                        *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(normed) + lo_plane + base + c) = l;
                 }
             }
         }
@@ -146,6 +151,10 @@ __global__ void __launch_bounds__(kLnWarpsPerBlock * 32)
             if (c < D) {
                 const float o = keep ? (v[i] - mean) * rstd * w[c] + b[c] : 0.0f;
                 store_val<NormT>(normed + base + c, o);
+                if constexpr (sizeof(NormT) == 2) {
+                    if (lo_plane != 0)
+                        store_val<NormT>(normed + lo_plane + base + c, o - __half2float(__float2half_rn(o)));
+                }
             }
         }
     }

@@ -30,7 +30,7 @@ import torch
 
 _lib: Optional[ctypes.CDLL] = None
 
-F32, F16 = 0, 1
+F32, F16, F16X2 = 0, 1, 2
 RESID_NONE, RESID_ADD, RESID_ADD_MASKSUB, RESID_ADD_MASKALL, MASK_ROWS = 0, 1, 2, 3, 4
 MASK_NONE, MASK_KEY, MASK_FULL = 0, 1, 2
 
@@ -47,11 +47,11 @@ _SIGNATURES = {
     "dotl_cast_f16_f32": ([_vp, _vp, _i64, _vp], _i32),
     "dotl_layernorm": ([_vp, _vp, _vp, _vp, _vp, _vp, _i32, _vp, _i64, _i64, _f32, _vp], _i32),
     "dotl_linear": ([_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i32, _vp, _i64, _vp, _i32,
-                     _vp, _i32, _i64, _i32, _vp], _i32),
+                     _vp, _i32, _i64, _i32, _i32, _vp], _i32),
     "dotl_linear_ln": ([_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _i32, _vp, _i64,
-                        _vp, _vp, _f32, _vp, _i32, _i64, _vp, _i32, _vp], _i32),
+                        _vp, _vp, _f32, _vp, _i32, _i64, _vp, _i32, _i32, _vp], _i32),
     "dotl_attention": ([_vp, _vp, _vp, _i32, _i32, _i32, _i32, _P64, _P64, _P64, _vp, _i32, _P64,
-                        _i32, _f32, _vp, _i32, _vp], _i32),
+                        _i32, _f32, _vp, _i32, _i32, _vp], _i32),
     "dotl_ffn": ([_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _i64, _vp, _i32,
                   _vp, _i64, _vp, _vp, _f32, _vp, _i32, _i64, _vp, _vp], _i32),
     "dotl_peer_alloc": ([_i64, ctypes.POINTER(_vp)], _i32),
@@ -67,6 +67,7 @@ _SIGNATURES = {
 }
 
 IPC_HANDLE_BYTES = 64
+ABI_VERSION = 2
 
 
 def load(path: str) -> ctypes.CDLL:
@@ -79,8 +80,8 @@ def load(path: str) -> ctypes.CDLL:
         fn = getattr(lib, name)
         fn.argtypes = argtypes
         fn.restype = restype
-    if lib.dotl_abi_version() != 1:
-        raise RuntimeError(f"libdotl ABI version {lib.dotl_abi_version()} is not 1")
+    if lib.dotl_abi_version() != ABI_VERSION:
+        raise RuntimeError(f"libdotl ABI version {lib.dotl_abi_version()} is not {ABI_VERSION}")
     _lib = lib
     return lib
 
@@ -179,26 +180,42 @@ def to_f32(x: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def _pair_planes(t: torch.Tensor) -> Tuple[int, int]:
+    """(rows, ld) of one plane of an fp16 pair: a contiguous fp16 tensor
+    [2, ..., cols] whose lo plane starts rows * cols elements after its hi
+    plane (the C ABI's DOTL_F16X2 layout)."""
+    if t.dim() < 3 or t.shape[0] != 2 or t.dtype != torch.float16 or not t.is_contiguous():
+        raise RuntimeError("an fp16 pair is a contiguous fp16 tensor [2, ..., cols] (hi plane, lo plane)")
+    cols = t.shape[-1]
+    return (t[0].numel() // cols if cols else 0), cols
+
+
 def layernorm_rows(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float,
                    sub: Optional[torch.Tensor] = None, out_half: bool = False,
                    row_valid: Optional[torch.Tensor] = None,
                    x_new: Optional[torch.Tensor] = None,
-                   out: Optional[torch.Tensor] = None):
+                   out: Optional[torch.Tensor] = None, out_pair: bool = False):
     """(x + sub, LN(x + sub)) or LN(x) over the last dim of an fp32 tensor.
 
     row_valid: optional bool/uint8 tensor with one entry per row; rows with 0
-    get a zero LN output (the final masked_fill).
+    get a zero LN output (the final masked_fill). out_pair: the output is an
+    fp16 pair [2, *x.shape] (hi, lo) for the three-product GEMM mode.
     """
     D = x.shape[-1]
     rows = x.numel() // D if D else 0
     if out is None:
-        out = torch.empty(x.shape, dtype=torch.float16 if out_half else torch.float32, device=x.device)
+        if out_pair:
+            out = torch.empty((2, *x.shape), dtype=torch.float16, device=x.device)
+        else:
+            out = torch.empty(x.shape, dtype=torch.float16 if out_half else torch.float32, device=x.device)
+    if out_pair and (out.shape[0] != 2 or not out.is_contiguous()):
+        raise RuntimeError("layernorm_rows: a pair output must be a contiguous [2, *x.shape] fp16 tensor")
     if sub is not None and x_new is None:
         x_new = torch.empty_like(x)
+    dtype = F16X2 if out_pair else (F16 if out.dtype == torch.float16 else F32)
     rc = lib().dotl_layernorm(
         x.data_ptr(), _ptr(sub), weight.data_ptr(), bias.data_ptr(), _ptr(x_new), out.data_ptr(),
-        F16 if out.dtype == torch.float16 else F32, _ptr(row_valid), rows, D, float(eps),
-        _stream(x.device))
+        dtype, _ptr(row_valid), rows, D, float(eps), _stream(x.device))
     _check(rc)
     return (x_new, out) if sub is not None else out
 
@@ -206,19 +223,38 @@ def layernorm_rows(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, ep
 def linear_fp16(a16: torch.Tensor, w16: torch.Tensor, bias: torch.Tensor, act: int = 0,
                 resid: Optional[torch.Tensor] = None, row_valid: Optional[torch.Tensor] = None,
                 resid_mode: int = RESID_NONE, out_half: bool = False,
-                out: Optional[torch.Tensor] = None, tile_n: int = 0) -> torch.Tensor:
-    """epilogue(a16 @ w16^T + bias) on the tcgen05 GEMM, a16 [..., K] fp16."""
+                out: Optional[torch.Tensor] = None, tile_n: int = 0, pair_operands: bool = False,
+                out_pair: bool = False) -> torch.Tensor:
+    """epilogue(a16 @ w16^T + bias) on the tcgen05 GEMM, a16 [..., K] fp16.
+
+    pair_operands: a16 is an fp16 pair [2, ..., K] and w16 one [2, N, K] (the
+    three-product mode). out_pair: fp16 pair output [2, ..., N]."""
     K = a16.shape[-1]
-    M = a16.numel() // K
-    N = w16.shape[0]
+    if pair_operands:
+        M, lda = _pair_planes(a16)
+        _pair_planes(w16)
+        lead = a16.shape[1:-1]
+        N, ldw = w16.shape[1], w16.stride(-2)
+    else:
+        M, lda = a16.numel() // K, (a16.stride(-2) if a16.dim() >= 2 else K)
+        lead = a16.shape[:-1]
+        N, ldw = w16.shape[0], w16.stride(0)
     if out is None:
-        out = torch.empty((*a16.shape[:-1], N), dtype=torch.float16 if out_half else torch.float32,
-                          device=a16.device)
+        if out_pair:
+            out = torch.empty((2, *lead, N), dtype=torch.float16, device=a16.device)
+        else:
+            out = torch.empty((*lead, N), dtype=torch.float16 if out_half else torch.float32, device=a16.device)
+    if out_pair:
+        _, ldo = _pair_planes(out)
+        odt = F16X2
+    else:
+        ldo = out.stride(-2) if out.dim() >= 2 else N
+        odt = F16 if out.dtype == torch.float16 else F32
     rc = lib().dotl_linear(
-        a16.data_ptr(), M, K, a16.stride(-2) if a16.dim() >= 2 else K, w16.data_ptr(), N, w16.stride(0),
+        a16.data_ptr(), M, K, lda, w16.data_ptr(), N, ldw,
         bias.data_ptr(), act, _ptr(resid), resid.stride(-2) if resid is not None and resid.dim() >= 2 else N,
-        _ptr(row_valid), resid_mode, out.data_ptr(), F16 if out.dtype == torch.float16 else F32,
-        out.stride(-2) if out.dim() >= 2 else N, tile_n, _stream(a16.device))
+        _ptr(row_valid), resid_mode, out.data_ptr(), odt, ldo, tile_n, F16X2 if pair_operands else F16,
+        _stream(a16.device))
     _check(rc)
     return out
 
@@ -289,26 +325,43 @@ def linear_ln(a16: torch.Tensor, w16: torch.Tensor, bias: torch.Tensor, ln_w: to
               row_valid: Optional[torch.Tensor] = None, resid_mode: int = RESID_NONE,
               store_x: bool = True, normed_half: bool = True,
               normed_row_valid: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
-              normed: Optional[torch.Tensor] = None, tile_n: int = 0):
+              normed: Optional[torch.Tensor] = None, tile_n: int = 0, pair_operands: bool = False,
+              normed_pair: bool = False):
     """(x_new, normed): x_new = resid epilogue(a16 @ w16^T + bias) in fp32 (None
     when store_x is False) and normed = LayerNorm(x_new) * ln_w + ln_b, from one
-    kernel whose CTA cluster shares each row's statistics."""
+    kernel whose CTA cluster shares each row's statistics. pair_operands /
+    normed_pair: fp16 pairs as linear_fp16 takes and gives them."""
     K = a16.shape[-1]
-    M = a16.numel() // K
-    N = w16.shape[0]
-    lead = a16.shape[:-1]
+    if pair_operands:
+        M, lda = _pair_planes(a16)
+        _pair_planes(w16)
+        lead = a16.shape[1:-1]
+        N, ldw = w16.shape[1], w16.stride(-2)
+    else:
+        M, lda = a16.numel() // K, (a16.stride(-2) if a16.dim() >= 2 else K)
+        lead = a16.shape[:-1]
+        N, ldw = w16.shape[0], w16.stride(0)
     if store_x and out is None:
         out = torch.empty((*lead, N), dtype=torch.float32, device=a16.device)
     if normed is None:
-        normed = torch.empty((*lead, N), dtype=torch.float16 if normed_half else torch.float32,
-                             device=a16.device)
+        if normed_pair:
+            normed = torch.empty((2, *lead, N), dtype=torch.float16, device=a16.device)
+        else:
+            normed = torch.empty((*lead, N), dtype=torch.float16 if normed_half else torch.float32,
+                                 device=a16.device)
+    if normed_pair:
+        _, ldn = _pair_planes(normed)
+        ndt = F16X2
+    else:
+        ldn = normed.stride(-2) if normed.dim() >= 2 else N
+        ndt = F16 if normed.dtype == torch.float16 else F32
     rc = lib().dotl_linear_ln(
-        a16.data_ptr(), M, K, a16.stride(-2) if a16.dim() >= 2 else K, w16.data_ptr(), N, w16.stride(0),
+        a16.data_ptr(), M, K, lda, w16.data_ptr(), N, ldw,
         bias.data_ptr(), _ptr(resid), resid.stride(-2) if resid is not None and resid.dim() >= 2 else N,
         _ptr(row_valid), resid_mode, out.data_ptr() if store_x else None,
         out.stride(-2) if store_x and out.dim() >= 2 else N, ln_w.data_ptr(), ln_b.data_ptr(), float(eps),
-        normed.data_ptr(), F16 if normed.dtype == torch.float16 else F32,
-        normed.stride(-2) if normed.dim() >= 2 else N, _ptr(normed_row_valid), tile_n, _stream(a16.device))
+        normed.data_ptr(), ndt, ldn, _ptr(normed_row_valid), tile_n, F16X2 if pair_operands else F16,
+        _stream(a16.device))
     _check(rc)
     return (out if store_x else None), normed
 
@@ -316,16 +369,19 @@ def linear_ln(a16: torch.Tensor, w16: torch.Tensor, bias: torch.Tensor, ln_w: to
 def attention_packed(q16: torch.Tensor, k16: torch.Tensor, v16: torch.Tensor, causal: bool,
                      scale: float, key_mask: Optional[torch.Tensor] = None,
                      full_mask: Optional[torch.Tensor] = None, out_layout: int = 1,
-                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                     out: Optional[torch.Tensor] = None, out_pair: bool = False) -> torch.Tensor:
     """Flash attention over fp16 [B,H,S,hd] views (head_dim stride 1).
 
     key_mask: bool [B,S] (True = may attend), any strides.
     full_mask: bool tensor already expanded to [B,H,S,S] (any strides).
+    out_pair: the output is an fp16 pair [2, *shape] (hi, lo planes).
     """
     B, H, S, hd = q16.shape
+    shape = (B, S, H * hd) if out_layout == 1 else (B, H, S, hd)
     if out is None:
-        shape = (B, S, H * hd) if out_layout == 1 else (B, H, S, hd)
-        out = torch.empty(shape, dtype=torch.float16, device=q16.device)
+        out = torch.empty(((2,) if out_pair else ()) + shape, dtype=torch.float16, device=q16.device)
+    if out_pair and (tuple(out.shape) != (2, *shape) or not out.is_contiguous()):
+        raise RuntimeError("attention_packed: a pair output must be a contiguous [2, *shape] fp16 tensor")
     if key_mask is not None:
         kind, mptr, ms = MASK_KEY, key_mask.data_ptr(), (key_mask.stride(0), 0, 0, key_mask.stride(1))
     elif full_mask is not None:
@@ -336,7 +392,7 @@ def attention_packed(q16: torch.Tensor, k16: torch.Tensor, v16: torch.Tensor, ca
         q16.data_ptr(), k16.data_ptr(), v16.data_ptr(), B, H, S, hd,
         _i64arr(q16.stride()[:3]), _i64arr(k16.stride()[:3]), _i64arr(v16.stride()[:3]),
         mptr, kind, _i64arr(ms), 1 if causal else 0, float(scale), out.data_ptr(), out_layout,
-        _stream(q16.device))
+        F16X2 if out_pair else F16, _stream(q16.device))
     _check(rc)
     return out
 

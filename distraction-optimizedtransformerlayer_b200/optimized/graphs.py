@@ -93,7 +93,7 @@ class _GraphRunner:
 def _graph_key(x: torch.Tensor, use_mask: bool) -> Tuple:
     """What makes two calls interchangeable to one captured graph."""
     return (tuple(x.shape), x.dtype, x.device.index, use_mask, config.ATTENTION_IMPL,
-            config.ATTENTION_PRECISION)
+            config.ATTENTION_PRECISION, config.GEMM_PRECISION)
 
 
 def _graph_eligible(x: torch.Tensor, entries: int) -> bool:
@@ -123,7 +123,8 @@ def _weight_caches(model) -> Tuple:
     out = []
     for layer in model.layers:
         attn = layer.attention
-        out += [attn._qkv_weight, attn._qkv_bias, attn.out_proj._w16, layer.ffn_in._w16, layer.ffn_out._w16]
+        out += [attn._qkv_weight, attn._qkv_bias, attn.out_proj._w16, layer.ffn_in._w16, layer.ffn_out._w16,
+                attn._qkv_pair, attn.out_proj._wpair, layer.ffn_in._wpair, layer.ffn_out._wpair]
         for mod in (layer.norm1, layer.norm2, attn.out_proj, layer.ffn_in, layer.ffn_out):
             out += [entry[1] for entry in mod.__dict__.get("_f32_cache", {}).values()]
     out += [entry[1] for entry in model.final_norm.__dict__.get("_f32_cache", {}).values()]

@@ -45,11 +45,12 @@ def _f32_param(module, name: str) -> torch.Tensor:
 
 
 def _layernorm(x: torch.Tensor, norm, out_half: bool = False,
-               row_valid: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """LayerNorm(x) * w + b over the last dim of fp32 x; padded rows -> 0 if row_valid."""
+               row_valid: Optional[torch.Tensor] = None, out_pair: bool = False) -> torch.Tensor:
+    """LayerNorm(x) * w + b over the last dim of fp32 x; padded rows -> 0 if
+    row_valid; out_pair: an fp16 pair [2, *x.shape] for three-product GEMMs."""
     k = _custom_kernels()
     return k.layernorm_rows(x, _f32_param(norm, "weight"), _f32_param(norm, "bias"), norm.eps,
-                            out_half=out_half, row_valid=row_valid)
+                            out_half=out_half, row_valid=row_valid, out_pair=out_pair)
 
 
 def _add_layernorm(x: torch.Tensor, sub: torch.Tensor, norm,
@@ -62,11 +63,13 @@ def _add_layernorm(x: torch.Tensor, sub: torch.Tensor, norm,
 
 def _linear(a16: torch.Tensor, w16: torch.Tensor, bias32: torch.Tensor, act: int = 0,
             resid: Optional[torch.Tensor] = None, row_valid: Optional[torch.Tensor] = None,
-            resid_mode: int = 0, out_half: bool = False) -> torch.Tensor:
-    """epilogue(a16 @ w16^T + bias) on the tcgen05 GEMM."""
+            resid_mode: int = 0, out_half: bool = False, pairs: bool = False,
+            out_pair: bool = False) -> torch.Tensor:
+    """epilogue(a16 @ w16^T + bias) on the tcgen05 GEMM (pairs: a16 and w16
+    are fp16 pairs, the three-product mode; out_pair: an fp16 pair out)."""
     k = _custom_kernels()
     return k.linear_fp16(a16, w16, bias32, act=act, resid=resid, row_valid=row_valid,
-                         resid_mode=resid_mode, out_half=out_half)
+                         resid_mode=resid_mode, out_half=out_half, pair_operands=pairs, out_pair=out_pair)
 
 
 def _linear_ln_ok(rows: int, n: int) -> bool:
@@ -98,14 +101,16 @@ def _ffn(n2: torch.Tensor, ffn_in, ffn_out, norm, resid: torch.Tensor,
 def _linear_ln(a16: torch.Tensor, w16: torch.Tensor, bias32: torch.Tensor, norm,
                resid: Optional[torch.Tensor] = None, row_valid: Optional[torch.Tensor] = None,
                resid_mode: int = 0, store_x: bool = True, normed_half: bool = True,
-               normed_row_valid: Optional[torch.Tensor] = None):
+               normed_row_valid: Optional[torch.Tensor] = None, pairs: bool = False,
+               normed_pair: bool = False):
     """(x_new, norm(x_new)) from one kernel: x_new = epilogue(a16 @ w16^T + bias)
     as _linear computes it (fp32; None when store_x is False), then the
     LayerNorm over its rows (fp16 or fp32, padded rows 0 with normed_row_valid)."""
     k = _custom_kernels()
     return k.linear_ln(a16, w16, bias32, _f32_param(norm, "weight"), _f32_param(norm, "bias"), norm.eps,
                        resid=resid, row_valid=row_valid, resid_mode=resid_mode, store_x=store_x,
-                       normed_half=normed_half, normed_row_valid=normed_row_valid)
+                       normed_half=normed_half, normed_row_valid=normed_row_valid, pair_operands=pairs,
+                       normed_pair=normed_pair)
 
 
 def _linear_bias(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,
@@ -121,7 +126,7 @@ def _linear_gelu(x: torch.Tensor, lin) -> torch.Tensor:
 
 def _attention_dispatch(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                         key_mask: Optional[torch.Tensor], is_causal: bool, scale: float,
-                        out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                        out: Optional[torch.Tensor] = None, out_pair: bool = False) -> torch.Tensor:
     """Attention on the tcgen05 kernel; q/k/v fp16 [B,H,S,hd] views; returns [B,S,H*hd] fp16.
 
     key_mask: bool [B,S], True = may attend (the [B,1,1,S] mask upstream).
@@ -129,4 +134,4 @@ def _attention_dispatch(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     config.validate()
     kernels = _custom_kernels()
     return kernels.attention_packed(q, k, v, is_causal, scale, key_mask=key_mask,
-                                    out_layout=config._OUT_LAYOUT_BSHD, out=out)
+                                    out_layout=config._OUT_LAYOUT_BSHD, out=out, out_pair=out_pair)

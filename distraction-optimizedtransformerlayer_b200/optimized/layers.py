@@ -34,6 +34,15 @@ from .util import _version_or_none
 RESID_ADD, RESID_ADD_MASKSUB, RESID_ADD_MASKALL = 1, 2, 3
 
 
+def fp16_pair(w: torch.Tensor) -> torch.Tensor:
+    """[2, *w.shape] fp16: hi = fp16(w) and lo = fp16(w - hi), both round to
+    nearest even (the DOTL_F16X2 layout, planes back to back)."""
+    w = w.float()
+    hi = w.to(torch.float16)
+    lo = (w - hi.float()).to(torch.float16)
+    return torch.stack([hi, lo]).contiguous()
+
+
 class MyLinear(nn.Module):
     """A linear layer whose `weight` [out, in] and `bias` [out] are laid out as
     nn.Linear's, so a baseline state_dict loads with strict=True; the GEMM runs
@@ -45,6 +54,8 @@ class MyLinear(nn.Module):
         self.bias = nn.Parameter(torch.empty(out_features)) if bias else None
         self._w16_key = None
         self._w16: Optional[torch.Tensor] = None
+        self._wpair_key = None
+        self._wpair: Optional[torch.Tensor] = None
 
     def half_weight(self) -> torch.Tensor:
         """The weight narrowed to fp16 once per version (the GEMM's B operand)."""
@@ -54,6 +65,16 @@ class MyLinear(nn.Module):
             self._w16 = w.detach().to(torch.float16).contiguous()
             self._w16_key = key
         return self._w16
+
+    def pair_weight(self) -> torch.Tensor:
+        """The weight as an fp16 pair [2, out, in] (hi = fp16(w), lo = fp16(w - hi)),
+        the B operand of the three-product GEMM mode, once per version."""
+        w = self.weight
+        key = (w.device, w.dtype, w.data_ptr(), _version_or_none(w))
+        if self._wpair_key != key:
+            self._wpair = fp16_pair(w.detach())
+            self._wpair_key = key
+        return self._wpair
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if self.bias is None:
@@ -93,6 +114,8 @@ class MySelfAttention(nn.Module):
         self._qkv_key: Optional[Tuple] = None
         self._qkv_weight: Optional[torch.Tensor] = None
         self._qkv_bias: Optional[torch.Tensor] = None
+        self._qkv_pair_key: Optional[Tuple] = None
+        self._qkv_pair: Optional[torch.Tensor] = None
 
     def _get_qkv_weight(self) -> Tuple[torch.Tensor, torch.Tensor]:
         """Q, K and V as one fp16 [3d, d] weight and one fp32 [3d] bias
@@ -110,41 +133,56 @@ class MySelfAttention(nn.Module):
             self._qkv_key = key
         return self._qkv_weight, self._qkv_bias
 
+    def _get_qkv_pair(self) -> Tuple[torch.Tensor, torch.Tensor]:
+        """The fused QKV weight as an fp16 pair [2, 3d, d] and the fp32 bias."""
+        _w, bias = self._get_qkv_weight()
+        if self._qkv_pair_key != self._qkv_key:
+            w_q, w_k, w_v = self.q_proj.weight, self.k_proj.weight, self.v_proj.weight
+            self._qkv_pair = fp16_pair(torch.cat([w_q, w_k, w_v], dim=0).detach())
+            self._qkv_pair_key = self._qkv_key
+        return self._qkv_pair, bias
+
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None,
                 causal: bool = False, mask_is_trivial: bool = False,
-                residual: Optional[torch.Tensor] = None, norm: Optional["MyLayerNorm"] = None):
+                residual: Optional[torch.Tensor] = None, norm: Optional["MyLayerNorm"] = None,
+                pairs: bool = False):
         """out_proj(attention(x)) with padded rows zeroed, plus `residual` if given.
 
-        x is the block's normalised input [B,S,d] (fp16 or fp32). With
+        x is the block's normalised input [B,S,d] (fp16 or fp32), or with
+        `pairs` an fp16 pair [2,B,S,d] for the three-product GEMM mode. With
         `residual`, the add x + attn happens in the out_proj epilogue and the
         fp32 sum is returned; without it, the attention output alone. With
-        `norm` as well, returns (sum, norm(sum) in fp16) from one GEMM +
-        LayerNorm kernel.
+        `norm` as well, returns (sum, norm(sum)) from one GEMM + LayerNorm
+        kernel, norm(sum) fp16 (an fp16 pair with `pairs`).
         """
-        batch, seq_len, d_model = x.shape
-        x16 = x if x.dtype == torch.float16 else x.to(torch.float16)
-        x16 = x16.contiguous()
-        qkv_w, qkv_b = self._get_qkv_weight()
-        qkv = _linear(x16, qkv_w, qkv_b, out_half=True)           # [B, S, 3d] fp16
+        if pairs:
+            batch, seq_len, d_model = x.shape[1:]
+            qkv_w, qkv_b = self._get_qkv_pair()
+            wo = self.out_proj.pair_weight()
+            a = x
+        else:
+            batch, seq_len, d_model = x.shape
+            qkv_w, qkv_b = self._get_qkv_weight()
+            wo = self.out_proj.half_weight()
+            a = (x if x.dtype == torch.float16 else x.to(torch.float16)).contiguous()
+        qkv = _linear(a, qkv_w, qkv_b, out_half=True, pairs=pairs)   # [B, S, 3d] fp16
         q, k, v = (qkv.view(batch, seq_len, 3, self.num_heads, self.head_dim)
                    .permute(2, 0, 3, 1, 4).unbind(0))              # [B, H, S, hd] views
         use_mask = valid_token_mask is not None and not mask_is_trivial
         key_mask = valid_token_mask if use_mask else None
-        context = _attention_dispatch(q, k, v, key_mask, causal, self.scale)   # [B, S, d] fp16
+        # [B, S, d] fp16, or its fp16 pair [2, B, S, d]
+        context = _attention_dispatch(q, k, v, key_mask, causal, self.scale, out_pair=pairs)
         row_valid = valid_token_mask.reshape(-1) if use_mask else None
+        bo = _f32_param(self.out_proj, "bias")
+        mode = RESID_ADD_MASKSUB if use_mask else RESID_ADD
         if residual is None:
             # Plain attention output, padded rows zeroed: residual is zero.
             zeros = torch.zeros(batch, seq_len, d_model, device=x.device, dtype=torch.float32)
-            return _linear(context, self.out_proj.half_weight(), _f32_param(self.out_proj, "bias"),
-                           resid=zeros, row_valid=row_valid,
-                           resid_mode=RESID_ADD_MASKSUB if use_mask else RESID_ADD)
+            return _linear(context, wo, bo, resid=zeros, row_valid=row_valid, resid_mode=mode, pairs=pairs)
         if norm is not None:
-            return _linear_ln(context, self.out_proj.half_weight(), _f32_param(self.out_proj, "bias"), norm,
-                              resid=residual, row_valid=row_valid,
-                              resid_mode=RESID_ADD_MASKSUB if use_mask else RESID_ADD)
-        return _linear(context, self.out_proj.half_weight(), _f32_param(self.out_proj, "bias"),
-                       resid=residual, row_valid=row_valid,
-                       resid_mode=RESID_ADD_MASKSUB if use_mask else RESID_ADD)
+            return _linear_ln(context, wo, bo, norm, resid=residual, row_valid=row_valid, resid_mode=mode,
+                              pairs=pairs, normed_pair=pairs)
+        return _linear(context, wo, bo, resid=residual, row_valid=row_valid, resid_mode=mode, pairs=pairs)
 
 
 class MyTransformerBlock(nn.Module):
@@ -162,47 +200,52 @@ class MyTransformerBlock(nn.Module):
 
     def forward(self, x: torch.Tensor, normed: torch.Tensor, next_norm: "MyLayerNorm",
                 valid_token_mask: Optional[torch.Tensor] = None, mask_is_trivial: bool = False,
-                next_norm_is_output: bool = False) -> Tuple[torch.Tensor, torch.Tensor]:
+                next_norm_is_output: bool = False, pairs: bool = False) -> Tuple[torch.Tensor, torch.Tensor]:
         """Returns (residual stream, next_norm applied to it) (layers.py:206-262 upstream).
 
         `normed` is norm1(x), produced by whoever produced x. `next_norm` is
         the next block's norm1 or the model's final_norm; when it is the final
         norm (next_norm_is_output) its output is fp32 with padded rows zeroed
-        (the model's final masked_fill), otherwise fp16 for the next QKV GEMM.
-        After the last block the residual stream is only returned when the
-        unfused path ran (None otherwise: nothing reads it).
+        (the model's final masked_fill), otherwise fp16 for the next QKV GEMM
+        (an fp16 pair [2, B, S, d] with `pairs`, the three-product GEMM mode,
+        in which `normed` is one too). After the last block the residual
+        stream is only returned when the unfused path ran (None otherwise:
+        nothing reads it).
         """
         use_mask = valid_token_mask is not None and not mask_is_trivial
         row_valid = valid_token_mask.reshape(-1) if use_mask else None
+        rows, d = x.numel() // x.shape[-1], x.shape[-1]
         # out_proj + residual + norm2, and ffn_out + residual + next norm, each
         # as one GEMM whose epilogue also normalises (a thread-block cluster
         # shares each row's statistics) on the shapes where that is faster.
-        fused = _linear_ln_ok(x.numel() // x.shape[-1], x.shape[-1])
+        fused = _linear_ln_ok(rows, d)
         if fused:
             x1, n2 = self.attention(normed, valid_token_mask, self.causal, mask_is_trivial, residual=x,
-                                    norm=self.norm2)
+                                    norm=self.norm2, pairs=pairs)
         else:
-            x1 = self.attention(normed, valid_token_mask, self.causal, mask_is_trivial, residual=x)
-            n2 = _layernorm(x1, self.norm2, out_half=True)
+            x1 = self.attention(normed, valid_token_mask, self.causal, mask_is_trivial, residual=x, pairs=pairs)
+            n2 = _layernorm(x1, self.norm2, out_half=True, out_pair=pairs)
         # x1 + ffn_out(h); padded rows of the whole sum zeroed (the block's
         # trailing masked_fill), before the next LayerNorm reads it.
         mode = RESID_ADD_MASKALL if use_mask else RESID_ADD
-        if _ffn_ok(x.numel() // x.shape[-1], x.shape[-1], self.ffn_in.weight.shape[0]):
+        last = next_norm_is_output
+        if not pairs and _ffn_ok(rows, d, self.ffn_in.weight.shape[0]):
             # ffn_in + GELU + ffn_out + residual + next norm in one kernel
             x2, out = _ffn(n2, self.ffn_in, self.ffn_out, next_norm, x1, row_valid, mode,
-                           store_x=not next_norm_is_output, normed_half=not next_norm_is_output,
-                           normed_row_valid=row_valid if next_norm_is_output else None)
+                           store_x=not last, normed_half=not last,
+                           normed_row_valid=row_valid if last else None)
             return (x2.view(x.shape) if x2 is not None else None), out
-        h = _linear(n2, self.ffn_in.half_weight(), _f32_param(self.ffn_in, "bias"), act=1,
-                    out_half=True)
+        w1 = self.ffn_in.pair_weight() if pairs else self.ffn_in.half_weight()
+        w2 = self.ffn_out.pair_weight() if pairs else self.ffn_out.half_weight()
+        b2 = _f32_param(self.ffn_out, "bias")
+        h = _linear(n2, w1, _f32_param(self.ffn_in, "bias"), act=1, out_half=True, pairs=pairs, out_pair=pairs)
         if fused:
-            # the model's output: x2 itself is not needed, only its final norm
-            return _linear_ln(h, self.ffn_out.half_weight(), _f32_param(self.ffn_out, "bias"), next_norm,
-                              resid=x1, row_valid=row_valid, resid_mode=mode,
-                              store_x=not next_norm_is_output, normed_half=not next_norm_is_output,
-                              normed_row_valid=row_valid if next_norm_is_output else None)
-        x2 = _linear(h, self.ffn_out.half_weight(), _f32_param(self.ffn_out, "bias"), resid=x1,
-                     row_valid=row_valid, resid_mode=mode)
-        if next_norm_is_output:
+            # after the last block x2 itself is not needed, only its final norm
+            return _linear_ln(h, w2, b2, next_norm, resid=x1, row_valid=row_valid, resid_mode=mode,
+                              store_x=not last, normed_half=not last,
+                              normed_row_valid=row_valid if last else None, pairs=pairs,
+                              normed_pair=pairs and not last)
+        x2 = _linear(h, w2, b2, resid=x1, row_valid=row_valid, resid_mode=mode, pairs=pairs)
+        if last:
             return x2, _layernorm(x2, next_norm, out_half=False, row_valid=row_valid)
-        return x2, _layernorm(x2, next_norm, out_half=True)
+        return x2, _layernorm(x2, next_norm, out_half=True, out_pair=pairs)

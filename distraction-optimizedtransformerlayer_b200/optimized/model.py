@@ -65,11 +65,13 @@ class OptimizedTransformer(nn.Module):
         dtype = x.dtype
         x = x.float().contiguous()
         mask = valid_token_mask.contiguous() if use_mask else None
-        normed = _layernorm(x, self.layers[0].norm1, out_half=True)
+        # three-product GEMMs (fp16 pair operands) for stacks of layers
+        pairs = config.gemm_pairs(len(self.layers))
+        normed = _layernorm(x, self.layers[0].norm1, out_half=True, out_pair=pairs)
         last = len(self.layers) - 1
         for index, layer in enumerate(self.layers):
             next_norm = self.final_norm if index == last else self.layers[index + 1].norm1
-            x, normed = layer(x, normed, next_norm, mask, not use_mask, index == last)
+            x, normed = layer(x, normed, next_norm, mask, not use_mask, index == last, pairs=pairs)
         # The last block folded final_norm and the final masked_fill into its
         # trailing LayerNorm, so `normed` is already the model's output.
         return normed if dtype == torch.float32 else normed.to(dtype)
@@ -111,10 +113,12 @@ class OptimizedTransformer(nn.Module):
     def _bytes_per_row(self, x: torch.Tensor) -> int:
         """Device bytes one batch row of one forward holds at its peak: the
         fp32 input copy and output, and one block's intermediates (fp16 n1,
-        qkv and ctx; fp32 x1 and x2; fp16 n2 and the [S, F] hidden)."""
+        qkv and ctx; fp32 x1 and x2; fp16 n2 and the [S, F] hidden; n1, ctx,
+        n2 and the hidden twice over as fp16 pairs in the three-product mode)."""
         S, d = x.shape[1], x.shape[2]
         F = max(layer.ffn_in.weight.shape[0] for layer in self.layers)
-        per_token = 4 * d * 2 + 2 * d * (1 + 3 + 1 + 1) + 4 * d * 2 + 2 * F
+        k = 2 if config.gemm_pairs(len(self.layers)) else 1
+        per_token = 4 * d * 2 + 2 * d * 3 + k * 2 * d * 3 + 4 * d * 2 + k * 2 * F
         return S * per_token
 
     def _plan_rows(self, x: torch.Tensor) -> int:

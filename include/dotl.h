@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define DOTL_ABI_VERSION 1
+#define DOTL_ABI_VERSION 2
 
 /* status codes */
 #define DOTL_OK 0
@@ -38,6 +38,16 @@ extern "C" {
 /* element types */
 #define DOTL_F32 0
 #define DOTL_F16 1
+/*
+ * An fp16 pair: a [rows, cols] tensor v stored as two fp16 planes of
+ * [rows, ld] each, back to back: hi = fp16(v) (round to nearest even) in plane
+ * 0 and lo = fp16(v - hi) in plane 1, starting rows * ld elements after plane
+ * 0. hi + lo carries v to about 22 bits. GEMMs given DOTL_F16X2 operands run
+ * three passes into one fp32 accumulator, a_hi w_hi + a_lo w_hi + a_hi w_lo
+ * (the three-product mode: 3x the tensor work, for layer stacks whose fp16
+ * operand error would otherwise exceed the harness's bound).
+ */
+#define DOTL_F16X2 2
 
 /* dotl_linear residual modes */
 #define DOTL_RESID_NONE 0        /* out = act(a w^T + bias) */
@@ -80,8 +90,10 @@ int dotl_cast_f16_f32(const void* in_f16, float* out, int64_t n, void* stream);
  *   x_new  = x + sub                 written when sub and x_new are non-NULL
  *   normed = LN(x_new) * weight + bias, stored as fp32 or fp16 (normed_dtype)
  *   row_valid (optional, [rows] uint8): rows with 0 get normed = 0
- * All row pointers must be 16-byte aligned for the vectorised path; other
- * alignments take a scalar path. D <= 2048.
+ * normed_dtype DOTL_F32, DOTL_F16 or DOTL_F16X2 (normed then holds 2 * rows
+ * rows: the hi plane, then the lo plane). All row pointers must be 16-byte
+ * aligned for the vectorised path; other alignments take a scalar path.
+ * D <= 2048.
  */
 int dotl_layernorm(const float* x, const float* sub, const float* weight, const float* bias,
                    float* x_new, void* normed, int normed_dtype, const uint8_t* row_valid,
@@ -93,7 +105,10 @@ int dotl_layernorm(const float* x, const float* sub, const float* weight, const 
  * (linear_gelu.cuh:598-756; pybind fused_attention.cu:129-148).
  *   act: 0 none, 1 exact erf GELU (applied before any residual)
  *   resid_mode: DOTL_RESID_*; resid is fp32 [M, ldr]; row_valid [M] uint8
- *   out_dtype: DOTL_F32 or DOTL_F16, leading dimension ldo
+ *   out_dtype: DOTL_F32, DOTL_F16 or DOTL_F16X2 (fp16 pair, out holding 2 * M
+ *              rows of ldo), leading dimension ldo
+ *   operands: DOTL_F16 (a, w fp16), or DOTL_F16X2 (a is an fp16 pair of 2 * M
+ *             rows of lda and w one of 2 * N rows of ldw; the three-product mode)
  * Requirements: K % 8 == 0, lda % 8 == 0, ldw % 8 == 0, a/w 16-byte aligned
  * (TMA), N % 8 == 0. tile_n: 0 = auto, else 64, 128 or 256, or -128 for two
  * CTAs per 128-wide tile that split K and add their partial sums (auto picks it
@@ -103,7 +118,7 @@ int dotl_layernorm(const float* x, const float* sub, const float* weight, const 
 int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N,
                 int64_t ldw, const float* bias, int act, const float* resid, int64_t ldr,
                 const uint8_t* row_valid, int resid_mode, void* out, int out_dtype, int64_t ldo,
-                int tile_n, void* stream);
+                int tile_n, int operands, void* stream);
 
 /*
  * dotl_linear with a residual + LayerNorm epilogue, in one kernel. Replaces the
@@ -113,7 +128,8 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
  *   normed = LN(x_new) * ln_weight + ln_bias      over all N columns, eps as given
  *   normed_row_valid (optional, [M] uint8): rows with 0 get normed = 0
  * resid_mode: NONE, ADD, ADD_MASKSUB or ADD_MASKALL (as dotl_linear; row_valid
- * for the masked ones). normed_dtype DOTL_F32 or DOTL_F16, leading dimension ldn.
+ * for the masked ones). normed_dtype DOTL_F32, DOTL_F16 or DOTL_F16X2 (2 * M rows
+ * of ldn), leading dimension ldn; operands as dotl_linear.
  * The row is shared by a cluster of N / tile_n CTAs, so N must be 64, 128 or
  * 256 times a cluster size of at most 8 (tile_n 0 = auto). Other requirements
  * as dotl_linear; ln_weight and ln_bias 16-byte aligned.
@@ -123,7 +139,7 @@ int dotl_linear_ln(const void* a, int64_t M, int64_t K, int64_t lda, const void*
                    const uint8_t* row_valid, int resid_mode, float* out, int64_t ldo,
                    const float* ln_weight, const float* ln_bias, float eps, void* normed,
                    int normed_dtype, int64_t ldn, const uint8_t* normed_row_valid, int tile_n,
-                   void* stream);
+                   int operands, void* stream);
 
 /*
  * The layer's whole MLP in one kernel, the [M, F] hidden kept on chip.
@@ -151,7 +167,8 @@ int dotl_ffn(const void* a, int64_t M, int64_t D, int64_t lda, const void* w1, i
  *          (head_dim stride 1), 16-byte aligned, strides multiples of 8.
  *   mask_kind: DOTL_MASK_*; mask strides ms[4] in elements (b, h, query, key).
  *   causal: key j may be attended by query i only if j <= i (combinable).
- *   out: fp16, layout 0 = [B,H,S,head_dim], 1 = [B,S,H*head_dim].
+ *   out: fp16, layout 0 = [B,H,S,head_dim], 1 = [B,S,H*head_dim]; out_dtype
+ *        DOTL_F16, or DOTL_F16X2 (the lo plane follows, B*H*S*head_dim later).
  * Fully masked query rows are written as 0. head_dim 32, 64 or 128 run on the
  * tcgen05 kernel; other multiples of 8 up to 256 on a CUDA-core flash kernel
  * (the reference's scalar/wmma shapes, e.g. head_dim 8 and 256).
@@ -159,7 +176,7 @@ int dotl_ffn(const void* a, int64_t M, int64_t D, int64_t lda, const void* w1, i
 int dotl_attention(const void* q, const void* k, const void* v, int B, int H, int S, int head_dim,
                    const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
                    const uint8_t* mask, int mask_kind, const int64_t* mask_strides, int causal,
-                   float scale, void* out, int out_layout, void* stream);
+                   float scale, void* out, int out_layout, int out_dtype, void* stream);
 
 /*
  * Peer memory for the tensor-parallel layer (one process per GPU). These are

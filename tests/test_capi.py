@@ -43,7 +43,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_abi_version(lib):
-    assert lib.dotl_abi_version() == 1
+    assert lib.dotl_abi_version() == 2
 
 
 def _err(lib):
@@ -51,51 +51,58 @@ def _err(lib):
 
 
 def test_linear_rejects_unaligned_k(lib):
-    rc = lib.dotl_linear(16, 4, 7, 7, 16, 16, 7, 16, 0, None, 0, None, 0, 16, 0, 16, 0, None)
+    rc = lib.dotl_linear(16, 4, 7, 7, 16, 16, 7, 16, 0, None, 0, None, 0, 16, 0, 16, 0, 1, None)
     assert rc == 2 and "multiples of 8" in _err(lib)
 
 
 def test_linear_rejects_bad_modes(lib):
-    assert lib.dotl_linear(16, 4, 8, 8, 16, 16, 8, 16, 2, None, 0, None, 0, 16, 0, 16, 0, None) == 1
+    assert lib.dotl_linear(16, 4, 8, 8, 16, 16, 8, 16, 2, None, 0, None, 0, 16, 0, 16, 0, 1, None) == 1
     assert "act must be" in _err(lib)
-    assert lib.dotl_linear(16, 4, 8, 8, 16, 16, 8, 16, 0, None, 0, None, 9, 16, 0, 16, 0, None) == 1
+    assert lib.dotl_linear(16, 4, 8, 8, 16, 16, 8, 16, 0, None, 0, None, 9, 16, 0, 16, 0, 1, None) == 1
     assert "residual mode" in _err(lib)
-    assert lib.dotl_linear(16, 4, 8, 8, 16, 16, 8, 16, 0, None, 0, None, 0, 16, 5, 16, 0, None) == 1
+    assert lib.dotl_linear(16, 4, 8, 8, 16, 16, 8, 16, 0, None, 0, None, 0, 16, 5, 16, 0, 1, None) == 1
+    assert "out dtype" in _err(lib)
+    # operand and output codes: DOTL_F16 / DOTL_F16X2 only
+    assert lib.dotl_linear(16, 4, 8, 8, 16, 16, 8, 16, 0, None, 0, None, 0, 16, 0, 16, 0, 0, None) == 1
+    assert "operands" in _err(lib)
+    assert lib.dotl_linear(16, 4, 8, 8, 16, 16, 8, 16, 0, None, 0, None, 0, 16, 3, 16, 0, 1, None) == 1
     assert "out dtype" in _err(lib)
     # masked residual needs the row mask
-    assert lib.dotl_linear(16, 4, 8, 8, 16, 16, 8, 16, 0, 16, 16, None, 3, 16, 0, 16, 0, None) == 1
+    assert lib.dotl_linear(16, 4, 8, 8, 16, 16, 8, 16, 0, 16, 16, None, 3, 16, 0, 16, 0, 1, None) == 1
     assert "row_valid" in _err(lib)
 
 
 def test_linear_empty_m_is_ok(lib):
-    assert lib.dotl_linear(None, 0, 8, 8, None, 16, 8, None, 0, None, 0, None, 0, None, 0, 16, 0, None) == 0
+    assert lib.dotl_linear(None, 0, 8, 8, None, 16, 8, None, 0, None, 0, None, 0, None, 0, 16, 0, 1, None) == 0
 
 
 def test_attention_rejects_head_dim(lib):
     st = (ctypes.c_int64 * 3)(0, 0, 0)
     for hd in (4, 12, 264):
-        rc = lib.dotl_attention(16, 16, 16, 1, 1, 8, hd, st, st, st, None, 0, None, 0, 0.1, 16, 0, None)
+        rc = lib.dotl_attention(16, 16, 16, 1, 1, 8, hd, st, st, st, None, 0, None, 0, 0.1, 16, 0, 1, None)
         assert rc == 2 and "head_dim" in _err(lib)
 
 
 def test_attention_rejects_generic_grid_overflow(lib):
     # head_dim 8 takes the CUDA-core kernel, one grid row per (batch, head)
     st = (ctypes.c_int64 * 3)(0, 0, 0)
-    rc = lib.dotl_attention(16, 16, 16, 65536, 1, 8, 8, st, st, st, None, 0, None, 0, 0.1, 16, 0, None)
+    rc = lib.dotl_attention(16, 16, 16, 65536, 1, 8, 8, st, st, st, None, 0, None, 0, 0.1, 16, 0, 1, None)
     assert rc == 2 and "65535" in _err(lib)
 
 
 def test_attention_rejects_layout_and_mask(lib):
     st = (ctypes.c_int64 * 3)(0, 0, 0)
-    assert lib.dotl_attention(16, 16, 16, 1, 1, 8, 64, st, st, st, None, 0, None, 0, 0.1, 16, 2, None) == 1
+    assert lib.dotl_attention(16, 16, 16, 1, 1, 8, 64, st, st, st, None, 0, None, 0, 0.1, 16, 2, 1, None) == 1
     assert "out_layout" in _err(lib)
-    assert lib.dotl_attention(16, 16, 16, 1, 1, 8, 64, st, st, st, None, 1, None, 0, 0.1, 16, 0, None) == 1
+    assert lib.dotl_attention(16, 16, 16, 1, 1, 8, 64, st, st, st, None, 1, None, 0, 0.1, 16, 0, 1, None) == 1
     assert "needs mask" in _err(lib)
+    assert lib.dotl_attention(16, 16, 16, 1, 1, 8, 64, st, st, st, None, 0, None, 0, 0.1, 16, 0, 0, None) == 1
+    assert "out dtype" in _err(lib)
 
 
 def test_attention_rejects_unaligned_strides(lib):
     st = (ctypes.c_int64 * 3)(64 * 8, 64, 12)
-    rc = lib.dotl_attention(16, 16, 16, 1, 1, 8, 64, st, st, st, None, 0, None, 0, 0.1, 16, 0, None)
+    rc = lib.dotl_attention(16, 16, 16, 1, 1, 8, 64, st, st, st, None, 0, None, 0, 0.1, 16, 0, 1, None)
     assert rc == 2 and "multiples of 8" in _err(lib)
 
 

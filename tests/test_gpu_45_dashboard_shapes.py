@@ -2,12 +2,17 @@
 d_model; the shapes are listed with the reference's published results) through
 the whole multi-layer model, gpu.
 
-Every shape is checked (head_dim 32/64/128 on the tcgen05 attention, 8 and 256
-on the CUDA-core kernel) on a few batch rows (rows never interact) with the
-reference harness's pass rule against the reference's fp16 kernel arithmetic,
-and against the fp32 baseline no worse than that arithmetic is itself.
-The last shape (S = 100,000, two layers) is beyond what the CPU oracle can
-check in a test and is left to the benchmark.
+Every shape (head_dim 32/64/128 on the tcgen05 attention, 8 and 256 on the
+CUDA-core kernel) must pass the reference harness's rule against the fp32
+baseline layer stack: 2e-3 absolute or 2 % relative, zero failing elements,
+on a few batch rows (rows never interact). A stack of layers runs its GEMMs in
+the three-product mode (fp16 pair operands, optimized.config.GEMM_PRECISION
+"auto"); with fp16 operands alone the error of four layers passes the bound
+on a few elements, which the last test shows is the operands' own rounding.
+
+Shape 14 (S = 100,000, two layers) is beyond the CPU oracle (the reference's
+harness skips its baseline too): it runs for finiteness, throughput and
+bit-identical batch-row independence.
 """
 
 import pytest
@@ -65,20 +70,62 @@ def test_dashboard_shape(kernels, shape):
     idx = torch.tensor(rows)
     sub = O.TransformerConfig(len(rows), S, d, H, F, L, True)
     got = out[idx]
-    # (1) Parity: the harness rule against the reference's fp16 kernel
-    # arithmetic (fp16 operands where its kernels round them, exact otherwise).
-    ref16 = O.fp16_operand_forward(params, sub, x[idx], mask[idx])
-    r16 = O.compare_outputs(ref16, got, rtol=RTOL, atol=ATOL)
-    assert r16.passed, (shape, r16.failed_elements, r16.max_abs_error, r16.worst_index)
-    # (2) Against the fp32 baseline, a sanity bound. Over 4 layers fp16
-    # operands alone can miss the 2e-3 bound on a few elements (e.g. 1-4 of
-    # 49,152 on shapes 1-5 with these seeds). The rule here: at most twice the
-    # misses of the reference's own fp16 arithmetic plus 4 (counts this small
-    # are rounding noise: shape 7, d_model 32, has 4 against its 1 of 12,288),
-    # and the largest error at most 1.25x the larger of atol and its largest error.
     ref = O.baseline_forward(params, sub, x[idx], mask[idx])
     r32 = O.compare_outputs(ref, got, rtol=RTOL, atol=ATOL)
-    e32 = O.compare_outputs(ref, ref16, rtol=RTOL, atol=ATOL)
-    detail = (shape, r32.failed_elements, r32.max_abs_error, e32.failed_elements, e32.max_abs_error)
-    assert r32.failed_elements <= 2 * e32.failed_elements + 4, detail
-    assert r32.max_abs_error <= 1.25 * max(ATOL, e32.max_abs_error), detail
+    assert r32.passed, (shape, r32.failed_elements, r32.max_abs_error, r32.worst_index)
+
+
+def test_fp16_operands_alone_miss_the_bound_over_four_layers(kernels):
+    """Why the mode exists: with GEMM_PRECISION "fp16" the 4-layer stack meets
+    the reference's own fp16 kernel arithmetic (oracle.fp16_operand_forward,
+    the harness rule) but not always the fp32 baseline; the pairs do."""
+    from optimized import config
+
+    B, S, d, H, F, L = SHAPES[5]
+    cfg = O.TransformerConfig(B, S, d, H, F, L, True)
+    model, params = _model(cfg, 105)
+    x, mask = O.generate_random_case(cfg, 205, 0.25, 1.0)
+    idx = torch.tensor([0, B // 2, B - 1])
+    sub = O.TransformerConfig(3, S, d, H, F, L, True)
+    ref = O.baseline_forward(params, sub, x[idx], mask[idx])
+    old = config.GEMM_PRECISION
+    try:
+        config.GEMM_PRECISION = "fp16"
+        with torch.inference_mode():
+            out16 = model(x.cuda(), mask.cuda()).cpu()[idx]
+        config.GEMM_PRECISION = "fp16x3"
+        with torch.inference_mode():
+            out3 = model(x.cuda(), mask.cuda()).cpu()[idx]
+    finally:
+        config.GEMM_PRECISION = old
+    ref16 = O.fp16_operand_forward(params, sub, x[idx], mask[idx])
+    assert O.compare_outputs(ref16, out16, rtol=RTOL, atol=ATOL).passed
+    r16 = O.compare_outputs(ref, out16, rtol=RTOL, atol=ATOL)
+    r3 = O.compare_outputs(ref, out3, rtol=RTOL, atol=ATOL)
+    assert r3.passed and r3.max_abs_error < 0.75 * r16.max_abs_error, (r3.max_abs_error, r16.max_abs_error)
+
+
+def test_shape14_long_sequence(kernels):
+    """Dashboard shape 14: B=32, S=100,000, d_model 1024, 16 heads x 64, FFN
+    1024, two causal layers (13 GB of fp32 input). The whole batch runs (in
+    chunks the device memory allows); the output is finite, a row run alone
+    gives the same bits as in the batch, and the throughput is recorded."""
+    import time
+
+    B, S, d, H, F, L = 32, 100_000, 1024, 16, 1024, 2
+    cfg = O.TransformerConfig(B, S, d, H, F, L, True)
+    model, _ = _model(cfg, 114)
+    g = torch.Generator(device="cuda").manual_seed(214)
+    x = torch.randn(B, S, d, device="cuda", generator=g)
+    with torch.inference_mode():
+        model(x[:1])                                        # warm-up
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        out = model(x)
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        assert torch.isfinite(out).all()
+        for r in (0, B - 1):
+            alone = model(x[r:r + 1])
+            assert torch.equal(alone[0], out[r]), f"row {r} differs when run alone"
+    print(f"shape 14: {B * S / dt / 1e6:.2f} M tokens/s ({dt * 1e3:.0f} ms for {B}x{S} tokens, 2 layers)")
