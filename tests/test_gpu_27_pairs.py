@@ -78,7 +78,10 @@ def test_linear_gelu_pair_out(kernels, M, N, K):
     assert h.shape == (2, M, N)
     exact = F.gelu(a.double() @ w.double().t() + b.double(), approximate="none")
     hi, lo = h[0].double(), h[1].double()
-    assert (((hi + lo) - exact).abs() / (exact.abs() + 1e-2)).max().item() < 1e-5
+    # the GEMM's bound (4e-6 of the row scale; GELU's slope is at most 1.13)
+    # plus the GELU epilogue's own 7e-7 absolute
+    scale = (a.double().abs() @ w.double().abs().t()).clamp_min(1e-3)
+    assert (((hi + lo) - exact).abs() - 4.6e-6 * scale).max().item() < 1e-6
     assert (lo.abs() <= hi.abs() * 2 ** -10 + 2 ** -24).all(), "lo is the remainder of hi"
 
 
