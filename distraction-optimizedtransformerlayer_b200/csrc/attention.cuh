@@ -37,6 +37,15 @@
 // sequences share one 128-row tile; a row's keys are confined to its own
 // sequence by an interval test. It needs batch stride == S * sequence stride,
 // which the fused QKV buffer has.
+//
+// Split-KV (splits > 1; the reference's split-KV path, attention_wmma.cuh:
+// 662-759, with its combine :1783-1826): when there are too few (stream, query
+// tile) items to fill the SMs and the sequences are long, each item's key
+// range is cut into `splits` runs of kt_per_split key tiles, each run its own
+// work item. A run writes its unnormalised fp32 O rows and their (max, sum)
+// into a workspace slot instead of the output, and attn_combine_kernel folds a
+// query tile's runs: O = sum_s 2^(c (m_s - M)) O_s / sum_s 2^(c (m_s - M)) l_s,
+// in run order (the same bits on every call).
 
 #pragma once
 
@@ -67,7 +76,16 @@ struct AttnParams {
     int head_inner;      // bit t (q=0,k=1,v=2): tensor map dims are {hd, H, rows, B}
     int64_t out_lo;      // 0, or the element offset from `out` of a plane receiving
                          // fp16(o - fp16(o)) (the fp16 pair of the three-product GEMM mode)
+    int splits;          // key runs per query tile (1: no split-KV)
+    int kt_per_split;    // key tiles per run
+    float* ws_o;         // split-KV: [slot][128][HD] unnormalised fp32 O
+    float2* ws_ml;       // split-KV: [slot][128] (row max in score units, row sum)
 };
+
+// Workspace slot of (stream, query tile, run).
+__device__ __forceinline__ int64_t attn_slot(const AttnParams& p, int stream, int qt, int split) {
+    return (static_cast<int64_t>(stream) * p.num_q_tiles + qt) * p.splits + split;
+}
 
 // Loads one 128-row box of `map` at (col, row, head, batch), in whichever
 // dimension order the map was encoded with.
@@ -114,16 +132,20 @@ struct AttnSmem {
     static constexpr uint32_t kColO = kNS * kAttnTile;
 };
 
-// Item -> (stream, query tile), query-tile index descending in the slowest
-// position: under causal masking the longest tiles go first.
-__device__ __forceinline__ void attn_item(const AttnParams& p, int item, int& stream, int& qt) {
-    const int tile_rank = item / p.num_streams;
-    stream = item - tile_rank * p.num_streams;
+// Item -> (stream, query tile, key run), query-tile index descending in the
+// slowest position: under causal masking the longest tiles go first.
+__device__ __forceinline__ void attn_item(const AttnParams& p, int item, int& stream, int& qt, int& split) {
+    const int per_rank = p.num_streams * p.splits;
+    const int tile_rank = item / per_rank;
+    const int rem = item - tile_rank * per_rank;
+    split = rem / p.num_streams;
+    stream = rem - split * p.num_streams;
     qt = p.num_q_tiles - 1 - tile_rank;
 }
 
-// Key range [k_lo, k_hi) in map coordinates that query tile qt can see.
-__device__ __forceinline__ void attn_key_range(const AttnParams& p, int qt, int& k_lo, int& k_hi) {
+// Key range [k_lo, k_hi) in map coordinates that query tile qt can see, cut
+// to key run `split` (k_lo >= k_hi: nothing to do).
+__device__ __forceinline__ void attn_key_range(const AttnParams& p, int qt, int split, int& k_lo, int& k_hi) {
     const int r0 = qt * kAttnTile;
     const int r1 = min(r0 + kAttnTile, p.rows_total) - 1;
     if (p.packed) {
@@ -132,6 +154,11 @@ __device__ __forceinline__ void attn_key_range(const AttnParams& p, int qt, int&
     } else {
         k_lo = 0;
         k_hi = p.causal ? r1 + 1 : p.S;
+    }
+    if (p.splits > 1) {
+        const int run_lo = k_lo + split * p.kt_per_split * kAttnTile;
+        k_hi = min(k_hi, run_lo + p.kt_per_split * kAttnTile);
+        k_lo = run_lo;
     }
 }
 
@@ -238,7 +265,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    const int num_items = p.num_streams * p.num_q_tiles;
+    const int num_items = p.num_streams * p.num_q_tiles * p.splits;
     const bool scan_mask = p.mask_kind == 1 && !p.packed;
 
     // Which group takes an item's first key tile. Items with several tiles
@@ -259,9 +286,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             int k_issued_phase[STAGES], v_issued_phase[STAGES], q_issued_phase[2] = {-1, -1};
             for (int s = 0; s < STAGES; ++s) k_issued_phase[s] = v_issued_phase[s] = -1;
             for (int item = blockIdx.x; item < num_items; item += gridDim.x, ++icount) {
-                int stream, qt, k_lo, k_hi;
-                attn_item(p, item, stream, qt);
-                attn_key_range(p, qt, k_lo, k_hi);
+                int stream, qt, split, k_lo, k_hi;
+                attn_item(p, item, stream, qt, split);
+                attn_key_range(p, qt, split, k_lo, k_hi);
                 const int h = p.packed ? stream : stream % p.H;
                 const int bq = p.packed ? 0 : stream / p.H;
                 int hole = 0;
@@ -437,10 +464,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             const uint32_t t_item = tbase;      // this CTA's index of the item's first key tile
             tbase += static_cast<uint32_t>(n_kt);
 
-            int stream, qt, k_lo, k_hi;
-            attn_item(p, item, stream, qt);
-            attn_key_range(p, qt, k_lo, k_hi);
+            int stream, qt, split, k_lo, k_hi;
+            attn_item(p, item, stream, qt, split);
+            attn_key_range(p, qt, split, k_lo, k_hi);
             const int h = p.packed ? stream : stream % p.H;
+            const bool split_out = p.splits > 1;
+            const int64_t ws_slot = split_out ? attn_slot(p, stream, qt, split) : 0;
             const int rq = qt * kAttnTile + row;
             const bool q_ok = rq < p.rows_total;
             int b, s, klo_r, khi_r;
@@ -468,7 +497,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 return reinterpret_cast<__half*>(p.out) + off;
             };
             if (n_kt == 0) {
-                if (grp == 0 && q_ok) {
+                if (grp == 0 && q_ok && split_out) {
+                    p.ws_ml[ws_slot * kAttnTile + row] = make_float2(-INFINITY, 0.0f);   // an empty run
+                } else if (grp == 0 && q_ok) {
                     __half* op = out_row();
 #pragma unroll
                     for (int i = 0; i < HD; i += 8) {
@@ -684,7 +715,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 ++ccount;
                 continue;
             }
-            float a0 = 1.0f, a1 = 0.0f, l_tot = l_run;
+            float a0 = 1.0f, a1 = 0.0f, l_tot = l_run, m_tot = m_used;
             if (two) {
                 ok = mbar_wait(comb_full, ccount & 1u, abort_flag);
                 if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
@@ -695,6 +726,34 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 a0 = (m_used == -INFINITY) ? 0.0f : fast_exp2((m_used - m) * c);
                 a1 = (other.x == -INFINITY) ? 0.0f : fast_exp2((other.x - m) * c);
                 l_tot = l_run * a0 + other.y * a1;
+                m_tot = m;
+            }
+            if (split_out) {
+                // this key run's unnormalised rows and their (max, sum)
+                float* wo = p.ws_o + (ws_slot * kAttnTile + row) * HD;
+#pragma unroll 1
+                for (int cc = 0; cc < HD; cc += 16) {
+                    uint32_t o0[16], o1[16];
+                    tmem_ld_32x32b_x16(t_o + cc, o0);
+                    if (two) tmem_ld_32x32b_x16(t_o0 + HD + cc, o1);
+                    tmem_ld_wait16(o0);
+                    if (two) tmem_ld_wait16(o1);
+                    float v[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)
+                        v[i] = two ? fmaf(__uint_as_float(o0[i]), a0, __uint_as_float(o1[i]) * a1)
+                                   : __uint_as_float(o0[i]) * a0;
+                    if (q_ok) {
+#pragma unroll
+                        for (int i = 0; i < 16; i += 4)
+                            *reinterpret_cast<float4*>(wo + cc + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+                    }
+                }
+                if (q_ok) p.ws_ml[ws_slot * kAttnTile + row] = make_float2(m_tot, l_tot);
+                tc_fence_before();
+                mbar_arrive(o_free(grp));
+                if (two) mbar_arrive(o_free(1));
+                continue;
             }
             const float inv = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;
             a0 *= inv;
@@ -738,6 +797,62 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (warp == 9) {
         tc_fence_after();
         tmem_dealloc(tmem_base, L::kTmemCols);
+    }
+}
+
+// Split-KV combine: one warp per query row folds the row's key runs, in run
+// order, and stores the normalised fp16 row (and its fp16 pair's lo plane
+// when out_lo is set). Runs with no allowed key (sum 0) add nothing; a row
+// with none at all is written as 0. Not packed (split-KV needs tiles of one
+// sequence). Lane l owns head-dim columns [l * HD/32, (l+1) * HD/32).
+constexpr int kCombineWarps = 8;
+
+template <int HD>
+__global__ void __launch_bounds__(kCombineWarps * 32) attn_combine_kernel(const AttnParams p) {
+    pdl_wait();
+    pdl_launch_dependents();
+    constexpr int kPer = HD / 32;
+    const int lane = threadIdx.x & 31;
+    const int64_t gw = static_cast<int64_t>(blockIdx.x) * kCombineWarps + (threadIdx.x >> 5);
+    const int64_t tiles = static_cast<int64_t>(p.num_streams) * p.num_q_tiles;
+    if (gw >= tiles * kAttnTile) return;
+    const int row = static_cast<int>(gw % kAttnTile);
+    const int64_t tile = gw / kAttnTile;
+    const int qt = static_cast<int>(tile % p.num_q_tiles);
+    const int stream = static_cast<int>(tile / p.num_q_tiles);
+    const int s = qt * kAttnTile + row;
+    if (s >= p.rows_total) return;
+    const float c = p.scale_log2;
+    float m_all = -INFINITY;
+    for (int r = 0; r < p.splits; ++r) {
+        const float2 ml = p.ws_ml[attn_slot(p, stream, qt, r) * kAttnTile + row];
+        if (ml.y > 0.0f) m_all = fmaxf(m_all, ml.x);
+    }
+    float acc[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) acc[i] = 0.0f;
+    float l_all = 0.0f;
+    for (int r = 0; r < p.splits; ++r) {
+        const int64_t sl = attn_slot(p, stream, qt, r);
+        const float2 ml = p.ws_ml[sl * kAttnTile + row];
+        if (!(ml.y > 0.0f)) continue;
+        const float wgt = fast_exp2((ml.x - m_all) * c);
+        l_all = fmaf(ml.y, wgt, l_all);
+        const float* o = p.ws_o + (sl * kAttnTile + row) * HD + lane * kPer;
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) acc[i] = fmaf(o[i], wgt, acc[i]);
+    }
+    const float inv = l_all > 0.0f ? 1.0f / l_all : 0.0f;
+    const int b = stream / p.H, h = stream % p.H;
+    const int64_t off = (p.out_layout == 1) ? ((static_cast<int64_t>(b) * p.S + s) * p.H + h) * HD
+                                            : ((static_cast<int64_t>(b) * p.H + h) * p.S + s) * HD;
+    __half* op = reinterpret_cast<__half*>(p.out) + off + lane * kPer;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const float y = acc[i] * inv;
+        const __half hi = __float2half_rn(y);
+        op[i] = hi;
+        if (p.out_lo != 0) op[p.out_lo + i] = __float2half_rn(y - __half2float(hi));
     }
 }
 

@@ -313,11 +313,42 @@ int launch_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap&
     static DeviceFlags regs_ok;
     if (int rc = ensure_smem(kernel, L::kAlloc, dev, done)) return rc;
     if (int rc = check_regs(kernel, dotl::kAttnThreads, dotl::kAttnRegSplit, regs_ok, dev, "dotl_attention")) return rc;
-    const int items = p.num_streams * p.num_q_tiles;
+    const int items = p.num_streams * p.num_q_tiles * p.splits;
     const int grid = items < sm_count(dev) ? items : sm_count(dev);
-    const cudaError_t e = launch_pdl(kernel, dim3(grid), dim3(dotl::kAttnThreads), L::kAlloc, stream, tq, tk, tv, p);
+    cudaError_t e = launch_pdl(kernel, dim3(grid), dim3(dotl::kAttnThreads), L::kAlloc, stream, tq, tk, tv, p);
     if (e != cudaSuccess) return fail(DOTL_ECUDA, "dotl_attention: launch failed: %s", cudaGetErrorString(e));
+    if (p.splits > 1) {
+        // fold each query tile's key runs (workspace -> out)
+        const int64_t rows = static_cast<int64_t>(p.num_streams) * p.num_q_tiles * dotl::kAttnTile;
+        const dim3 cgrid(static_cast<unsigned>((rows + dotl::kCombineWarps - 1) / dotl::kCombineWarps));
+        e = launch_pdl(dotl::attn_combine_kernel<HD>, cgrid, dim3(dotl::kCombineWarps * 32), 0, stream, p);
+        if (e != cudaSuccess) return fail(DOTL_ECUDA, "dotl_attention: combine launch failed: %s", cudaGetErrorString(e));
+    }
     return check_launch("dotl_attention");
+}
+
+// Split-KV plan for the tcgen05 attention: key runs per query tile and key
+// tiles per run. Split only when the (stream, query tile) items cannot fill
+// the SMs and a tile sees at least 4 key tiles; each run then takes about
+// half an SM's fair share of all key tiles, and at least two.
+int attn_split_plan(int streams, int q_tiles, int max_kt, bool causal, int sms, int* kt_per_split) {
+    *kt_per_split = max_kt;
+    const int64_t items = static_cast<int64_t>(streams) * q_tiles;
+    if (items >= sms || max_kt < 4) return 1;
+    const int64_t total_kt = causal ? static_cast<int64_t>(streams) * q_tiles * (q_tiles + 1) / 2
+                                    : items * max_kt;
+    int64_t kt = (total_kt + 2LL * sms - 1) / (2LL * sms);
+    if (kt < 2) kt = 2;
+    const int splits = static_cast<int>((max_kt + kt - 1) / kt);
+    if (splits < 2) return 1;
+    *kt_per_split = static_cast<int>(kt);
+    return splits;
+}
+
+// Workspace of a split-KV plan: per slot, 128 rows of head_dim fp32 values
+// and a (max, sum) pair.
+int64_t attn_split_bytes(int streams, int q_tiles, int splits, int head_dim) {
+    return static_cast<int64_t>(streams) * q_tiles * splits * dotl::kAttnTile * (head_dim * 4 + 8);
 }
 
 // ------------------------------------------------------------- fused MLP --
@@ -712,10 +743,16 @@ int dotl_linear_ln(const void* a, int64_t M, int64_t K, int64_t lda, const void*
                : launch_gemm_ln<64, 6, false>(ta, tw, tx, tn, tr, tnl, p, dev, s);
 }
 
-int dotl_attention(const void* q, const void* k, const void* v, int B, int H, int S, int head_dim,
-                   const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, const uint8_t* mask,
-                   int mask_kind, const int64_t* mask_strides, int causal, float scale, void* out, int out_layout,
-                   int out_dtype, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// dotl_attention's body. workspace / workspace_bytes: where the split-KV
+// partial rows may go (NULL or too small: no split-KV).
+int attention_run(const void* q, const void* k, const void* v, int B, int H, int S, int head_dim,
+                  const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, const uint8_t* mask,
+                  int mask_kind, const int64_t* mask_strides, int causal, float scale, void* out, int out_layout,
+                  int out_dtype, void* workspace, int64_t workspace_bytes, void* stream) {
     const char* who = "fused_attention_forward";
     if (B < 0 || H < 0 || S < 0) return fail(DOTL_EINVAL, "%s: negative shape", who);
     if (out_layout != 0 && out_layout != 1)
@@ -811,6 +848,10 @@ int dotl_attention(const void* q, const void* k, const void* v, int B, int H, in
     p.out = out;
     p.out_layout = out_layout;
     p.out_lo = out_lo;
+    p.splits = 1;
+    p.kt_per_split = 0;
+    p.ws_o = nullptr;
+    p.ws_ml = nullptr;
 
     const uint32_t box_cols = head_dim < 64 ? static_cast<uint32_t>(head_dim) : 64u;
     const void* bases[3] = {q, k, v};
@@ -854,12 +895,52 @@ int dotl_attention(const void* q, const void* k, const void* v, int B, int H, in
     }
     int dev;
     if (int rc = current_device(&dev)) return rc;
+    if (!packed && workspace != nullptr) {
+        int kt = 0;
+        const int splits = attn_split_plan(p.num_streams, p.num_q_tiles, (S + dotl::kAttnTile - 1) / dotl::kAttnTile,
+                                           causal != 0, sm_count(dev), &kt);
+        const int64_t need = attn_split_bytes(p.num_streams, p.num_q_tiles, splits, head_dim);
+        if (splits > 1 && workspace_bytes >= need && aligned16(workspace)) {
+            p.splits = splits;
+            p.kt_per_split = kt;
+            p.ws_o = static_cast<float*>(workspace);
+            p.ws_ml = reinterpret_cast<float2*>(static_cast<uint8_t*>(workspace) +
+                                                static_cast<int64_t>(p.num_streams) * p.num_q_tiles * splits *
+                                                    dotl::kAttnTile * head_dim * 4);
+        }
+    }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     switch (head_dim) {
         case 32: return launch_attn<32, 4>(maps[0], maps[1], maps[2], p, dev, s);
         case 64: return launch_attn<64, 3>(maps[0], maps[1], maps[2], p, dev, s);
         default: return launch_attn<128, 2>(maps[0], maps[1], maps[2], p, dev, s);
     }
+}
+
+}  // namespace
+
+extern "C" {
+
+int dotl_attention(const void* q, const void* k, const void* v, int B, int H, int S, int head_dim,
+                   const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, const uint8_t* mask,
+                   int mask_kind, const int64_t* mask_strides, int causal, float scale, void* out, int out_layout,
+                   int out_dtype, void* workspace, int64_t workspace_bytes, void* stream) {
+    return attention_run(q, k, v, B, H, S, head_dim, q_strides, k_strides, v_strides, mask, mask_kind, mask_strides,
+                         causal, scale, out, out_layout, out_dtype, workspace, workspace_bytes, stream);
+}
+
+int dotl_attention_workspace_bytes(int B, int H, int S, int head_dim, int causal, int64_t* bytes) {
+    if (bytes == nullptr || B < 0 || H < 0 || S < 0) return fail(DOTL_EINVAL, "dotl_attention_workspace_bytes: bad arguments");
+    *bytes = 0;
+    const bool tc = head_dim == 32 || head_dim == 64 || head_dim == 128;
+    if (!tc || B == 0 || H == 0 || S < dotl::kAttnTile) return DOTL_OK;   // no split-KV there
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    const int streams = B * H, q_tiles = (S + dotl::kAttnTile - 1) / dotl::kAttnTile;
+    int kt = 0;
+    const int splits = attn_split_plan(streams, q_tiles, q_tiles, causal != 0, sm_count(dev), &kt);
+    if (splits > 1) *bytes = attn_split_bytes(streams, q_tiles, splits, head_dim);
+    return DOTL_OK;
 }
 
 int dotl_ffn(const void* a, int64_t M, int64_t D, int64_t lda, const void* w1, int64_t F, int64_t ldw1,

@@ -51,7 +51,8 @@ _SIGNATURES = {
     "dotl_linear_ln": ([_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _i32, _vp, _i64,
                         _vp, _vp, _f32, _vp, _i32, _i64, _vp, _i32, _i32, _vp], _i32),
     "dotl_attention": ([_vp, _vp, _vp, _i32, _i32, _i32, _i32, _P64, _P64, _P64, _vp, _i32, _P64,
-                        _i32, _f32, _vp, _i32, _i32, _vp], _i32),
+                        _i32, _f32, _vp, _i32, _i32, _vp, _i64, _vp], _i32),
+    "dotl_attention_workspace_bytes": ([_i32, _i32, _i32, _i32, _i32, _P64], _i32),
     "dotl_ffn": ([_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _i64, _vp, _i32,
                   _vp, _i64, _vp, _vp, _f32, _vp, _i32, _i64, _vp, _vp], _i32),
     "dotl_peer_alloc": ([_i64, ctypes.POINTER(_vp)], _i32),
@@ -369,12 +370,15 @@ def linear_ln(a16: torch.Tensor, w16: torch.Tensor, bias: torch.Tensor, ln_w: to
 def attention_packed(q16: torch.Tensor, k16: torch.Tensor, v16: torch.Tensor, causal: bool,
                      scale: float, key_mask: Optional[torch.Tensor] = None,
                      full_mask: Optional[torch.Tensor] = None, out_layout: int = 1,
-                     out: Optional[torch.Tensor] = None, out_pair: bool = False) -> torch.Tensor:
+                     out: Optional[torch.Tensor] = None, out_pair: bool = False,
+                     split_kv: bool = True) -> torch.Tensor:
     """Flash attention over fp16 [B,H,S,hd] views (head_dim stride 1).
 
     key_mask: bool [B,S] (True = may attend), any strides.
     full_mask: bool tensor already expanded to [B,H,S,S] (any strides).
     out_pair: the output is an fp16 pair [2, *shape] (hi, lo planes).
+    split_kv: give the kernel a workspace (from torch's caching allocator) so
+    shapes with few query tiles and long key ranges run split-KV.
     """
     B, H, S, hd = q16.shape
     shape = (B, S, H * hd) if out_layout == 1 else (B, H, S, hd)
@@ -382,6 +386,11 @@ def attention_packed(q16: torch.Tensor, k16: torch.Tensor, v16: torch.Tensor, ca
         out = torch.empty(((2,) if out_pair else ()) + shape, dtype=torch.float16, device=q16.device)
     if out_pair and (tuple(out.shape) != (2, *shape) or not out.is_contiguous()):
         raise RuntimeError("attention_packed: a pair output must be a contiguous [2, *shape] fp16 tensor")
+    ws = None
+    if split_kv:
+        nbytes = attention_workspace_bytes(B, H, S, hd, causal, q16.device)
+        if nbytes:
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=q16.device)
     if key_mask is not None:
         kind, mptr, ms = MASK_KEY, key_mask.data_ptr(), (key_mask.stride(0), 0, 0, key_mask.stride(1))
     elif full_mask is not None:
@@ -392,9 +401,26 @@ def attention_packed(q16: torch.Tensor, k16: torch.Tensor, v16: torch.Tensor, ca
         q16.data_ptr(), k16.data_ptr(), v16.data_ptr(), B, H, S, hd,
         _i64arr(q16.stride()[:3]), _i64arr(k16.stride()[:3]), _i64arr(v16.stride()[:3]),
         mptr, kind, _i64arr(ms), 1 if causal else 0, float(scale), out.data_ptr(), out_layout,
-        F16X2 if out_pair else F16, _stream(q16.device))
+        F16X2 if out_pair else F16, None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(),
+        _stream(q16.device))
     _check(rc)
     return out
+
+
+_WS_BYTES: Dict[Tuple, int] = {}
+
+
+def attention_workspace_bytes(B: int, H: int, S: int, hd: int, causal: bool, device: torch.device) -> int:
+    """Split-KV workspace dotl_attention uses for this shape (0: none),
+    memoised per shape and device."""
+    key = (B, H, S, hd, bool(causal), torch.device(device).index)
+    n = _WS_BYTES.get(key)
+    if n is None:
+        out = ctypes.c_int64(0)
+        with torch.cuda.device(device):
+            _check(lib().dotl_attention_workspace_bytes(B, H, S, hd, 1 if causal else 0, ctypes.byref(out)))
+        n = _WS_BYTES[key] = int(out.value)
+    return n
 
 
 # -------------------------------------------- reference-named entry points ---

@@ -172,11 +172,26 @@ int dotl_ffn(const void* a, int64_t M, int64_t D, int64_t lda, const void* w1, i
  * Fully masked query rows are written as 0. head_dim 32, 64 or 128 run on the
  * tcgen05 kernel; other multiples of 8 up to 256 on a CUDA-core flash kernel
  * (the reference's scalar/wmma shapes, e.g. head_dim 8 and 256).
+ *   workspace: NULL, or at least dotl_attention_workspace_bytes(...) bytes of
+ *   16-byte-aligned device memory. Given one, shapes with too few (batch,
+ *   head, 128-row query tile) items to fill the SMs and long key ranges run
+ *   split-KV: each tile's keys in runs on separate CTAs, then a combine
+ *   kernel folds the runs (the reference's split-KV path and its combine,
+ *   attention_wmma.cuh:662-759, 1783-1826). Same results either way to
+ *   fp32 rounding; repeat calls give the same bits.
  */
 int dotl_attention(const void* q, const void* k, const void* v, int B, int H, int S, int head_dim,
                    const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
                    const uint8_t* mask, int mask_kind, const int64_t* mask_strides, int causal,
-                   float scale, void* out, int out_layout, int out_dtype, void* stream);
+                   float scale, void* out, int out_layout, int out_dtype, void* workspace,
+                   int64_t workspace_bytes, void* stream);
+
+/*
+ * Workspace dotl_attention would use for split-KV on this shape on the current
+ * device (0: it would not split). Replaces the caching-allocator workspace of
+ * the reference's split path (attention_wmma.cuh:1925-1937).
+ */
+int dotl_attention_workspace_bytes(int B, int H, int S, int head_dim, int causal, int64_t* bytes);
 
 /*
  * Peer memory for the tensor-parallel layer (one process per GPU). These are

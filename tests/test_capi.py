@@ -79,30 +79,30 @@ def test_linear_empty_m_is_ok(lib):
 def test_attention_rejects_head_dim(lib):
     st = (ctypes.c_int64 * 3)(0, 0, 0)
     for hd in (4, 12, 264):
-        rc = lib.dotl_attention(16, 16, 16, 1, 1, 8, hd, st, st, st, None, 0, None, 0, 0.1, 16, 0, 1, None)
+        rc = lib.dotl_attention(16, 16, 16, 1, 1, 8, hd, st, st, st, None, 0, None, 0, 0.1, 16, 0, 1, None, 0, None)
         assert rc == 2 and "head_dim" in _err(lib)
 
 
 def test_attention_rejects_generic_grid_overflow(lib):
     # head_dim 8 takes the CUDA-core kernel, one grid row per (batch, head)
     st = (ctypes.c_int64 * 3)(0, 0, 0)
-    rc = lib.dotl_attention(16, 16, 16, 65536, 1, 8, 8, st, st, st, None, 0, None, 0, 0.1, 16, 0, 1, None)
+    rc = lib.dotl_attention(16, 16, 16, 65536, 1, 8, 8, st, st, st, None, 0, None, 0, 0.1, 16, 0, 1, None, 0, None)
     assert rc == 2 and "65535" in _err(lib)
 
 
 def test_attention_rejects_layout_and_mask(lib):
     st = (ctypes.c_int64 * 3)(0, 0, 0)
-    assert lib.dotl_attention(16, 16, 16, 1, 1, 8, 64, st, st, st, None, 0, None, 0, 0.1, 16, 2, 1, None) == 1
+    assert lib.dotl_attention(16, 16, 16, 1, 1, 8, 64, st, st, st, None, 0, None, 0, 0.1, 16, 2, 1, None, 0, None) == 1
     assert "out_layout" in _err(lib)
-    assert lib.dotl_attention(16, 16, 16, 1, 1, 8, 64, st, st, st, None, 1, None, 0, 0.1, 16, 0, 1, None) == 1
+    assert lib.dotl_attention(16, 16, 16, 1, 1, 8, 64, st, st, st, None, 1, None, 0, 0.1, 16, 0, 1, None, 0, None) == 1
     assert "needs mask" in _err(lib)
-    assert lib.dotl_attention(16, 16, 16, 1, 1, 8, 64, st, st, st, None, 0, None, 0, 0.1, 16, 0, 0, None) == 1
+    assert lib.dotl_attention(16, 16, 16, 1, 1, 8, 64, st, st, st, None, 0, None, 0, 0.1, 16, 0, 0, None, 0, None) == 1
     assert "out dtype" in _err(lib)
 
 
 def test_attention_rejects_unaligned_strides(lib):
     st = (ctypes.c_int64 * 3)(64 * 8, 64, 12)
-    rc = lib.dotl_attention(16, 16, 16, 1, 1, 8, 64, st, st, st, None, 0, None, 0, 0.1, 16, 0, 1, None)
+    rc = lib.dotl_attention(16, 16, 16, 1, 1, 8, 64, st, st, st, None, 0, None, 0, 0.1, 16, 0, 1, None, 0, None)
     assert rc == 2 and "multiples of 8" in _err(lib)
 
 

@@ -157,3 +157,44 @@ def test_uncovered_precision_raises(kernels):
         kernels.fused_attention_forward(q, q, q, None, False, 0.125, 1, 0, 0)
     with pytest.raises(RuntimeError, match="not covered"):
         kernels.fused_attention_forward(q, q, q, None, False, 0.125, 0, 0, 4)
+
+
+# Split-KV: shapes with fewer (batch, head, query tile) items than SMs and long
+# key ranges, where dotl_attention cuts each tile's keys into runs and a
+# combine kernel folds them (the reference's split path and combine,
+# attention_wmma.cuh:662-759, 1783-1826). (batch, heads, seq, head_dim,
+# causal, per-row valid key counts or None)
+SPLIT_CASES = [
+    (1, 2, 2048, 64, True, None),
+    (1, 4, 4096, 128, False, None),
+    (2, 1, 1536, 32, True, [1536, 300]),
+    (2, 2, 1024, 64, False, [1024, 0]),      # a row with no valid key: zeros
+    (1, 8, 2048, 64, True, None),            # verify_kernel's "long seq causal"
+]
+
+
+@pytest.mark.parametrize("case", SPLIT_CASES)
+def test_split_kv_matches_one_pass(kernels, case):
+    b, h, s, d, causal, lengths = case
+    assert kernels.attention_workspace_bytes(b, h, s, d, causal, torch.device("cuda")) > 0, \
+        "the plan must split this shape"
+    g = torch.Generator(device="cuda").manual_seed(s + d)
+    q, k, v = (torch.randn(b, h, s, d, device="cuda", generator=g).half() for _ in range(3))
+    key_mask = None
+    if lengths is not None:
+        key_mask = torch.arange(s, device="cuda")[None, :] < torch.tensor(lengths, device="cuda")[:, None]
+    scale = d ** -0.5
+    one = kernels.attention_packed(q, k, v, causal, scale, key_mask=key_mask, split_kv=False)
+    split = kernels.attention_packed(q, k, v, causal, scale, key_mask=key_mask)
+    again = kernels.attention_packed(q, k, v, causal, scale, key_mask=key_mask)
+    assert torch.equal(split, again), "split-KV must give the same bits on every call"
+    # the runs fold in another order than one pass: within fp16 output rounding
+    assert (split.float() - one.float()).abs().max().item() <= 2e-3
+    mask4 = key_mask[:, None, None, :] if key_mask is not None else None
+    ref = reference_attention_f64(q, k, v, mask4, causal, scale).transpose(1, 2).reshape(b, s, h * d)
+    err = (split.double() - ref).abs().max().item()
+    assert err <= TOL, err
+    pair = kernels.attention_packed(q, k, v, causal, scale, key_mask=key_mask, out_pair=True)
+    assert torch.equal(pair[0], split)
+    if lengths is not None and 0 in lengths:
+        assert torch.all(split[lengths.index(0)] == 0)
