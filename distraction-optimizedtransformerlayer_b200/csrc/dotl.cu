@@ -328,17 +328,21 @@ int launch_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap&
 }
 
 // Split-KV plan for the tcgen05 attention: key runs per query tile and key
-// tiles per run. Split only when the (stream, query tile) items cannot fill
-// the SMs and a tile sees at least 4 key tiles; each run then takes about
-// half an SM's fair share of all key tiles, and at least two.
+// tiles per run. Each work item pays a fixed cost (its Q tile, the pipeline
+// fill, the epilogue) and the runs a combine pass, which measured on B200 as
+// a loss whenever the items already came near the SM count (config 2's 128
+// items of at most 4 key tiles: 10.3 -> 19.8 us; 128 items of 32 key tiles:
+// 44 -> 65 us). So split only when the items fill at most a quarter of the
+// SMs and a tile sees at least 8 key tiles, in runs of at least 4 key tiles
+// (about one SM's fair share of all key tiles when that is more).
 int attn_split_plan(int streams, int q_tiles, int max_kt, bool causal, int sms, int* kt_per_split) {
     *kt_per_split = max_kt;
     const int64_t items = static_cast<int64_t>(streams) * q_tiles;
-    if (items >= sms || max_kt < 4) return 1;
+    if (items * 4 > sms || max_kt < 8) return 1;
     const int64_t total_kt = causal ? static_cast<int64_t>(streams) * q_tiles * (q_tiles + 1) / 2
                                     : items * max_kt;
-    int64_t kt = (total_kt + 2LL * sms - 1) / (2LL * sms);
-    if (kt < 2) kt = 2;
+    int64_t kt = (total_kt + sms - 1) / sms;
+    if (kt < 4) kt = 4;
     const int splits = static_cast<int>((max_kt + kt - 1) / kt);
     if (splits < 2) return 1;
     *kt_per_split = static_cast<int>(kt);
