@@ -933,6 +933,68 @@ int dotl_attention(const void* q, const void* k, const void* v, int B, int H, in
                          causal, scale, out, out_layout, out_dtype, workspace, workspace_bytes, stream);
 }
 
+// ---------------------------------------------- attention without allocation --
+//
+// For callers that cannot allocate device memory on their own: a caller whose
+// host side has no CUDA allocator it may use (a binding that can only hand
+// over the pointers it already owns), or one running while allocation is off
+// limits to it (inside a memory pool it must not grow). The split-KV scratch
+// lives in one static device array of kStaticScratchBytes instead of a
+// caller workspace. The array is per device and per process, held from the
+// library's load until exit, and shared by every call.
+
+}  // extern "C"
+
+namespace {
+
+constexpr int64_t kStaticScratchBytes = int64_t{16} << 20;
+static_assert(kStaticScratchBytes == DOTL_ATTENTION_STATIC_SCRATCH_BYTES, "the header states the array's size");
+static __device__ __align__(256) uint8_t g_attn_static_scratch[kStaticScratchBytes];
+
+// The array's device address on device `dev` (the current device). The name
+// in host code only stands in for the symbol; the address comes from
+// cudaGetSymbolAddress, once per device, with that device current.
+int static_scratch_address(int dev, void** out) {
+    static std::atomic<void*> addr[kMaxDevices];
+    if (dev < 0 || dev >= kMaxDevices) return fail(DOTL_EUNSUPPORTED, "dotl_attention_static_scratch: device %d", dev);
+    void* p = addr[dev].load(std::memory_order_acquire);
+    if (p == nullptr) {
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_attn_static_scratch);
+        if (e != cudaSuccess || p == nullptr)
+            return fail(DOTL_ECUDA, "dotl_attention_static_scratch: cudaGetSymbolAddress failed: %s",
+                        cudaGetErrorString(e));
+        addr[dev].store(p, std::memory_order_release);
+    }
+    *out = p;
+    return DOTL_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int dotl_attention_static_scratch(const void* q, const void* k, const void* v, int B, int H, int S, int head_dim,
+                                  const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                                  const uint8_t* mask, int mask_kind, const int64_t* mask_strides, int causal,
+                                  float scale, void* out, int out_layout, int out_dtype, void* stream) {
+    int64_t need = 0;
+    if (int rc = dotl_attention_workspace_bytes(B, H, S, head_dim, causal, &need)) return rc;
+    if (need > kStaticScratchBytes)
+        return fail(DOTL_EUNSUPPORTED,
+                    "dotl_attention_static_scratch: B=%d H=%d S=%d head_dim=%d needs %lld bytes of split-KV scratch, "
+                    "over the %lld-byte static array; call dotl_attention with a workspace instead",
+                    B, H, S, head_dim, (long long)need, (long long)kStaticScratchBytes);
+    void* scratch = nullptr;
+    if (need > 0) {
+        int dev;
+        if (int rc = current_device(&dev)) return rc;
+        if (int rc = static_scratch_address(dev, &scratch)) return rc;
+    }
+    return attention_run(q, k, v, B, H, S, head_dim, q_strides, k_strides, v_strides, mask, mask_kind, mask_strides,
+                         causal, scale, out, out_layout, out_dtype, scratch, need > 0 ? kStaticScratchBytes : 0,
+                         stream);
+}
+
 int dotl_attention_workspace_bytes(int B, int H, int S, int head_dim, int causal, int64_t* bytes) {
     if (bytes == nullptr || B < 0 || H < 0 || S < 0) return fail(DOTL_EINVAL, "dotl_attention_workspace_bytes: bad arguments");
     *bytes = 0;

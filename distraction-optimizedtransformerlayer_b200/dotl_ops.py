@@ -53,6 +53,8 @@ _SIGNATURES = {
     "dotl_attention": ([_vp, _vp, _vp, _i32, _i32, _i32, _i32, _P64, _P64, _P64, _vp, _i32, _P64,
                         _i32, _f32, _vp, _i32, _i32, _vp, _i64, _vp], _i32),
     "dotl_attention_workspace_bytes": ([_i32, _i32, _i32, _i32, _i32, _P64], _i32),
+    "dotl_attention_static_scratch": ([_vp, _vp, _vp, _i32, _i32, _i32, _i32, _P64, _P64, _P64, _vp, _i32, _P64,
+                                       _i32, _f32, _vp, _i32, _i32, _vp], _i32),
     "dotl_ffn": ([_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _i64, _vp, _i32,
                   _vp, _i64, _vp, _vp, _f32, _vp, _i32, _i64, _vp, _vp], _i32),
     "dotl_peer_alloc": ([_i64, ctypes.POINTER(_vp)], _i32),

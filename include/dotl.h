@@ -194,6 +194,29 @@ int dotl_attention(const void* q, const void* k, const void* v, int B, int H, in
 int dotl_attention_workspace_bytes(int B, int H, int S, int head_dim, int causal, int64_t* bytes);
 
 /*
+ * dotl_attention without a caller workspace, for callers that cannot allocate
+ * device memory themselves: a host binding with no CUDA allocator of its own
+ * to call, or code running where growing device memory is not allowed. It
+ * allocates nothing. The split-KV scratch is one static device array of
+ * DOTL_ATTENTION_STATIC_SCRATCH_BYTES per device, held by every GPU that loads
+ * the library until the process exits. Shapes whose split plan needs more
+ * (dotl_attention_workspace_bytes above the limit) are rejected with
+ * DOTL_EUNSUPPORTED; shapes that need none run the one-pass kernel. Every call
+ * on a device uses the same array: calls whose kernels may overlap on the GPU
+ * (other streams, other threads) race on it, so serialise them, e.g. on one
+ * stream. Each call writes every scratch word it reads, so nothing needs
+ * clearing between calls. The first call on a device looks up the array's
+ * device address (with that device current); make it before any stream
+ * capture. Otherwise the same arguments and results as dotl_attention.
+ * No counterpart in the reference.
+ */
+#define DOTL_ATTENTION_STATIC_SCRATCH_BYTES (16 << 20)
+int dotl_attention_static_scratch(const void* q, const void* k, const void* v, int B, int H, int S, int head_dim,
+                                  const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                                  const uint8_t* mask, int mask_kind, const int64_t* mask_strides, int causal,
+                                  float scale, void* out, int out_layout, int out_dtype, void* stream);
+
+/*
  * Peer memory for the tensor-parallel layer (one process per GPU). These are
  * setup calls, made once per peer group, and the only entry points that
  * allocate or map device memory:
