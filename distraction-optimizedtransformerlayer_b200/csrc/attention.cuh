@@ -606,29 +606,33 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 tc_fence_after();
                 float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
                 if (interior) {
-                    // Every key allowed: 64 scores per TMEM read (two reads per
-                    // pass instead of four).
+                    // Every key allowed: the row max from all 128 scores in one
+                    // TMEM round trip (four loads, one wait), then the
+                    // exponentials over two reads of 64 (s c - m c as paired
+                    // fp32 FMAs), P stored over the columns already read.
                     float mx8[8];
 #pragma unroll
                     for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
-#pragma unroll 1
-                    for (int h = 0; h < 2; ++h) {
-                        uint32_t sr[2][32];
-                        tmem_ld_32x32b_x32(t_s + h * 64, sr[0]);
-                        tmem_ld_32x32b_x32(t_s + h * 64 + 32, sr[1]);
+                    {
+                        uint32_t sr[4][32];
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) tmem_ld_32x32b_x32(t_s + q * 32, sr[q]);
                         tmem_ld_wait(sr[0]);
                         tmem_ld_wait(sr[1]);
+                        tmem_ld_wait(sr[2]);
+                        tmem_ld_wait(sr[3]);
 #pragma unroll
-                        for (int u = 0; u < 2; ++u)
+                        for (int q = 0; q < 4; ++q)
 #pragma unroll
                             for (int i = 0; i < 32; i += 2)
-                                mx8[(i >> 1) & 7] = fmax3(mx8[(i >> 1) & 7], __uint_as_float(sr[u][i]),
-                                                          __uint_as_float(sr[u][i + 1]));
+                                mx8[(i >> 1) & 7] = fmax3(mx8[(i >> 1) & 7], __uint_as_float(sr[q][i]),
+                                                          __uint_as_float(sr[q][i + 1]));
                     }
                     const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                            fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
                     const float mc = softmax_rescale(mx);
                     if (!alive) break;
+                    const unsigned long long c2 = f32x2(c, c), nmc2 = f32x2(-mc, -mc);
 #pragma unroll 1
                     for (int h = 0; h < 2; ++h) {
                         uint32_t sr[2][32];
@@ -641,8 +645,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                             uint32_t pk[16];
 #pragma unroll
                             for (int i = 0; i < 16; ++i) {
-                                const float p0 = fast_exp2(fmaf(__uint_as_float(sr[u][2 * i]), c, -mc));
-                                const float p1 = fast_exp2(fmaf(__uint_as_float(sr[u][2 * i + 1]), c, -mc));
+                                float a0, a1;
+                                f32x2_split(fma_x2(f32x2(__uint_as_float(sr[u][2 * i]),
+                                                         __uint_as_float(sr[u][2 * i + 1])), c2, nmc2),
+                                            a0, a1);
+                                const float p0 = fast_exp2(a0);
+                                const float p1 = fast_exp2(a1);
                                 sum8[i & 7] += p0 + p1;
                                 pk[i] = pack_half2(p0, p1);
                             }
