@@ -307,8 +307,9 @@ class _ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def _attention_pairs(cfg, mask):
-    """Allowed (query, key) pairs per head, summed over the batch."""
+def _attention_pairs(cfg, mask, batch=None):
+    """Allowed (query, key) pairs per head, summed over the batch rows run
+    (`batch` rows without a mask; the mask's rows with one)."""
     S = cfg.seq_len
     if mask is not None:
         total = 0
@@ -316,7 +317,8 @@ def _attention_pairs(cfg, mask):
             # every query row (padded ones too) sees keys < n, and j <= i if causal
             total += (n * (n + 1) // 2 + (S - n) * n) if cfg.causal else S * n
         return total
-    return cfg.batch_size * (S * (S + 1) // 2 if cfg.causal else S * S)
+    rows = cfg.batch_size if batch is None else batch
+    return rows * (S * (S + 1) // 2 if cfg.causal else S * S)
 
 
 def _layer_ops(model, x, mask, kernels, cfg):
@@ -344,7 +346,7 @@ def _layer_ops(model, x, mask, kernels, cfg):
                             out_half=True)
     x2 = kernels.linear_fp16(h, layer.ffn_out.half_weight(), _f32_param(layer.ffn_out, "bias"), resid=x1,
                              row_valid=row_valid, resid_mode=3 if use_mask else 1)
-    pairs = _attention_pairs(cfg, mask.cpu() if use_mask else None)
+    pairs = _attention_pairs(cfg, mask.cpu() if use_mask else None, batch=B)
     lnw2, lnb2 = _f32_param(layer.norm2, "weight"), _f32_param(layer.norm2, "bias")
     lnwf, lnbf = _f32_param(model.final_norm, "weight"), _f32_param(model.final_norm, "bias")
     out_f = torch.empty_like(x)

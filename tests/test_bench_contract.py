@@ -68,6 +68,7 @@ def test_attention_pairs_counts():
 
     cfg = bench._Cfg(2, 1)   # causal, no mask
     assert bench._attention_pairs(cfg, None) == 4 * 512 * 513 // 2
+    assert bench._attention_pairs(cfg, None, batch=1) == 512 * 513 // 2   # one shard's rows
     cfg1 = bench._Cfg(1, 1)  # key padding
     mask = torch.zeros(2, 128, dtype=torch.bool)
     mask[0, :100] = True
