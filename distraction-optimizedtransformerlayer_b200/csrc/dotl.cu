@@ -162,8 +162,8 @@ int encode_f16_map(CUtensorMap* map, const void* base, int rank, const cuuint64_
 // ------------------------------------------------------------------ GEMM --
 
 template <int BN, int STAGES, bool OUT_F16, bool SPLIT2 = false, bool PEER = false>
-int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const dotl::GemmParams& p,
-                int dev, cudaStream_t stream, const dotl::GemmPeerOut* po_in = nullptr) {
+int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const CUtensorMap& tr,
+                const dotl::GemmParams& p, int dev, cudaStream_t stream, const dotl::GemmPeerOut* po_in = nullptr) {
     using L = dotl::GemmSmem<BN, STAGES>;
     auto kernel = dotl::gemm_tc_kernel<BN, STAGES, OUT_F16, SPLIT2, PEER>;
     static const dotl::GemmPeerOut kNoPeers = {};
@@ -189,10 +189,10 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap&
         attr[1].val.clusterDim.z = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 2;
-        e = cudaLaunchKernelEx(&cfg, kernel, ta, tw, to, p, po);
+        e = cudaLaunchKernelEx(&cfg, kernel, ta, tw, to, tr, p, po);
     } else {
         const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
-        e = launch_pdl(kernel, dim3(grid), dim3(dotl::kGemmThreads), L::kAlloc, stream, ta, tw, to, p, po);
+        e = launch_pdl(kernel, dim3(grid), dim3(dotl::kGemmThreads), L::kAlloc, stream, ta, tw, to, tr, p, po);
     }
     if (e != cudaSuccess) return fail(DOTL_ECUDA, "dotl_linear: launch failed: %s", cudaGetErrorString(e));
     return check_launch("dotl_linear");
@@ -557,6 +557,10 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
     CUtensorMap to;
     const int store_dtype = out_dtype == DOTL_F16X2 ? DOTL_F16 : out_dtype;
     if (int rc = encode_out_map(&to, out, M, N, ldo, store_dtype, who)) return rc;
+    // the residual in as 32 x 32 fp32 blocks (fp32 out); without one the map is unused
+    CUtensorMap tr = to;
+    if (resid_mode != DOTL_RESID_NONE && resid_mode != DOTL_MASK_ROWS)
+        if (int rc = encode_out_map(&tr, const_cast<float*>(resid), M, N, ldr, DOTL_F32, who)) return rc;
     // DOTL_F16X2 out: the lo plane, M rows of ldo below the hi plane
     dotl::GemmPeerOut lo_out = {};
     if (out_dtype == DOTL_F16X2)
@@ -585,16 +589,16 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
     const bool f16 = store_dtype == DOTL_F16;
     const dotl::GemmPeerOut* po = &lo_out;
     if (split2)
-        return f16 ? launch_gemm<128, 5, true, true>(ta, tw, to, p, dev, s, po)
-                   : launch_gemm<128, 5, false, true>(ta, tw, to, p, dev, s, po);
+        return f16 ? launch_gemm<128, 5, true, true>(ta, tw, to, tr, p, dev, s, po)
+                   : launch_gemm<128, 5, false, true>(ta, tw, to, tr, p, dev, s, po);
     if (bn == 256)
-        return f16 ? launch_gemm<256, 4, true>(ta, tw, to, p, dev, s, po)
-                   : launch_gemm<256, 4, false>(ta, tw, to, p, dev, s, po);
+        return f16 ? launch_gemm<256, 4, true>(ta, tw, to, tr, p, dev, s, po)
+                   : launch_gemm<256, 4, false>(ta, tw, to, tr, p, dev, s, po);
     if (bn == 64)
-        return f16 ? launch_gemm<64, 7, true>(ta, tw, to, p, dev, s, po)
-                   : launch_gemm<64, 7, false>(ta, tw, to, p, dev, s, po);
-    return f16 ? launch_gemm<128, 5, true>(ta, tw, to, p, dev, s, po)
-               : launch_gemm<128, 5, false>(ta, tw, to, p, dev, s, po);
+        return f16 ? launch_gemm<64, 7, true>(ta, tw, to, tr, p, dev, s, po)
+                   : launch_gemm<64, 7, false>(ta, tw, to, tr, p, dev, s, po);
+    return f16 ? launch_gemm<128, 5, true>(ta, tw, to, tr, p, dev, s, po)
+               : launch_gemm<128, 5, false>(ta, tw, to, tr, p, dev, s, po);
 }
 
 int dotl_linear_peer(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,
@@ -640,9 +644,9 @@ int dotl_linear_peer(const void* a, int64_t M, int64_t K, int64_t lda, const voi
     p.out = outs[0];
     p.ldo = ldo;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (bn == 256) return launch_gemm<256, 4, false, false, true>(ta, tw, po.map[0], p, dev, s, &po);
-    if (bn == 64) return launch_gemm<64, 7, false, false, true>(ta, tw, po.map[0], p, dev, s, &po);
-    return launch_gemm<128, 5, false, false, true>(ta, tw, po.map[0], p, dev, s, &po);
+    if (bn == 256) return launch_gemm<256, 4, false, false, true>(ta, tw, po.map[0], po.map[0], p, dev, s, &po);
+    if (bn == 64) return launch_gemm<64, 7, false, false, true>(ta, tw, po.map[0], po.map[0], p, dev, s, &po);
+    return launch_gemm<128, 5, false, false, true>(ta, tw, po.map[0], po.map[0], p, dev, s, &po);
 }
 
 int dotl_linear_ln(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,

@@ -99,8 +99,9 @@ struct GemmSmem {
     static constexpr uint32_t kStageBufBytes = 32 * 128;
     static constexpr uint32_t kOffBar = kOffStage + 8 * kStageBufBytes;
     // full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], drain (GemmBars),
-    // then the split-K pair's peer_ready, recv_full and exit
-    static constexpr uint32_t kNumBars = 2 * STAGES + 8;
+    // then the split-K pair's peer_ready, recv_full and exit, then one
+    // residual-block barrier per epilogue warp
+    static constexpr uint32_t kNumBars = 2 * STAGES + 16;
     static constexpr uint32_t kOffSlot = kOffBar + kNumBars * 8;
     static constexpr uint32_t kOffAbort = kOffSlot + 4;
     static constexpr uint32_t kBytes = kOffAbort + 4;
@@ -236,8 +237,8 @@ mma_done:
 template <int BN, int STAGES, bool OUT_F16, bool SPLIT2 = false, bool PEER = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
-                   const __grid_constant__ CUtensorMap tmap_out, const GemmParams p,
-                   const __grid_constant__ GemmPeerOut po) {
+                   const __grid_constant__ CUtensorMap tmap_out, const __grid_constant__ CUtensorMap tmap_r,
+                   const GemmParams p, const __grid_constant__ GemmPeerOut po) {
     using L = GemmSmem<BN, STAGES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -268,11 +269,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         mbar_init(peer_ready, 256);
         mbar_init(recv_full, 256);
         mbar_init(exit_bar, 2);
+        for (int w = 0; w < 8; ++w) mbar_init(bar0 + 8u * (GemmBars<STAGES>::kCount + 3 + w), 1);
         *abort_flag = 0;
         fence_barrier_init();
         tma_prefetch_map(&tmap_a);
         tma_prefetch_map(&tmap_w);
         tma_prefetch_map(&tmap_out);
+        tma_prefetch_map(&tmap_r);
         if constexpr (PEER)
             for (int r = 0; r * po.rows < p.M && r < kGemmPeerMax; ++r) tma_prefetch_map(&po.map[r]);
     }
@@ -317,6 +320,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t stage_addr = sbase + L::kOffStage + static_cast<uint32_t>(warp - 2) * L::kStageBufBytes;
         uint8_t* stage_ptr = smem + L::kOffStage + (warp - 2) * L::kStageBufBytes;
         const bool has_resid = p.resid_mode != kResidNone && p.resid_mode != kMaskRows;
+        // fp32 out with a residual: each 32 x 32 residual block comes in by TMA
+        // (through tmap_r) into the warp's staging buffer, and the result
+        // leaves from the same buffer, so every global access is a full-line
+        // bulk copy (a lane per row reading its own 128 bytes touched 32 lines
+        // per load instruction)
+        const bool resid_tma = !OUT_F16 && has_resid;
+        const uint32_t rbar = bar0 + 8u * (GemmBars<STAGES>::kCount + 3 + (warp - 2));
+        uint32_t r_issued = 0, r_waited = 0;
         int acc = 0;
         uint32_t acc_phase = 0;
         uint32_t nstore = 0;                              // chunks this warp has staged
@@ -344,8 +355,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 omap = &po.map[owner];
                 orow -= owner * po.rows;
             }
+            auto issue_resid = [&](int nc) {
+                __syncwarp();
+                if (lane == 0) {
+                    bulk_wait_read<0>();              // the last store has read the buffer
+                    fence_proxy_async_smem();
+                    mbar_arrive_expect_tx(rbar, 4096);
+                    tma_load_2d(stage_addr, &tmap_r, rbar, nc, m_blk * kGemmBM + quarter * 32);
+                }
+                ++r_issued;
+            };
             auto load_resid = [&](int nc) {
-                if (has_resid && row_ok && nc + kCW <= p.N) {
+                if (!resid_tma && has_resid && row_ok && nc + kCW <= p.N) {
                     const float4* rp = reinterpret_cast<const float4*>(p.resid + static_cast<int64_t>(row) * p.ldr + nc);
 #pragma unroll
                     for (int j = 0; j < kCW / 4; ++j) rr[j] = rp[j];
@@ -356,6 +377,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int c_hi = SPLIT2 ? c_lo + BN / 2 : BN;
             const int c_first = c_lo + half * kCW;
             float b_cur = load_bias(n0 + c_first);
+            if (resid_tma && n0 + c_first < p.N) issue_resid(n0 + c_first);
             load_resid(n0 + c_first);
             bool ok = mbar_wait(bars.accf(acc), acc_phase, abort_flag);
             ok = __all_sync(0xffffffffu, ok);
@@ -394,10 +416,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 ok2 = mbar_wait_cluster(recv_full, 0, abort_flag);
                 if (!__all_sync(0xffffffffu, ok2)) break;
             }
+            bool tile_aborted = false;
 #pragma unroll 1
             for (int c = c_first; c < c_hi; c += 2 * kCW) {
                 const int nc = n0 + c;
-                if (c != c_first) load_resid(nc);
+                if (c != c_first) {
+                    if (resid_tma && nc < p.N) issue_resid(nc);
+                    load_resid(nc);
+                }
                 const float b_next = c + 2 * kCW < c_hi ? load_bias(nc + 2 * kCW) : 0.0f;
                 float v[kCW];
                 {
@@ -430,7 +456,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
                         for (int j = 0; j < kCW; ++j) v[j] = 0.0f;
                     }
-                    if (has_resid && row_ok) {
+                    if (resid_tma) {
+                        // the block's wait is warp-wide (rows past M included)
+                        const bool okr = mbar_wait(rbar, r_waited & 1u, abort_flag);
+                        if (!__all_sync(0xffffffffu, okr)) {
+                            tile_aborted = true;
+                            break;
+                        }
+                        ++r_waited;
+                        const bool keep_sub = valid || p.resid_mode == kResidAdd;
+                        const bool keep_all = valid || p.resid_mode != kResidAddMaskAll;
+                        const uint8_t* rrow = stage_ptr + lane * 128;
+#pragma unroll
+                        for (int j = 0; j < kCW; j += 4) {
+                            const float4 rq = *reinterpret_cast<const float4*>(rrow + (((j >> 2) ^ (lane & 7)) << 4));
+                            v[j] = keep_all ? rq.x + (keep_sub ? v[j] : 0.0f) : 0.0f;
+                            v[j + 1] = keep_all ? rq.y + (keep_sub ? v[j + 1] : 0.0f) : 0.0f;
+                            v[j + 2] = keep_all ? rq.z + (keep_sub ? v[j + 2] : 0.0f) : 0.0f;
+                            v[j + 3] = keep_all ? rq.w + (keep_sub ? v[j + 3] : 0.0f) : 0.0f;
+                        }
+                    } else if (has_resid && row_ok) {
                         const bool keep_sub = valid || p.resid_mode == kResidAdd;
                         const bool keep_all = valid || p.resid_mode != kResidAddMaskAll;
                         if (full) {
@@ -494,6 +539,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
                 b_cur = b_next;
             }
+            if (tile_aborted) break;
             tc_fence_before();
             mbar_arrive(bars.acce(acc));
             if (++acc == 2) {
@@ -501,6 +547,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 acc_phase ^= 1u;
             }
         }
+        // a residual block still in flight after an abort lands before exit
+        if (lane == 0 && r_issued != r_waited) mbar_wait_drain(rbar, r_waited & 1u);
         if (lane == 0) bulk_wait_all();
     }
 
