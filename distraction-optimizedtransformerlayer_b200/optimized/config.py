@@ -87,6 +87,12 @@ CUDA_GRAPH = "auto"
 # faster eager (679 vs 778, 1005 vs 1208, 1821 vs 1953 us). Replay is
 # bit-identical to eager.
 _GRAPH_MAX_ACTIVATION = 1 << 22
+# ... and at most this much GEMM work per forward: an 8-way shard of config 5
+# (2 rows, 4 M elements, 206 GFLOP) ran 249 us eager against 260 us replayed
+# (the replay's copies of x and the output cost more than the launches, which
+# the GPU time covers), while a 2,048-token shard of config 3 (52 GFLOP) ran
+# 151 us replayed against 157 eager; config 2 (13 GFLOP) 77 against 194.
+_GRAPH_MAX_GEMM_FLOPS = 150e9
 # graphs kept per model (one per input shape / mask mode)
 _GRAPH_MAX_ENTRIES = 4
 # no capture when less than this much device memory is free

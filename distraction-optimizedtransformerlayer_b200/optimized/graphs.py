@@ -96,8 +96,9 @@ def _graph_key(x: torch.Tensor, use_mask: bool) -> Tuple:
             config.ATTENTION_PRECISION, config.GEMM_PRECISION)
 
 
-def _graph_eligible(x: torch.Tensor, entries: int) -> bool:
-    """Cheap per-call gate; pure Python, no GPU calls."""
+def _graph_eligible(x: torch.Tensor, entries: int, gemm_flops: float = 0.0) -> bool:
+    """Cheap per-call gate; pure Python, no GPU calls. gemm_flops: the
+    forward's GEMM work, for the size gate."""
     if config.CUDA_GRAPH == "off":
         return False
     if x.device.type != "cuda" or x.dim() != 3:
@@ -108,7 +109,8 @@ def _graph_eligible(x: torch.Tensor, entries: int) -> bool:
         return False
     if config.CUDA_GRAPH == "always":
         return True
-    return x.shape[0] * x.shape[1] * x.shape[2] <= config._GRAPH_MAX_ACTIVATION
+    return (x.shape[0] * x.shape[1] * x.shape[2] <= config._GRAPH_MAX_ACTIVATION
+            and gemm_flops <= config._GRAPH_MAX_GEMM_FLOPS)
 
 
 def _weights_fingerprint(model) -> Tuple:

@@ -84,7 +84,7 @@ class OptimizedTransformer(nn.Module):
         runner = self._graphs.get(key, lambda: _weights_fingerprint(self))
         if runner is not None:
             return runner.replay(x, valid_token_mask, out)
-        if key not in self._graphs.declined and _graph_eligible(x, len(self._graphs)):
+        if key not in self._graphs.declined and _graph_eligible(x, len(self._graphs), self._gemm_flops(x)):
             runner, y = _capture_graph(self, x, valid_token_mask, use_mask)
             if runner is None:
                 self._graphs.declined.add(key)
@@ -107,6 +107,13 @@ class OptimizedTransformer(nn.Module):
         if out.shape != x.shape or out.dtype != x.dtype or out.device != x.device:
             raise ValueError("out must match x in shape, dtype and device")
         return self.forward(x, valid_token_mask, out=out)
+
+    def _gemm_flops(self, x: torch.Tensor) -> float:
+        """GEMM FLOPs of one forward over x: 2 T (4 d^2 + 2 d F) per layer."""
+        if x.dim() != 3:
+            return 0.0
+        T, d = x.shape[0] * x.shape[1], x.shape[2]
+        return float(sum(2 * T * (4 * d * d + 2 * d * layer.ffn_in.weight.shape[0]) for layer in self.layers))
 
     # ------------------------------------------------------------ memory --
 
