@@ -161,22 +161,24 @@ int encode_f16_map(CUtensorMap* map, const void* base, int rank, const cuuint64_
 
 // ------------------------------------------------------------------ GEMM --
 
-template <int BN, int STAGES, bool OUT_F16, bool SPLIT2 = false, bool PEER = false>
+template <int BN, int STAGES, bool OUT_F16, bool SPLIT2 = false, bool PEER = false, bool PAIR = false>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const CUtensorMap& tr,
                 const dotl::GemmParams& p, int dev, cudaStream_t stream, const dotl::GemmPeerOut* po_in = nullptr) {
-    using L = dotl::GemmSmem<BN, STAGES>;
-    auto kernel = dotl::gemm_tc_kernel<BN, STAGES, OUT_F16, SPLIT2, PEER>;
+    using L = dotl::GemmSmem<BN, STAGES, PAIR ? BN / 2 : BN>;
+    auto kernel = dotl::gemm_tc_kernel<BN, STAGES, OUT_F16, SPLIT2, PEER, PAIR>;
     static const dotl::GemmPeerOut kNoPeers = {};
     const dotl::GemmPeerOut& po = po_in != nullptr ? *po_in : kNoPeers;
     static DeviceFlags done;
     if (int rc = ensure_smem(kernel, L::kAlloc, dev, done)) return rc;
     const int tiles = p.num_m_tiles * p.num_n_tiles;
     cudaError_t e;
-    if constexpr (SPLIT2) {
-        // one cluster of two CTAs per tile (the exchange buffer reuses the
-        // stage ring, so no CTA may own a second tile)
+    if constexpr (SPLIT2 || PAIR) {
+        // split-K: one cluster of two CTAs per tile (the exchange buffer reuses
+        // the stage ring, so no CTA may own a second tile); pair: persistent
+        // clusters of two, at most one CTA per SM
+        const int pairs = PAIR ? (tiles < sm_count(dev) / 2 ? tiles : sm_count(dev) / 2) : tiles;
         cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(static_cast<unsigned>(2 * tiles));
+        cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
         cfg.blockDim = dim3(dotl::kGemmThreads);
         cfg.dynamicSmemBytes = L::kAlloc;
         cfg.stream = stream;
@@ -527,8 +529,12 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
     const int64_t nkb = (x3 ? 3 : 1) * ((K + dotl::kGemmBK - 1) / dotl::kGemmBK);
     const int64_t mt = (M + dotl::kGemmBM - 1) / dotl::kGemmBM;
     int bn = tile_n;
-    bool split2 = false;
-    if (bn == 0) {
+    bool split2 = false, pair = false;
+    if (bn == -256) {
+        // CTA pairs on 256 x 256 tiles (M = 256 MMAs over two SMs)
+        bn = 256;
+        pair = true;
+    } else if (bn == 0) {
         bn = pick_tile_n(M, N, K, sm_count(dev));
         // Too few tiles for the SMs even at width 64, and a long K: split K
         // between the two CTAs of a cluster at width 128 instead (each CTA
@@ -544,7 +550,7 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
         split2 = true;
     }
     if (bn != 64 && bn != 128 && bn != 256)
-        return fail(DOTL_EINVAL, "%s: tile_n must be 0, 64, 128, 256 or -128 (split K)", who);
+        return fail(DOTL_EINVAL, "%s: tile_n must be 0, 64, 128, 256, -128 (split K) or -256 (CTA pairs)", who);
 
     // DOTL_F16X2 operands: one map over both planes of each (lo rows below hi)
     CUtensorMap ta, tw;
@@ -553,7 +559,8 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
     if (int rc = encode_f16_map(&ta, a, 2, adims, astr, dotl::kGemmBK, dotl::kGemmBM, who)) return rc;
     const cuuint64_t wdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(x3 ? 2 * N : N)};
     const cuuint64_t wstr[1] = {static_cast<cuuint64_t>(ldw) * 2};
-    if (int rc = encode_f16_map(&tw, w, 2, wdims, wstr, dotl::kGemmBK, static_cast<uint32_t>(bn), who)) return rc;
+    if (int rc = encode_f16_map(&tw, w, 2, wdims, wstr, dotl::kGemmBK, static_cast<uint32_t>(pair ? bn / 2 : bn), who))
+        return rc;
     CUtensorMap to;
     const int store_dtype = out_dtype == DOTL_F16X2 ? DOTL_F16 : out_dtype;
     if (int rc = encode_out_map(&to, out, M, N, ldo, store_dtype, who)) return rc;
@@ -571,7 +578,7 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
     p.M = static_cast<int>(M);
     p.N = static_cast<int>(N);
     p.K = static_cast<int>(K);
-    p.num_m_tiles = static_cast<int>((M + dotl::kGemmBM - 1) / dotl::kGemmBM);
+    p.num_m_tiles = static_cast<int>((M + (pair ? 2 : 1) * dotl::kGemmBM - 1) / ((pair ? 2 : 1) * dotl::kGemmBM));
     p.num_n_tiles = static_cast<int>((N + bn - 1) / bn);
     p.bias = bias;
     p.resid = resid;
@@ -588,6 +595,9 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const bool f16 = store_dtype == DOTL_F16;
     const dotl::GemmPeerOut* po = &lo_out;
+    if (pair)
+        return f16 ? launch_gemm<256, 6, true, false, false, true>(ta, tw, to, tr, p, dev, s, po)
+                   : launch_gemm<256, 6, false, false, false, true>(ta, tw, to, tr, p, dev, s, po);
     if (split2)
         return f16 ? launch_gemm<128, 5, true, true>(ta, tw, to, tr, p, dev, s, po)
                    : launch_gemm<128, 5, false, true>(ta, tw, to, tr, p, dev, s, po);

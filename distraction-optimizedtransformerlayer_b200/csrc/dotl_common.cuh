@@ -274,6 +274,54 @@ __device__ __forceinline__ void tc_commit(uint32_t bar) {
                  : "memory");
 }
 
+// ------------------------------------------------ CTA pairs (cta_group::2) --
+// Two CTAs of a cluster run one M=256 MMA: each holds 128 rows of A, half of
+// B's rows and 128 rows of the accumulator in its own TMEM. The leader (rank
+// 0) issues the MMAs and commits; every CTA loads its own operand halves.
+
+// TMEM allocation for the pair (one warp of each CTA, the same warp index and
+// the same destination offset in both).
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t slot_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot_smem), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// A tile into this CTA's shared memory whose completion (bytes) is counted on
+// the mbarrier at shared::cluster address `bar_cluster` (the leader's).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar_cluster, int c0,
+                                                 int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar_cluster)
+        : "memory");
+}
+
+// D[tmem of both CTAs] (+)= A[smem of both] * B[smem of both], M = 256, issued
+// by the leader alone.
+__device__ __forceinline__ void mma_f16_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrives once on the mbarrier at shared::cluster address `bar` (this CTA's
+// or the peer's) when the pair MMAs this thread issued so far have completed.
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
 // D[tmem] (+)= A[smem] * B[smem], fp16 inputs, fp32 accumulate. One thread issues.
 __device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                            uint32_t idesc, uint32_t accumulate) {

@@ -87,9 +87,11 @@ struct GemmPeerOut {
     int rows;                // rows per rank; 0: the ordinary output map
 };
 
-template <int BN, int STAGES>
+// BROWS: the W rows a CTA stages per k-block (BN, or BN / 2 for a CTA pair,
+// which splits the tile's W rows between its two CTAs).
+template <int BN, int STAGES, int BROWS = BN>
 struct GemmSmem {
-    static constexpr uint32_t kBTileBytes = BN * kGemmBK * 2;
+    static constexpr uint32_t kBTileBytes = BROWS * kGemmBK * 2;
     static constexpr uint32_t kStageBytes = kGemmATileBytes + kBTileBytes;
     static constexpr uint32_t kOffA = 0;
     static constexpr uint32_t kOffB = STAGES * kGemmATileBytes;
@@ -227,6 +229,102 @@ mma_done:
     mbar_wait_drain(bars.drain(), 0);
 }
 
+// CTA-pair producer (PAIR, one thread in each CTA): per k-block this CTA's
+// 128 rows of the pair's 256-row A block and its half of the tile's W rows,
+// both counted on the leader's full barrier, which the leader arms for the
+// pair's bytes. The stage is free again when the leader's MMA commit arrives
+// on this CTA's empty barrier.
+template <int BN, int STAGES>
+__device__ __forceinline__ void gemm_produce_pair(const CUtensorMap* tmap_a, const CUtensorMap* tmap_w,
+                                                  uint32_t sbase, GemmBars<STAGES> bars, volatile int* abort_flag,
+                                                  const TileSched& ts, int nkb, X3Pass x3, uint32_t rank) {
+    using L = GemmSmem<BN, STAGES, BN / 2>;
+    int stage = 0;
+    uint32_t phase = 0;
+    int issued_phase[STAGES];
+    for (int s = 0; s < STAGES; ++s) issued_phase[s] = -1;
+    for (int t = ts.first; t < ts.count; t += ts.stride) {
+        int m_blk, n_blk;
+        ts.decode(t, m_blk, n_blk);
+        for (int kb = 0; kb < nkb; ++kb) {
+            if (!mbar_wait(bars.empty(stage), phase ^ 1u, abort_flag)) goto pair_producer_done;
+            if (rank == 0) mbar_arrive_expect_tx(bars.full(stage), 2 * L::kStageBytes);
+            int ka = kb;
+            int arow = m_blk * 2 * kGemmBM + static_cast<int>(rank) * kGemmBM;
+            int wrow = n_blk * BN + static_cast<int>(rank) * (BN / 2);
+            if (x3.nkb > 0) {
+                const int pass = kb / x3.nkb;
+                ka = kb - pass * x3.nkb;
+                if (pass == 1) arow += x3.a_lo;
+                if (pass == 2) wrow += x3.w_lo;
+            }
+            const uint32_t fbar = mapa_shared(bars.full(stage), 0);
+            tma_load_2d_pair(sbase + L::kOffA + stage * kGemmATileBytes, tmap_a, fbar, ka * kGemmBK, arow);
+            tma_load_2d_pair(sbase + L::kOffB + stage * L::kBTileBytes, tmap_w, fbar, ka * kGemmBK, wrow);
+            issued_phase[stage] = static_cast<int>(phase);
+            if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1u;
+            }
+        }
+    }
+pair_producer_done:
+    if (*abort_flag && rank == 0) {
+        // the leader's full barriers count both CTAs' copies: wait them out
+        for (int s = 0; s < STAGES; ++s)
+            if (issued_phase[s] >= 0) mbar_wait_drain(bars.full(s), static_cast<uint32_t>(issued_phase[s]));
+    }
+}
+
+// CTA-pair MMA issuer (the leader's one thread): M = 256 MMAs over both CTAs'
+// operands into both CTAs' TMEM; each commit arrives on the barrier in both
+// CTAs (one commit per CTA, no fan-out form). The accumulator is free again
+// once all 16 epilogue warps of the pair have arrived on the leader's acce.
+template <int BN, int STAGES>
+__device__ __forceinline__ void gemm_mma_pair(uint32_t sbase, uint32_t tmem_base, GemmBars<STAGES> bars,
+                                              volatile int* abort_flag, const TileSched& ts, int nkb) {
+    using L = GemmSmem<BN, STAGES, BN / 2>;
+    constexpr uint32_t idesc = idesc_f16_f32(2 * kGemmBM, BN, false, false);
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = ts.first; t < ts.count; t += ts.stride) {
+        if (!mbar_wait_cluster(bars.acce(acc), acc_phase ^ 1u, abort_flag)) goto pair_mma_done;
+        tc_fence_after();
+        {
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+            for (int kb = 0; kb < nkb; ++kb) {
+                if (!mbar_wait(bars.full(stage), phase, abort_flag)) goto pair_mma_done;
+                tc_fence_after();
+                const uint32_t a_addr = sbase + L::kOffA + stage * kGemmATileBytes;
+                const uint32_t b_addr = sbase + L::kOffB + stage * L::kBTileBytes;
+#pragma unroll
+                for (int kk = 0; kk < kGemmBK / 16; ++kk) {
+                    const uint64_t ad = smem_desc(a_addr + kk * 32, 16, 1024, kSwizzle128);
+                    const uint64_t bd = smem_desc(b_addr + kk * 32, 16, 1024, kSwizzle128);
+                    mma_f16_ss_pair(d_tmem, ad, bd, idesc, (kb != 0 || kk != 0) ? 1u : 0u);
+                }
+                tc_commit_pair(mapa_shared(bars.empty(stage), 0));
+                tc_commit_pair(mapa_shared(bars.empty(stage), 1));
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+        }
+        tc_commit_pair(mapa_shared(bars.accf(acc), 0));
+        tc_commit_pair(mapa_shared(bars.accf(acc), 1));
+        if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1u;
+        }
+    }
+pair_mma_done:
+    tc_commit_pair(mapa_shared(bars.drain(), 0));
+    mbar_wait_drain(bars.drain(), 0);
+}
+
 // SPLIT2: a cluster of two CTAs shares each output tile, CTA r running
 // k-blocks [r nkb/2, (r+1) nkb/2). After the main loop each sends the other's
 // column half of its partial accumulator into the other's shared memory (the
@@ -234,12 +332,19 @@ mma_done:
 // own half as partial_0 + partial_1 (one fp32 add, which commutes: both CTAs
 // and every run give the same bits). Used when a problem has too few tiles
 // to fill the SMs with long K.
-template <int BN, int STAGES, bool OUT_F16, bool SPLIT2 = false, bool PEER = false>
+//
+// PAIR: a cluster of two CTAs computes each 256 x BN output tile with M = 256
+// MMAs (tcgen05 cta_group::2): CTA r stages rows [128 r, 128 r + 128) of the
+// tile's A block and W rows [r BN/2, (r+1) BN/2) of its N block, so per MMA each
+// SM's shared memory feeds half the W operand it would alone; CTA r's TMEM
+// holds output rows [128 r, 128 r + 128), drained by its own epilogue.
+template <int BN, int STAGES, bool OUT_F16, bool SPLIT2 = false, bool PEER = false, bool PAIR = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
                    const __grid_constant__ CUtensorMap tmap_out, const __grid_constant__ CUtensorMap tmap_r,
                    const GemmParams p, const __grid_constant__ GemmPeerOut po) {
-    using L = GemmSmem<BN, STAGES>;
+    static_assert(!(PAIR && (SPLIT2 || PEER)), "a CTA pair is neither split-K nor peer-scattered");
+    using L = GemmSmem<BN, STAGES, PAIR ? BN / 2 : BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -254,7 +359,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const uint32_t rank = SPLIT2 ? cluster_ctarank() : 0u;
+    const uint32_t rank = (SPLIT2 || PAIR) ? cluster_ctarank() : 0u;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -263,7 +368,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(bars.accf(b), 1);
-            mbar_init(bars.acce(b), 256);
+            mbar_init(bars.acce(b), PAIR ? 16 : 256);   // pair: one arrival per epilogue warp of both CTAs
         }
         mbar_init(bars.drain(), 1);
         mbar_init(peer_ready, 256);
@@ -279,15 +384,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if constexpr (PEER)
             for (int r = 0; r * po.rows < p.M && r < kGemmPeerMax; ++r) tma_prefetch_map(&po.map[r]);
     }
-    if constexpr (SPLIT2) cluster_sync_after_init();
+    if constexpr (SPLIT2 || PAIR) cluster_sync_after_init();
     pdl_wait();
     pdl_launch_dependents();
     if (warp == 1) {
-        tmem_alloc(smem_u32(tmem_slot), L::kTmemCols);
-        tmem_relinquish();
+        if constexpr (PAIR) {
+            tmem_alloc_pair(smem_u32(tmem_slot), L::kTmemCols);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(smem_u32(tmem_slot), L::kTmemCols);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
-    __syncthreads();
+    if constexpr (PAIR) {
+        cluster_sync_after_init();   // both CTAs' TMEM exists before the leader's first MMA
+    } else {
+        __syncthreads();
+    }
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
@@ -295,15 +409,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int num_kb = p.x3_nkb > 0 ? 3 * p.x3_nkb : (p.K + kGemmBK - 1) / kGemmBK;
     const X3Pass x3{p.x3_nkb, p.a_lo_row, p.w_lo_row};
 
-    const int cta_unit = SPLIT2 ? static_cast<int>(blockIdx.x) / 2 : static_cast<int>(blockIdx.x);
-    const int units = SPLIT2 ? static_cast<int>(gridDim.x) / 2 : static_cast<int>(gridDim.x);
+    const int cta_unit = (SPLIT2 || PAIR) ? static_cast<int>(blockIdx.x) / 2 : static_cast<int>(blockIdx.x);
+    const int units = (SPLIT2 || PAIR) ? static_cast<int>(gridDim.x) / 2 : static_cast<int>(gridDim.x);
     const TileSched ts{cta_unit, units, num_tiles, p.num_n_tiles, -1};
     const int kb0 = SPLIT2 ? static_cast<int>(rank) * (num_kb / 2) : 0;
     const int kb1 = SPLIT2 ? (rank == 0 ? num_kb / 2 : num_kb) : num_kb;
     if (warp == 0 && lane == 0) {
-        gemm_produce<BN, STAGES>(&tmap_a, &tmap_w, sbase, bars, abort_flag, ts, kb0, kb1, x3);
+        if constexpr (PAIR) gemm_produce_pair<BN, STAGES>(&tmap_a, &tmap_w, sbase, bars, abort_flag, ts, num_kb, x3, rank);
+        else gemm_produce<BN, STAGES>(&tmap_a, &tmap_w, sbase, bars, abort_flag, ts, kb0, kb1, x3);
     } else if (warp == 1 && lane == 0) {
-        gemm_mma<BN, STAGES>(sbase, tmem_base, bars, abort_flag, ts, kb0, kb1);
+        if constexpr (PAIR) {
+            if (rank == 0) gemm_mma_pair<BN, STAGES>(sbase, tmem_base, bars, abort_flag, ts, num_kb);
+        } else {
+            gemm_mma<BN, STAGES>(sbase, tmem_base, bars, abort_flag, ts, kb0, kb1);
+        }
     } else if (warp >= 2) {
         // -------------------------------------------------------- epilogue --
         // Eight warps, two per TMEM lane quarter (the 32 rows a warp may
@@ -334,7 +453,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int t = ts.first; t < ts.count; t += ts.stride) {
             int m_blk, n_blk;
             ts.decode(t, m_blk, n_blk);
-            const int row = m_blk * kGemmBM + row_in_tile;
+            // first output row of this CTA's accumulator rows
+            const int row0 = PAIR ? m_blk * 2 * kGemmBM + static_cast<int>(rank) * kGemmBM : m_blk * kGemmBM;
+            const int row = row0 + row_in_tile;
             const int n0 = n_blk * BN;
             const bool row_ok = row < p.M;
             const bool valid = (p.row_valid == nullptr) || !row_ok || (p.row_valid[row] != 0);
@@ -349,7 +470,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             };
             // where this tile's rows go: the output map, or the owning rank's
             const CUtensorMap* omap = &tmap_out;
-            int orow = m_blk * kGemmBM;
+            int orow = row0;
             if constexpr (PEER) {
                 const int owner = orow / po.rows;
                 omap = &po.map[owner];
@@ -361,7 +482,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     bulk_wait_read<0>();              // the last store has read the buffer
                     fence_proxy_async_smem();
                     mbar_arrive_expect_tx(rbar, 4096);
-                    tma_load_2d(stage_addr, &tmap_r, rbar, nc, m_blk * kGemmBM + quarter * 32);
+                    tma_load_2d(stage_addr, &tmap_r, rbar, nc, row0 + quarter * 32);
                 }
                 ++r_issued;
             };
@@ -541,7 +662,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             if (tile_aborted) break;
             tc_fence_before();
-            mbar_arrive(bars.acce(acc));
+            if constexpr (PAIR) {
+                // the leader's MMA may refill this CTA's TMEM rows
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(mapa_shared(bars.acce(acc), 0));
+            } else {
+                mbar_arrive(bars.acce(acc));
+            }
             if (++acc == 2) {
                 acc = 0;
                 acc_phase ^= 1u;
@@ -556,7 +683,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncwarp();
     tc_fence_before();
     __syncthreads();
-    if constexpr (SPLIT2) {
+    if constexpr (SPLIT2 || PAIR) {
         // neither CTA of the pair exits while the other may still write into it
         if (threadIdx.x == 0) {
             mbar_arrive_cluster(mapa_shared(exit_bar, 0));
@@ -567,7 +694,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, L::kTmemCols);
+        if constexpr (PAIR) tmem_dealloc_pair(tmem_base, L::kTmemCols);
+        else tmem_dealloc(tmem_base, L::kTmemCols);
     }
 }
 

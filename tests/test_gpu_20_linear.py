@@ -169,3 +169,31 @@ def test_split_k_is_auto_for_long_k_few_tiles(kernels):
     (128 tiles of width 64 and 32 k-blocks): auto and forced give the same bits."""
     a, w, b = _operands(2048, 512, 2048, 77)
     assert torch.equal(kernels.linear_fp16(a, w, b), kernels.linear_fp16(a, w, b, tile_n=-128))
+
+
+@pytest.mark.parametrize("M,N,K,mode,act,half_out", [
+    (256, 256, 64, 0, 0, False), (512, 1024, 512, 1, 0, False), (300, 512, 256, 3, 0, False),
+    (1000, 768, 1024, 0, 1, True), (2048, 2048, 2048, 2, 0, False), (129, 256, 72, 0, 0, True),
+    (4096, 6144, 512, 0, 0, True)])
+def test_cta_pair_tiles(kernels, M, N, K, mode, act, half_out):
+    """tile_n=-256: two CTAs of a cluster run each 256 x 256 tile with M = 256
+    MMAs, each staging half of W; every epilogue against float64."""
+    a, w, b = _operands(M, N, K, 40 + M)
+    g = torch.Generator(device="cuda").manual_seed(41)
+    resid = torch.randn(M, N, device="cuda", generator=g) if mode else None
+    valid = (torch.rand(M, device="cuda", generator=g) > 0.3) if mode >= 2 else None
+    out = kernels.linear_fp16(a, w, b, act=act, resid=resid, row_valid=valid, resid_mode=mode,
+                              out_half=half_out, tile_n=-256)
+    one = kernels.linear_fp16(a, w, b, act=act, resid=resid, row_valid=valid, resid_mode=mode,
+                              out_half=half_out, tile_n=256)
+    y = _ref(a, w, b, act=bool(act))
+    if mode == 1:
+        y = resid.double() + y
+    elif mode == 2:
+        y = resid.double() + torch.where(valid[:, None], y, torch.zeros_like(y))
+    elif mode == 3:
+        y = torch.where(valid[:, None], resid.double() + y, torch.zeros_like(y))
+    scale = _scale(a, w) + (resid.double().abs() if resid is not None else 0)
+    tol = 2 ** -10 if half_out else 1e-5
+    assert ((out.double() - y).abs() / (scale if not half_out else y.abs() + 1e-2)).max().item() < tol
+    assert ((out.double() - one.double()).abs() / scale).max().item() < 1e-5
