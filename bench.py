@@ -765,7 +765,8 @@ def run_tp(args, rank, world, dev, dist, kernels):
     full = OptimizedTransformer(cfg)
     _init_model(full, SEED)
     state = {k: v.detach() for k, v in full.state_dict().items()}
-    model = TensorParallelTransformer(cfg, state, device=dev, fused=args.tp_impl == "fused",
+    model = TensorParallelTransformer(cfg, state, device=dev,
+                                      fused=None if args.tp_impl == "auto" else args.tp_impl == "fused",
                                       push=not args.tp_oneshot,
                                       scatter=False if args.tp_no_scatter else None, error_check="deferred")
     x_cpu, mask_cpu = _synthetic_case(cfg, SEED, cfg.batch_size)
@@ -901,8 +902,9 @@ def main() -> int:
     ap.add_argument("--tp", action="store_true",
                     help="tensor parallel across all ranks (heads and FFN columns sharded, two reductions "
                          "per layer); one global batch per step")
-    ap.add_argument("--tp-impl", choices=("fused", "nccl"), default="fused",
-                    help="--tp: each all-reduce + add + LayerNorm as one peer-memory kernel, or NCCL + LN")
+    ap.add_argument("--tp-impl", choices=("auto", "fused", "nccl"), default="auto",
+                    help="--tp: each all-reduce + add + LayerNorm as one peer-memory kernel, or NCCL + LN "
+                         "(auto: the model's default, fused at 2 ranks)")
     ap.add_argument("--tp-oneshot", action="store_true",
                     help="--tp fused: one-shot mode (every rank reduces every row)")
     ap.add_argument("--tp-no-scatter", action="store_true",
