@@ -357,31 +357,6 @@ int64_t attn_split_bytes(int streams, int q_tiles, int splits, int head_dim) {
     return static_cast<int64_t>(streams) * q_tiles * splits * dotl::kAttnTile * (head_dim * 4 + 8);
 }
 
-// ------------------------------------------------- fused all-reduce + LN --
-
-// Launches the all-reduce + LN kernel; in bulk mode with D * 4 bytes of shared
-// memory per warp, falling back to per-lane stores (p.bulk = 0) if that would
-// leave fewer than kPeerBlocksPerSm CTAs resident per SM (the grid must be
-// resident at once: its CTAs wait for one another across GPUs).
-template <typename Kernel>
-cudaError_t launch_allreduce_ln(Kernel kernel, dim3 grid, dim3 block, cudaStream_t s, dotl::PeerLnParams& p) {
-    size_t smem = 0;
-    if (p.bulk) {
-        smem = static_cast<size_t>(dotl::kPeerWarps) * p.D * 4;
-        int fit = 0;
-        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
-                cudaSuccess ||
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&fit, kernel, static_cast<int>(block.x), smem) !=
-                cudaSuccess ||
-            fit < dotl::kPeerBlocksPerSm) {
-            (void)cudaGetLastError();
-            p.bulk = 0;
-            smem = 0;
-        }
-    }
-    return launch_pdl(kernel, grid, block, smem, s, p);
-}
-
 // ------------------------------------------------------------- fused MLP --
 
 template <int D, bool NF16>
@@ -1265,16 +1240,12 @@ int dotl_allreduce_ln(int world, int rank, const float* const* parts, void* cons
     p.parts_local = parts_local ? 1 : 0;
     p.timeout_ns = static_cast<unsigned long long>(timeout_ms) * 1000000ull;
     p.status = status;
-    // push mode sends each finished row to the ranks as bulk copies out of a
-    // per-warp shared row (rows of 16-byte multiples), where every CTA of the
-    // grid still fits at once with that shared memory
-    p.bulk = (push && world > 1 && D % 8 == 0) ? 1 : 0;
     const dim3 grid(static_cast<unsigned>(blocks)), block(dotl::kPeerWarps * 32);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t le;
 #define DOTL_ARLN(EPL)                                                                                   \
-    le = normed_dtype == DOTL_F16 ? launch_allreduce_ln(dotl::allreduce_ln_kernel<EPL, __half>, grid, block, s, p) \
-                                  : launch_allreduce_ln(dotl::allreduce_ln_kernel<EPL, float>, grid, block, s, p)
+    le = normed_dtype == DOTL_F16 ? launch_pdl(dotl::allreduce_ln_kernel<EPL, __half>, grid, block, 0, s, p) \
+                                  : launch_pdl(dotl::allreduce_ln_kernel<EPL, float>, grid, block, 0, s, p)
     if (D <= 128) DOTL_ARLN(4);
     else if (D <= 256) DOTL_ARLN(8);
     else if (D <= 512) DOTL_ARLN(16);

@@ -232,13 +232,6 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t sr
                  "r"(c0), "r"(c1), "r"(src)
                  : "memory");
 }
-// Shared -> global bulk copy of `bytes` (a multiple of 16; both addresses
-// 16-byte aligned), completion tracked by bulk groups like tma_store_2d.
-__device__ __forceinline__ void bulk_store(void* gdst, uint32_t ssrc, uint32_t bytes) {
-    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(gdst)),
-                 "r"(ssrc), "r"(bytes)
-                 : "memory");
-}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // At most N committed bulk groups of this thread still reading shared memory.
 template <int N>

@@ -75,7 +75,6 @@ struct PeerLnParams {
     int parts_local;               // part[i]: rows [lo, hi) of rank i's partial sums, in this rank's memory
     unsigned long long timeout_ns;
     unsigned int* status;          // optional caller word (e.g. host-mapped) that a timeout also sets
-    int bulk;                      // push: rows leave through shared memory as bulk copies (D * 4 bytes per warp)
 };
 
 __device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
@@ -134,10 +133,6 @@ __global__ void __launch_bounds__(kPeerWarps * 32, kPeerBlocksPerSm) allreduce_l
 
     const int lane = threadIdx.x & 31;
     const int D = p.D;
-    // bulk mode: this warp's staging row (D fp32, reused for x_new then normed)
-    extern __shared__ __align__(128) uint8_t peer_stage[];
-    uint8_t* wstage = peer_stage + static_cast<size_t>(threadIdx.x >> 5) * D * 4;
-    const uint32_t wstage_s = smem_u32(wstage);
     int64_t lo = 0, hi = p.rows;
     if (p.push) {
         const int64_t chunk = (p.rows + p.world - 1) / p.world;
@@ -210,59 +205,6 @@ __global__ void __launch_bounds__(kPeerWarps * 32, kPeerBlocksPerSm) allreduce_l
         const bool keep = p.normed_row_valid == nullptr || p.normed_row_valid[row] != 0;
         const int d0 = p.push ? 0 : p.rank;
         const int d1 = p.push ? p.world : p.rank + 1;
-        if (p.bulk) {
-            // The row's x_new, then its normed values, staged in this warp's
-            // shared row and sent to every rank as one bulk copy each: whole
-            // rows over NVLink in place of 8- and 16-byte stores per lane.
-            if (lane == 0) bulk_wait_read<0>();   // the last copies have read the row
-            __syncwarp();
-            if (p.x_new[d0] != nullptr) {
-#pragma unroll
-                for (int i = 0; i < EPL / 4; ++i) {
-                    const int c = (i * 32 + lane) * 4;
-                    if (c < D)
-                        *reinterpret_cast<float4*>(wstage + c * 4) =
-                            make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-                }
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                    for (int dst = d0; dst < d1; ++dst) bulk_store(p.x_new[dst] + base, wstage_s, D * 4);
-                    bulk_commit();
-                    bulk_wait_read<0>();
-                }
-                __syncwarp();
-            }
-#pragma unroll
-            for (int i = 0; i < EPL / 4; ++i) {
-                const int c = (i * 32 + lane) * 4;
-                if (c >= D) continue;
-                const float4 ww = *reinterpret_cast<const float4*>(p.ln_w + c);
-                const float4 bb = *reinterpret_cast<const float4*>(p.ln_b + c);
-                float o0 = (v[4 * i] - mean) * rstd * ww.x + bb.x;
-                float o1 = (v[4 * i + 1] - mean) * rstd * ww.y + bb.y;
-                float o2 = (v[4 * i + 2] - mean) * rstd * ww.z + bb.z;
-                float o3 = (v[4 * i + 3] - mean) * rstd * ww.w + bb.w;
-                if (!keep) o0 = o1 = o2 = o3 = 0.0f;
-                if constexpr (sizeof(NormT) == 4) {
-                    *reinterpret_cast<float4*>(wstage + c * 4) = make_float4(o0, o1, o2, o3);
-                } else {
-                    uint2 h;
-                    h.x = pack_half2(o0, o1);
-                    h.y = pack_half2(o2, o3);
-                    *reinterpret_cast<uint2*>(wstage + c * 2) = h;
-                }
-            }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-                for (int dst = d0; dst < d1; ++dst)
-                    bulk_store(reinterpret_cast<NormT*>(p.normed[dst]) + base, wstage_s,
-                               static_cast<uint32_t>(D * sizeof(NormT)));
-                bulk_commit();
-            }
-            continue;
-        }
 #pragma unroll
         for (int i = 0; i < EPL / 4; ++i) {
             const int c = (i * 32 + lane) * 4;
@@ -292,12 +234,6 @@ __global__ void __launch_bounds__(kPeerWarps * 32, kPeerBlocksPerSm) allreduce_l
 
     // End barrier: this CTA's stores (remote ones included) are ordered before
     // its flag; afterwards every peer's CTA b has finished reading and writing.
-    if (p.bulk) {
-        // every bulk copy of this warp complete, its writes ordered before the
-        // generic-proxy release below
-        if (lane == 0) bulk_wait_all();
-        asm volatile("fence.proxy.async.global;" ::: "memory");
-    }
     __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) peer_handshake(p, G + static_cast<int64_t>(G) * kPeerMax, val);
