@@ -858,13 +858,53 @@ def run_tp(args, rank, world, dev, dist, kernels):
     return 0
 
 
+def _profile_allreduce_ln(args, kernels, dev):
+    """dotl_allreduce_ln as one rank of config C's tensor-parallel layer runs it
+    (push mode, fp16 normed rows), 3 times inside "dotl_profile", with the
+    --profile-ranks ranks stood in for by local buffers: rank P-1 reduces its
+    T/P rows from P fp32 partial sums, adds bias and residual, normalises, and
+    writes x_new and normed into all P ranks' buffers. The peers' flags are
+    preset far ahead, so no wait ever spins."""
+    B, S, d = CONFIGS[args.config][:3]
+    T, P = B * S, args.profile_ranks
+    rank = P - 1
+    g = torch.Generator(device=dev).manual_seed(SEED)
+    parts = [torch.randn(T, d, device=dev, generator=g) for _ in range(P)]
+    x = torch.randn(T, d, device=dev, generator=g)
+    bias, w, b = (torch.randn(d, device=dev, generator=g) * 0.1 for _ in range(3))
+    x_new = [torch.empty(T, d, device=dev) for _ in range(P)]
+    normed = [torch.empty(T, d, device=dev, dtype=torch.float16) for _ in range(P)]
+    blocks = kernels.peer_blocks()
+    words = kernels.peer_signal_bytes(blocks) // 4
+    sig = [torch.zeros(words, dtype=torch.int32, device=dev) for _ in range(P)]
+    sig[rank][blocks:] = 1 << 30
+    torch.cuda.synchronize(dev)
+    torch.cuda.nvtx.range_push("dotl_profile")
+    for _ in range(3):
+        kernels.allreduce_ln(P, rank, [t.data_ptr() for t in parts], [t.data_ptr() for t in sig],
+                             [t.data_ptr() for t in x_new], [t.data_ptr() for t in normed], True, True,
+                             x, bias, w, b, 1e-5, None, None, T, d, blocks, 2000)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize(dev)
+    if kernels.device_error(clear=True):
+        raise SystemExit("allreduce_ln profile: the device error word is set")
+    print(f"profiled allreduce_ln x3: rank {rank} of {P}, {T // P} of {T} rows, d_model {d}")
+    return 0
+
+
 def _profile_kernel(args, kernels, dev):
     """Runs one kernel of the layer 3 times inside the NVTX range
     "dotl_profile" (for ncu --nvtx --nvtx-include dotl_profile/), nothing else
-    timed."""
+    timed. --profile-shape B,S,d,H,F replaces the config's shape (causal)."""
     from optimized import OptimizedTransformer
 
+    if args.profile_kernel == "allreduce_ln":
+        return _profile_allreduce_ln(args, kernels, dev)
     cfg = _Cfg(args.config, args.layers)
+    if args.profile_shape:
+        B, S, d, H, F = (int(v) for v in args.profile_shape.split(","))
+        cfg.batch_size, cfg.seq_len, cfg.d_model, cfg.num_heads, cfg.ffn_dim = B, S, d, H, F
+        cfg.causal, cfg.padding_ratio = True, 0.0
     model = OptimizedTransformer(cfg)
     _init_model(model, SEED)
     model = model.to(dev).eval()
@@ -881,7 +921,9 @@ def _profile_kernel(args, kernels, dev):
             ops[args.profile_kernel]()
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize(dev)
-    print(f"profiled {args.profile_kernel} x3 on {_describe(args.config)}")
+    shape = (f"B={cfg.batch_size} S={cfg.seq_len} d_model={cfg.d_model} heads={cfg.num_heads} "
+             f"ffn={cfg.ffn_dim} causal" if args.profile_shape else _describe(args.config))
+    print(f"profiled {args.profile_kernel} x3 on {shape}")
     return 0
 
 
@@ -916,7 +958,12 @@ def main() -> int:
                     help="seconds of CPU reference forwards per config for cpu_baseline (N=1, rank 0)")
     ap.add_argument("--settle", type=float, default=1.0, help="seconds of untimed steps before timing")
     ap.add_argument("--profile-kernel", default=None,
-                    help="run only this kernel of the layer 3x in an NVTX range (for ncu)")
+                    help="run only this kernel of the layer 3x in an NVTX range (for ncu); "
+                         "'allreduce_ln' runs one rank's fused tensor-parallel reduction")
+    ap.add_argument("--profile-shape", default=None,
+                    help="B,S,d_model,heads,ffn: profile the kernel on this causal shape instead of the config")
+    ap.add_argument("--profile-ranks", type=int, default=8,
+                    help="ranks emulated by --profile-kernel allreduce_ln")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")

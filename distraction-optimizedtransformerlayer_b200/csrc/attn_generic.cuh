@@ -9,13 +9,15 @@
 // kinds 1 and 2, causal, fully masked query rows written as 0, output layouts
 // [B,H,S,hd] and [B,S,H*hd].
 //
-// One warp per query row, the head dims spread over the lanes (hd <= 32 HPL),
+// Head dims 40 to 256: one warp per query row, the head dims spread over the
+// lanes (hd <= 32 HPL),
 // fp32 scores through an online softmax (running max, running sum, rescaled
 // accumulator; P rounded to fp16 before it multiplies V, as the tensor-core
 // kernels do), fp16 output. The block's 16 query rows share every key/value
 // tile, staged in shared memory (32 keys at a time, rows zero-padded to
-// 32 HPL) with 16-byte loads. Not a tensor-core kernel: these shapes are small
-// (the largest, dashboard shape 8, is 1 GFLOP per layer).
+// 32 HPL) with 16-byte loads. Head dims 8, 16 and 24 run attn_rows_kernel
+// below, a thread per query row. Not tensor-core kernels: these shapes are
+// small (the largest, dashboard shape 8, is 1 GFLOP per layer).
 
 #pragma once
 
@@ -120,6 +122,143 @@ __global__ void __launch_bounds__(kGenRows * 32) attn_generic_kernel(const AttnG
             p.out[base + d] = hi;
             if (p.out_lo != 0) p.out[p.out_lo + base + d] = __float2half_rn(y - __half2float(hi));
         }
+    }
+}
+
+// Head dims 8, 16 and 24: one THREAD per query row (q and the output row in
+// registers), 128 rows of one (batch, head) stream per block. The 32-key K/V
+// tiles are staged in shared memory as fp32 and read as broadcasts (every
+// thread of the block reads the same key). Per tile a row takes its 32
+// scores, their max, one rescale of its running output and sum, and then
+// P = exp2(s c - m c) per key: exponentials in the exp2 domain as in
+// attn_tc_kernel, P rounded to fp16 before it multiplies V, the row sum over
+// the unrounded P. One warp per row (attn_generic_kernel) would spend 32
+// lanes on 8-24 products and repeat each exponential 32 times.
+constexpr int kRowsBlock = 128;   // query rows (threads) per block
+constexpr int kRowsKeys = 32;     // keys per staged tile
+
+template <int HD>
+__global__ void __launch_bounds__(kRowsBlock) attn_rows_kernel(const AttnGenericParams p) {
+    static_assert(HD % 8 == 0 && HD <= 24, "attn_rows_kernel: head dims 8, 16, 24");
+    __shared__ __align__(16) float k_s[kRowsKeys][HD];
+    __shared__ __align__(16) float v_s[kRowsKeys][HD];
+    __shared__ uint8_t key_ok[kRowsKeys];
+    pdl_wait();
+    pdl_launch_dependents();
+    const int b = blockIdx.y / p.H;
+    const int h = blockIdx.y - b * p.H;
+    const int qi = blockIdx.x * kRowsBlock + threadIdx.x;
+    const bool q_ok = qi < p.S;
+    const float c = p.scale * 1.4426950408889634f;   // scores into the exp2 domain
+
+    float q[HD], o[HD];
+    {
+        const __half* qrow = p.q + b * p.qs[0] + h * p.qs[1] + static_cast<int64_t>(q_ok ? qi : 0) * p.qs[2];
+#pragma unroll
+        for (int d = 0; d < HD; d += 8) {
+            uint4 raw = q_ok ? *reinterpret_cast<const uint4*>(qrow + d) : make_uint4(0u, 0u, 0u, 0u);
+            const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 f = __half22float2(h2[i]);
+                q[d + 2 * i] = f.x;
+                q[d + 2 * i + 1] = f.y;
+            }
+        }
+#pragma unroll
+        for (int d = 0; d < HD; ++d) o[d] = 0.0f;
+    }
+    float m = -INFINITY, l = 0.0f;   // m in the exp2 domain (max of s c)
+    // under the causal rule no row of this block sees keys past its last row
+    const int k_end = p.causal ? min(p.S, blockIdx.x * kRowsBlock + kRowsBlock) : p.S;
+    constexpr int kChunks = HD / 8;   // 16-byte pieces per key row
+    for (int k0 = 0; k0 < k_end; k0 += kRowsKeys) {
+        __syncthreads();   // the previous tile is no longer read
+        for (int idx = threadIdx.x; idx < kRowsKeys * kChunks; idx += kRowsBlock) {
+            const int j = idx / kChunks;
+            const int d = (idx - j * kChunks) * 8;
+            uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = make_uint4(0u, 0u, 0u, 0u);
+            if (k0 + j < k_end) {
+                kv = *reinterpret_cast<const uint4*>(p.k + b * p.ks[0] + h * p.ks[1] +
+                                                     static_cast<int64_t>(k0 + j) * p.ks[2] + d);
+                vv = *reinterpret_cast<const uint4*>(p.v + b * p.vs[0] + h * p.vs[1] +
+                                                     static_cast<int64_t>(k0 + j) * p.vs[2] + d);
+            }
+            const __half2* k2 = reinterpret_cast<const __half2*>(&kv);
+            const __half2* v2 = reinterpret_cast<const __half2*>(&vv);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 kf = __half22float2(k2[i]);
+                const float2 vf = __half22float2(v2[i]);
+                k_s[j][d + 2 * i] = kf.x;
+                k_s[j][d + 2 * i + 1] = kf.y;
+                v_s[j][d + 2 * i] = vf.x;
+                v_s[j][d + 2 * i + 1] = vf.y;
+            }
+        }
+        if (threadIdx.x < kRowsKeys) {
+            const int kj = k0 + threadIdx.x;
+            bool ok = kj < k_end;
+            if (ok && p.mask_kind == 1) ok = p.mask[b * p.ms0 + static_cast<int64_t>(kj) * p.ms3] != 0;
+            key_ok[threadIdx.x] = ok ? 1 : 0;
+        }
+        __syncthreads();
+        float s[kRowsKeys];
+        float mt = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < kRowsKeys; ++j) {
+            const int kj = k0 + j;
+            bool allowed = q_ok && key_ok[j] && (!p.causal || kj <= qi);
+            if (allowed && p.mask_kind == 2)
+                allowed = p.mask[b * p.ms0 + h * p.ms1 + static_cast<int64_t>(qi) * p.ms2 +
+                                 static_cast<int64_t>(kj) * p.ms3] != 0;
+            float acc = 0.0f;
+#pragma unroll
+            for (int d = 0; d < HD; d += 4) {
+                const float4 kk = *reinterpret_cast<const float4*>(&k_s[j][d]);
+                acc = fmaf(q[d], kk.x, acc);
+                acc = fmaf(q[d + 1], kk.y, acc);
+                acc = fmaf(q[d + 2], kk.z, acc);
+                acc = fmaf(q[d + 3], kk.w, acc);
+            }
+            s[j] = allowed ? acc * c : -INFINITY;
+            mt = fmaxf(mt, s[j]);
+        }
+        if (mt == -INFINITY) continue;   // nothing allowed in this tile for this row
+        const float m_new = fmaxf(m, mt);
+        const float corr = fast_exp2(m - m_new);   // 0 while nothing was accumulated
+        l *= corr;
+#pragma unroll
+        for (int d = 0; d < HD; ++d) o[d] *= corr;
+        m = m_new;
+#pragma unroll
+        for (int j = 0; j < kRowsKeys; ++j) {
+            const float pj = fast_exp2(s[j] - m_new);   // -inf -> 0
+            l += pj;
+            const float ph = __half2float(__float2half_rn(pj));
+#pragma unroll
+            for (int d = 0; d < HD; d += 4) {
+                const float4 vv = *reinterpret_cast<const float4*>(&v_s[j][d]);
+                o[d] = fmaf(ph, vv.x, o[d]);
+                o[d + 1] = fmaf(ph, vv.y, o[d + 1]);
+                o[d + 2] = fmaf(ph, vv.z, o[d + 2]);
+                o[d + 3] = fmaf(ph, vv.w, o[d + 3]);
+            }
+        }
+    }
+    if (!q_ok) return;
+    const float inv = l > 0.0f ? 1.0f / l : 0.0f;   // no allowed key: the row is 0
+    const int64_t base = p.out_layout == 1 ? ((static_cast<int64_t>(b) * p.S + qi) * p.H + h) * HD
+                                           : ((static_cast<int64_t>(b) * p.H + h) * p.S + qi) * HD;
+#pragma unroll
+    for (int d = 0; d < HD; d += 8) {
+        uint4 hi, lo;
+        uint32_t* hw = reinterpret_cast<uint32_t*>(&hi);
+        uint32_t* lw = reinterpret_cast<uint32_t*>(&lo);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) split_half2(o[d + 2 * i] * inv, o[d + 2 * i + 1] * inv, hw[i], lw[i]);
+        *reinterpret_cast<uint4*>(p.out + base + d) = hi;
+        if (p.out_lo != 0) *reinterpret_cast<uint4*>(p.out + p.out_lo + base + d) = lo;
     }
 }
 

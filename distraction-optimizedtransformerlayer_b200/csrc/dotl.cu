@@ -826,13 +826,23 @@ int attention_run(const void* q, const void* k, const void* v, int B, int H, int
         g.out = static_cast<__half*>(out);
         g.out_layout = out_layout;
         g.out_lo = out_lo;
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        cudaError_t e;
+        if (head_dim <= 24) {
+            // a thread per query row
+            const dim3 rgrid(static_cast<unsigned>((S + dotl::kRowsBlock - 1) / dotl::kRowsBlock),
+                             static_cast<unsigned>(B * H));
+            const dim3 rblock(dotl::kRowsBlock);
+            if (head_dim == 8) e = launch_pdl(dotl::attn_rows_kernel<8>, rgrid, rblock, 0, s, g);
+            else if (head_dim == 16) e = launch_pdl(dotl::attn_rows_kernel<16>, rgrid, rblock, 0, s, g);
+            else e = launch_pdl(dotl::attn_rows_kernel<24>, rgrid, rblock, 0, s, g);
+            if (e != cudaSuccess) return fail(DOTL_ECUDA, "%s: launch failed: %s", who, cudaGetErrorString(e));
+            return check_launch(who);
+        }
         const dim3 grid(static_cast<unsigned>((S + dotl::kGenRows - 1) / dotl::kGenRows),
                         static_cast<unsigned>(B * H));
         const dim3 block(dotl::kGenRows * 32);
-        cudaStream_t s = static_cast<cudaStream_t>(stream);
-        cudaError_t e;
-        if (head_dim <= 32) e = launch_pdl(dotl::attn_generic_kernel<1>, grid, block, 0, s, g);
-        else if (head_dim <= 64) e = launch_pdl(dotl::attn_generic_kernel<2>, grid, block, 0, s, g);
+        if (head_dim <= 64) e = launch_pdl(dotl::attn_generic_kernel<2>, grid, block, 0, s, g);
         else if (head_dim <= 128) e = launch_pdl(dotl::attn_generic_kernel<4>, grid, block, 0, s, g);
         else e = launch_pdl(dotl::attn_generic_kernel<8>, grid, block, 0, s, g);
         if (e != cudaSuccess) return fail(DOTL_ECUDA, "%s: launch failed: %s", who, cudaGetErrorString(e));

@@ -42,6 +42,9 @@ CASES = [
     ("hd 8 caus+pad", 3, 4, 70, 8, True, True),
     ("hd 16 causal", 2, 3, 100, 16, True, False),
     ("hd 24", 1, 2, 33, 24, False, False),
+    ("hd 16 long causal", 2, 2, 300, 16, True, False),
+    ("hd 24 caus+pad", 2, 3, 257, 24, True, True),
+    ("hd 8 padded", 3, 2, 200, 8, False, True),
     ("hd 48 padded", 2, 2, 90, 48, False, True),
     ("hd 256 caus+pad", 2, 2, 130, 256, True, True),
 ]
@@ -120,7 +123,7 @@ def test_attention_cases(kernels, case):
         assert (a.float() - p.float()).abs().max().item() <= 1e-3
 
 
-@pytest.mark.parametrize("d", [64, 8, 256])
+@pytest.mark.parametrize("d", [64, 8, 16, 24, 256])
 def test_key_mask_with_causal_unfolded(kernels, d):
     """A [B,1,1,S] key mask plus is_causal (the model's call), not folded."""
     b, h, s = 3, 4, 256
@@ -133,8 +136,9 @@ def test_key_mask_with_causal_unfolded(kernels, d):
     assert (out.double() - ref).abs().max().item() <= TOL
 
 
-def test_fully_masked_rows_are_zero(kernels):
-    b, h, s, d = 2, 2, 64, 64
+@pytest.mark.parametrize("d", [64, 8])
+def test_fully_masked_rows_are_zero(kernels, d):
+    b, h, s = 2, 2, 64
     q, k, v, _, _ = build_case(b, h, s, d, False, False, seed=5)
     mask = torch.zeros(b, 1, 1, s, dtype=torch.bool, device="cuda")
     mask[0, ..., :10] = True
