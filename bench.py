@@ -637,12 +637,19 @@ def _measure(cid, args, kernels, dist, dev, rank, world, steps, cpu_budget_s):
     e2e_ms = e_start.elapsed_time(e_end)
     h2d = x_cpu.numel() * 4 + (mask_cpu.numel() if mask_cpu is not None else 0)
     d2h = x_cpu.numel() * 4
-    total_ms, e2e_ms = max_over_ranks([total_ms, e2e_ms], dist, dev)
+    link_in_ms, link_out_ms = _pcie_duplex_ms(x_host, out_hosts[0], dev)
+    total_ms, e2e_ms, link_in_ms, link_out_ms = max_over_ranks([total_ms, e2e_ms, link_in_ms, link_out_ms], dist, dev)
+    link_ms = max(link_in_ms, link_out_ms)
 
     res = {"config": cid, "tokens_per_rank": tokens_per_rank, "job_tokens": job_tokens,
            "ms_per_step": total_ms / steps, "value": job_tokens * steps / (total_ms / 1e3),
            "e2e": {"value": job_tokens * steps / (e2e_ms / 1e3), "unit": "tokens/s",
-                   "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                   "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                   # the copies alone, both directions at once: the e2e ceiling
+                   "pcie": {"h2d_gbs": x_host.numel() * 4 / link_in_ms / 1e6,
+                            "d2h_gbs": d2h / link_out_ms / 1e6, "concurrent": True,
+                            "bound_value": job_tokens / (link_ms / 1e3),
+                            "frac": (link_ms * steps) / e2e_ms}},
            "clocks": clocks, "batch_per_gpu": hi - lo, "strong": strong,
            "cuda_graph": len(model._graphs) > 0,
            "l2": "inputs " + ("larger" if x.numel() * 4 > 126 * 2 ** 20 else "smaller") + " than L2"}
@@ -677,9 +684,36 @@ def _measure(cid, args, kernels, dist, dev, rank, world, steps, cpu_budget_s):
     return res
 
 
+def _pcie_duplex_ms(x_host, out_host, dev, reps=5):
+    """Best-of-reps times (ms) of one host->device copy of x_host and one
+    device->host copy into out_host (both pinned, the e2e step's buffers),
+    issued together on two streams as the e2e pipeline overlaps them: the
+    link's ceiling for the e2e number."""
+    d_in = torch.empty(x_host.shape, dtype=x_host.dtype, device=dev)
+    d_out = torch.zeros(out_host.shape, dtype=out_host.dtype, device=dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    best_in = best_out = float("inf")
+    for _ in range(reps):
+        torch.cuda.synchronize(dev)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        with torch.cuda.stream(s_in):
+            ev[0].record(s_in)
+            d_in.copy_(x_host, non_blocking=True)
+            ev[1].record(s_in)
+        with torch.cuda.stream(s_out):
+            ev[2].record(s_out)
+            out_host.copy_(d_out, non_blocking=True)
+            ev[3].record(s_out)
+        torch.cuda.synchronize(dev)
+        best_in = min(best_in, ev[0].elapsed_time(ev[1]))
+        best_out = min(best_out, ev[2].elapsed_time(ev[3]))
+    return best_in, best_out
+
+
 def _per_config_entry(r):
     e = {"value": r["value"], "unit": "tokens/s", "ms_per_step": r["ms_per_step"],
-         "batch_per_gpu": r["batch_per_gpu"], "e2e": r["e2e"]["value"], "cuda_graph": r["cuda_graph"],
+         "batch_per_gpu": r["batch_per_gpu"], "e2e": r["e2e"]["value"],
+         "e2e_pcie_frac": round(r["e2e"]["pcie"]["frac"], 3), "cuda_graph": r["cuda_graph"],
          "sm_mhz": r["clocks"].get("sm_mhz"), "throttle": r["clocks"].get("reasons")}
     if "roofline" in r:
         rf = r["roofline"]
