@@ -116,8 +116,10 @@ struct AttnSmem {
     static constexpr int kBarQFull = 0, kBarQEmpty = 2;                  // [2] each
     static constexpr int kBarKFull = 4, kBarKEmpty = kBarKFull + STAGES; // [STAGES] each
     static constexpr int kBarVFull = kBarKEmpty + STAGES, kBarVEmpty = kBarVFull + STAGES;
-    static constexpr int kBarSFull = kBarVEmpty + STAGES, kBarPFull = kBarSFull + kNS;   // [NS] each
-    static constexpr int kBarODone = kBarPFull + kNS, kBarOFree = kBarODone + 2;         // [2] each
+    // S ready per (softmax group, buffer): a buffer's uses alternate between
+    // the groups, and each group must wait on its own uses' phases in order
+    static constexpr int kBarSFull = kBarVEmpty + STAGES, kBarPFull = kBarSFull + 2 * kNS;   // [2][NS], [NS]
+    static constexpr int kBarODone = kBarPFull + kNS, kBarOFree = kBarODone + 2;             // [2] each
     static constexpr int kBarCombFull = kBarOFree + 2, kBarCombEmpty = kBarCombFull + 1;
     static constexpr int kBarInfoFull = kBarCombEmpty + 1, kBarInfoEmpty = kBarInfoFull + 2;
     static constexpr int kBarDrain = kBarInfoEmpty + 2;
@@ -198,6 +200,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                    const __grid_constant__ CUtensorMap tmap_v, const AttnParams p) {
     using L = AttnSmem<HD, STAGES>;
+    // Every barrier has one consumer (a thread, or one softmax group) that
+    // steps through its phases in order and never falls two behind: an
+    // mbarrier parity wait cannot tell phase k from phase k + 2.
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -210,7 +215,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     auto k_empty = [&](int s) { return bar(L::kBarKEmpty + s); };
     auto v_full = [&](int s) { return bar(L::kBarVFull + s); };
     auto v_empty = [&](int s) { return bar(L::kBarVEmpty + s); };
-    auto s_full = [&](int i) { return bar(L::kBarSFull + i); };
+    auto s_full = [&](int g, int i) { return bar(L::kBarSFull + g * L::kNS + i); };
     auto p_full = [&](int i) { return bar(L::kBarPFull + i); };
     auto o_done = [&](int g) { return bar(L::kBarODone + g); };
     auto o_free = [&](int g) { return bar(L::kBarOFree + g); };
@@ -235,7 +240,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             mbar_init(v_empty(s), 1);
         }
         for (int i = 0; i < L::kNS; ++i) {
-            mbar_init(s_full(i), 1);
+            mbar_init(s_full(0, i), 1);
+            mbar_init(s_full(1, i), 1);
             mbar_init(p_full(i), 128);
         }
         for (int g = 0; g < 2; ++g) {
@@ -401,7 +407,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                                    smem_desc(ka + off, 16, 8 * L::kRowBytes, L::kSwz), idesc_s,
                                    kk != 0 ? 1u : 0u);
                     }
-                    tc_commit(s_full(sb));
+                    tc_commit(s_full((g0 + j) & 1, sb));
                     tc_commit(k_empty(st));
                     if (j == n_kt - 1) tc_commit(q_empty(qs));   // this Q slot is no longer read
                     return true;
@@ -451,6 +457,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t t_o = t_o0 + static_cast<uint32_t>(grp * HD);
         const float c = p.scale_log2;
         uint32_t gtiles = 0, icount = 0, ccount = 0, singles = 0, tbase = 0;
+        uint32_t s_par = 0;   // bit b = phase parity of this group's next S in buffer b
         bool alive = true;
         for (int item = blockIdx.x; item < num_items && alive; item += gridDim.x, ++icount) {
             const int slot = static_cast<int>(icount & 1u);
@@ -601,7 +608,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 const uint32_t t = t_item + static_cast<uint32_t>(j);
                 const int sb = static_cast<int>(t % L::kNS);
                 const uint32_t t_s = t_s0 + static_cast<uint32_t>(sb * kAttnTile);
-                ok = mbar_wait(s_full(sb), (t / L::kNS) & 1u, abort_flag);
+                ok = mbar_wait(s_full(grp, sb), (s_par >> sb) & 1u, abort_flag);
+                s_par ^= 1u << sb;
                 if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
                 tc_fence_after();
                 float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};

@@ -136,6 +136,26 @@ def test_key_mask_with_causal_unfolded(kernels, d):
     assert (out.double() - ref).abs().max().item() <= TOL
 
 
+@pytest.mark.parametrize("d", [128, 64, 32])
+def test_mixed_short_and_long_key_ranges(kernels, d):
+    """Batch rows of 100 and of 512 valid keys, many work items per CTA: one-
+    key-tile items (handled by one softmax group) interleave with four-tile
+    items (both groups), so an S/P buffer's uses alternate between the groups
+    in every pattern, and each group must still wait on its own S tiles'
+    phases, not a phase of the other group's."""
+    b, h, s = 96, 4, 512
+    q, k, v, _, _ = build_case(b, h, s, d, False, False, seed=8)
+    lengths = torch.tensor([100 if i % 2 == 0 else 512 for i in range(b)], device="cuda")
+    lengths[5::7] = 129   # two key tiles, one of them nearly empty
+    valid = torch.arange(s, device="cuda")[None, :] < lengths[:, None]
+    mask = valid[:, None, None, :]
+    out = kernels.fused_attention_forward(q, k, v, mask, False, d ** -0.5, 0, 0, 0)
+    again = kernels.fused_attention_forward(q, k, v, mask, False, d ** -0.5, 0, 0, 0)
+    assert torch.equal(out, again)
+    ref = reference_attention_f64(q, k, v, mask, False, d ** -0.5)
+    assert (out.double() - ref).abs().max().item() <= TOL
+
+
 @pytest.mark.parametrize("d", [64, 8])
 def test_fully_masked_rows_are_zero(kernels, d):
     b, h, s = 2, 2, 64
