@@ -544,6 +544,17 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
             bn = 128;
             split2 = true;
         }
+        // Large fp32 residual-stream GEMMs (out_proj, ffn_out of a wide layer)
+        // on CTA pairs: measured on B200 (interleaved medians, L2 flushed) at
+        // M=16384 N=2048: K=8192 450 -> 405 us, K=2048 124 -> 116 us, same
+        // bits; fp16-output GEMMs and shapes with fewer than four pair tiles
+        // per CTA pair gained nothing or lost (up to 16 %).
+        const bool resid_out = out_dtype == DOTL_F32 && resid_mode != DOTL_RESID_NONE && resid_mode != DOTL_MASK_ROWS;
+        const int64_t pair_tiles = ((M + 2 * dotl::kGemmBM - 1) / (2 * dotl::kGemmBM)) * (N / 256);
+        if (bn == 256 && resid_out && N >= 2048 && N % 256 == 0 && K >= 2048 &&
+            pair_tiles >= 4 * static_cast<int64_t>(sm_count(dev) / 2)) {
+            pair = true;
+        }
     } else if (bn == -128) {
         if (nkb < 2) return fail(DOTL_EINVAL, "%s: split-K needs at least two k-blocks (K > 64)", who);
         bn = 128;
