@@ -40,7 +40,8 @@ def test_traffic_table_parses_the_committed_summary():
     import bench
 
     table = bench._traffic_table()
-    assert table[(3, "attention")] == 107_401_984 + 24_509_184
+    assert table[(3, "attention")] == 104_517_376 + 24_575_488
+    assert table[(5, "gemm_ffn_in_gelu")] == 102_283_264 + 241_223_680
     assert all(v > 0 for v in table.values())
 
 
