@@ -113,7 +113,10 @@ int dotl_layernorm(const float* x, const float* sub, const float* weight, const 
  * (TMA), N % 8 == 0. tile_n: 0 = auto, else 64, 128 or 256, or -128 for two
  * CTAs per 128-wide tile that split K and add their partial sums (auto picks it
  * for long K when the tiles cannot fill the SMs; the add is one fp32 sum, so
- * results are the same on every run).
+ * results are the same on every run), or -256 for 256 x 256 tiles on CTA pairs
+ * (cta_group::2 MMAs with M = 256; the same bits as tile_n 256; auto picks it
+ * for fp32 residual outputs with N >= 2048, K >= 2048 and at least four pair
+ * tiles per pair of SMs).
  */
 int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N,
                 int64_t ldw, const float* bias, int act, const float* resid, int64_t ldr,
