@@ -122,7 +122,10 @@ struct AttnSmem {
     static constexpr int kBarODone = kBarPFull + kNS, kBarOFree = kBarODone + 2;             // [2] each
     static constexpr int kBarCombFull = kBarOFree + 2, kBarCombEmpty = kBarCombFull + 1;
     static constexpr int kBarInfoFull = kBarCombEmpty + 1, kBarInfoEmpty = kBarInfoFull + 2;
-    static constexpr int kBarDrain = kBarInfoEmpty + 2;
+    // O final per group: committed after the group's last PV of an item, so
+    // it completes only when every PV of the group in that item has
+    static constexpr int kBarOFinal = kBarInfoEmpty + 2;                                     // [2]
+    static constexpr int kBarDrain = kBarOFinal + 2;
     static constexpr uint32_t kNumBars = kBarDrain + 1;
     static constexpr uint32_t kOffSlot = kOffBar + kNumBars * 8;
     static constexpr uint32_t kOffAbort = kOffSlot + 4;
@@ -218,6 +221,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     auto s_full = [&](int g, int i) { return bar(L::kBarSFull + g * L::kNS + i); };
     auto p_full = [&](int i) { return bar(L::kBarPFull + i); };
     auto o_done = [&](int g) { return bar(L::kBarODone + g); };
+    auto o_final = [&](int g) { return bar(L::kBarOFinal + g); };
     auto o_free = [&](int g) { return bar(L::kBarOFree + g); };
     const uint32_t comb_full = bar(L::kBarCombFull);
     const uint32_t comb_empty = bar(L::kBarCombEmpty);
@@ -248,6 +252,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             mbar_init(q_full(g), 1);
             mbar_init(q_empty(g), 1);
             mbar_init(o_done(g), 1);
+            mbar_init(o_final(g), 1);
             mbar_init(o_free(g), 128);
             mbar_init(info_full(g), 1);
             mbar_init(info_empty(g), 1 + 8);
@@ -434,6 +439,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                                    idesc_o, (j >= 2 || kk != 0) ? 1u : 0u);
                     tc_commit(o_done(g));
                     tc_commit(v_empty(st));
+                    if (j + 2 >= n_kt) tc_commit(o_final(g));   // the group's last PV of this item
                     if (j + L::kNS < n_kt && !issue_s(j + L::kNS)) { ok = false; break; }
                 }
                 if (!ok) break;
@@ -456,7 +462,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t t_o0 = tmem_base + lane_off + L::kColO;
         const uint32_t t_o = t_o0 + static_cast<uint32_t>(grp * HD);
         const float c = p.scale_log2;
-        uint32_t gtiles = 0, icount = 0, ccount = 0, singles = 0, tbase = 0;
+        uint32_t gtiles = 0, icount = 0, ccount = 0, singles = 0, tbase = 0, fcount = 0;
         uint32_t s_par = 0;   // bit b = phase parity of this group's next S in buffer b
         bool alive = true;
         for (int item = blockIdx.x; item < num_items && alive; item += gridDim.x, ++icount) {
@@ -718,8 +724,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 mbar_arrive(p_full(sb));
             }
             if (!alive) break;
-            // the last PV of this group has landed in O
-            ok = mbar_wait(o_done(grp), (gtiles - 1) & 1u, abort_flag);
+            // every PV of this group in this item has landed in O. A per-item
+            // barrier: the phase of the last PV on o_done would alias an
+            // earlier one if the group's previous PV were still in flight.
+            ok = mbar_wait(o_final(grp), fcount & 1u, abort_flag);
+            ++fcount;
             if (!__all_sync(0xffffffffu, ok)) { alive = false; break; }
             tc_fence_after();
             if (two && grp == 1) {
