@@ -225,6 +225,8 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
     } else if (warp == 1 && lane == 0) {
         // ------------------------------------------------------------ MMA --
         constexpr uint32_t idesc = idesc_f16_f32(kGemmBM, 128, false, false);
+        constexpr uint32_t idesc_n256 = idesc_f16_f32(kGemmBM, 256, false, false);
+        static_assert(kRh != 2 || (kS % 2 == 0 && L::kKb % 2 == 0), "W2 half pairs must not wrap the ring");
         int stage = 0;
         uint32_t phase = 0;
         uint32_t c1 = 0, c2 = 0, it = 0;
@@ -276,15 +278,36 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
                         // hidden columns [64 h, 64 h + 64) of the chunk: packed fp16
                         // pairs in TMEM columns [b 128 + 64 h, + 32), 8 per K=16 step
                         const uint32_t h_tmem = tmem_base + static_cast<uint32_t>(b * kFfnChunk + h * 64);
-                        for (int r = 0; r < kRh; ++r) {
+                        if constexpr (kRh == 2) {
+                            // The two 128-row halves of this W2 k-block sit in
+                            // consecutive ring stages (every block of the walk takes
+                            // an even number of stages, and the ring's count is even,
+                            // so a pair never wraps): one N=256 MMA per K step reads
+                            // both, half the MMA instructions of two N=128 ones.
+                            const int s0 = stage;
                             if (!take()) return false;
-                            const uint32_t w_addr = sbase + L::kOffW + stage * kFfnTileBytes;
-                            const uint32_t d_tmem = tmem_base + L::kColAcc2 + static_cast<uint32_t>(r * 128);
+                            if (!mbar_wait(bars.w_full(s0 + 1), phase, abort_flag)) return false;
+                            tc_fence_after();
+                            const uint32_t w_addr = sbase + L::kOffW + s0 * kFfnTileBytes;
+                            const uint32_t d_tmem = tmem_base + L::kColAcc2;
 #pragma unroll
                             for (int kk = 0; kk < kGemmBK / 16; ++kk)
                                 mma_f16_ts(d_tmem, h_tmem + kk * 8, smem_desc(w_addr + kk * 32, 16, 1024, kSwizzle128),
-                                           idesc, (j != 0 || h != 0 || kk != 0) ? 1u : 0u);
+                                           idesc_n256, (j != 0 || h != 0 || kk != 0) ? 1u : 0u);
                             give();
+                            give();
+                        } else {
+                            for (int r = 0; r < kRh; ++r) {
+                                if (!take()) return false;
+                                const uint32_t w_addr = sbase + L::kOffW + stage * kFfnTileBytes;
+                                const uint32_t d_tmem = tmem_base + L::kColAcc2 + static_cast<uint32_t>(r * 128);
+#pragma unroll
+                                for (int kk = 0; kk < kGemmBK / 16; ++kk)
+                                    mma_f16_ts(d_tmem, h_tmem + kk * 8,
+                                               smem_desc(w_addr + kk * 32, 16, 1024, kSwizzle128), idesc,
+                                               (j != 0 || h != 0 || kk != 0) ? 1u : 0u);
+                                give();
+                            }
                         }
                     }
                     tc_commit(bars.g2_done(b));
