@@ -560,8 +560,9 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
         bn = 128;
         split2 = true;
     }
-    if (bn != 64 && bn != 128 && bn != 256)
-        return fail(DOTL_EINVAL, "%s: tile_n must be 0, 64, 128, 256, -128 (split K) or -256 (CTA pairs)", who);
+    if (bn != 64 && bn != 128 && bn != 160 && bn != 192 && bn != 224 && bn != 256)
+        return fail(DOTL_EINVAL,
+                    "%s: tile_n must be 0, 64, 128, 160, 192, 224, 256, -128 (split K) or -256 (CTA pairs)", who);
 
     // DOTL_F16X2 operands: one map over both planes of each (lo rows below hi)
     CUtensorMap ta, tw;
@@ -615,6 +616,15 @@ int dotl_linear(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
     if (bn == 256)
         return f16 ? launch_gemm<256, 4, true>(ta, tw, to, tr, p, dev, s, po)
                    : launch_gemm<256, 4, false>(ta, tw, to, tr, p, dev, s, po);
+    if (bn == 224)
+        return f16 ? launch_gemm<224, 4, true>(ta, tw, to, tr, p, dev, s, po)
+                   : launch_gemm<224, 4, false>(ta, tw, to, tr, p, dev, s, po);
+    if (bn == 192)
+        return f16 ? launch_gemm<192, 4, true>(ta, tw, to, tr, p, dev, s, po)
+                   : launch_gemm<192, 4, false>(ta, tw, to, tr, p, dev, s, po);
+    if (bn == 160)
+        return f16 ? launch_gemm<160, 5, true>(ta, tw, to, tr, p, dev, s, po)
+                   : launch_gemm<160, 5, false>(ta, tw, to, tr, p, dev, s, po);
     if (bn == 64)
         return f16 ? launch_gemm<64, 7, true>(ta, tw, to, tr, p, dev, s, po)
                    : launch_gemm<64, 7, false>(ta, tw, to, tr, p, dev, s, po);

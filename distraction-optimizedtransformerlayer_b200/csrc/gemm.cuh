@@ -108,7 +108,13 @@ struct GemmSmem {
     static constexpr uint32_t kOffAbort = kOffSlot + 4;
     static constexpr uint32_t kBytes = kOffAbort + 4;
     static constexpr uint32_t kAlloc = kBytes + 1024;   // room to align the base to 1024
-    static constexpr uint32_t kTmemCols = 2 * BN;
+    // Two accumulators of BN fp32 columns, the second at column kAccStride.
+    // tcgen05.alloc takes a power of two, so widths between the powers (160,
+    // 192, 224) allocate 512 columns and put the second accumulator at 256.
+    static constexpr uint32_t kTmemCols = 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
+    static constexpr uint32_t kAccStride = kTmemCols / 2;
+    static_assert(kAlloc <= 232448, "dynamic shared memory over the 227 KB an sm_100a CTA may use");
+    static_assert(BN % 32 == 0 && BN <= 256, "the epilogue walks 32-column chunks of at most 256 columns");
 };
 
 // Which output tiles a CTA visits: t = first, first + stride, ... < count.
@@ -198,7 +204,7 @@ __device__ __forceinline__ void gemm_mma(uint32_t sbase, uint32_t tmem_base, Gem
         if (!mbar_wait(bars.acce(acc), acc_phase ^ 1u, abort_flag)) goto mma_done;
         tc_fence_after();
         {
-            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc) * L::kAccStride;
             for (int kb = kb0; kb < kb1; ++kb) {
                 if (!mbar_wait(bars.full(stage), phase, abort_flag)) goto mma_done;
                 tc_fence_after();
@@ -293,7 +299,7 @@ __device__ __forceinline__ void gemm_mma_pair(uint32_t sbase, uint32_t tmem_base
         if (!mbar_wait_cluster(bars.acce(acc), acc_phase ^ 1u, abort_flag)) goto pair_mma_done;
         tc_fence_after();
         {
-            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc) * L::kAccStride;
             for (int kb = 0; kb < nkb; ++kb) {
                 if (!mbar_wait(bars.full(stage), phase, abort_flag)) goto pair_mma_done;
                 tc_fence_after();
@@ -505,7 +511,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (!ok) break;
             tc_fence_after();
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                                   static_cast<uint32_t>(acc * BN);
+                                   static_cast<uint32_t>(acc) * L::kAccStride;
             // Split-K exchange buffer: [128 rows][BN/2 fp32] in the stage ring,
             // 16-byte granule g of row r at g ^ (r & mask) (conflict-free).
             constexpr int kHalfGranules = BN / 8;

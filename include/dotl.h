@@ -110,7 +110,9 @@ int dotl_layernorm(const float* x, const float* sub, const float* weight, const 
  *   operands: DOTL_F16 (a, w fp16), or DOTL_F16X2 (a is an fp16 pair of 2 * M
  *             rows of lda and w one of 2 * N rows of ldw; the three-product mode)
  * Requirements: K % 8 == 0, lda % 8 == 0, ldw % 8 == 0, a/w 16-byte aligned
- * (TMA), N % 8 == 0. tile_n: 0 = auto, else 64, 128 or 256, or -128 for two
+ * (TMA), N % 8 == 0. tile_n: 0 = auto, else 64, 128, 160, 192, 224 or 256
+ * (the widths between the powers of two fill a last wave of tiles that 128 or
+ * 256 would leave partly idle; every width gives the same bits), or -128 for two
  * CTAs per 128-wide tile that split K and add their partial sums (auto picks it
  * for long K when the tiles cannot fill the SMs; the add is one fp32 sum, so
  * results are the same on every run), or -256 for 256 x 256 tiles on CTA pairs

@@ -197,3 +197,55 @@ def test_cta_pair_tiles(kernels, M, N, K, mode, act, half_out):
     tol = 2 ** -10 if half_out else 1e-5
     assert ((out.double() - y).abs() / (scale if not half_out else y.abs() + 1e-2)).max().item() < tol
     assert ((out.double() - one.double()).abs() / scale).max().item() < 1e-5
+
+
+@pytest.mark.parametrize("tile", [160, 192, 224])
+@pytest.mark.parametrize("M,N,K,mode,act,half_out", [
+    (300, 512, 256, 0, 0, False), (257, 1000, 128, 1, 0, False), (2048, 2048, 512, 3, 0, False),
+    (129, 456, 72, 2, 0, False), (1000, 768, 1024, 0, 1, True), (64, 8, 64, 0, 0, True)])
+def test_intermediate_tile_widths(kernels, tile, M, N, K, mode, act, half_out):
+    """tile_n 160/192/224 (two accumulators in a 512-column TMEM allocation,
+    the second at column 256; last N tile partial on most shapes): every
+    epilogue against float64, and the same bits as width 256, since each
+    output element's k loop is the same whatever the tile's width."""
+    a, w, b = _operands(M, N, K, 60 + M + tile)
+    g = torch.Generator(device="cuda").manual_seed(61)
+    resid = torch.randn(M, N, device="cuda", generator=g) if mode else None
+    valid = (torch.rand(M, device="cuda", generator=g) > 0.3) if mode >= 2 else None
+    out = kernels.linear_fp16(a, w, b, act=act, resid=resid, row_valid=valid, resid_mode=mode,
+                              out_half=half_out, tile_n=tile)
+    wide = kernels.linear_fp16(a, w, b, act=act, resid=resid, row_valid=valid, resid_mode=mode,
+                               out_half=half_out, tile_n=256)
+    y = _ref(a, w, b, act=bool(act))
+    if mode == 1:
+        y = resid.double() + y
+    elif mode == 2:
+        y = resid.double() + torch.where(valid[:, None], y, torch.zeros_like(y))
+    elif mode == 3:
+        y = torch.where(valid[:, None], resid.double() + y, torch.zeros_like(y))
+    scale = _scale(a, w) + (resid.double().abs() if resid is not None else 0)
+    tol = 2 ** -10 if half_out else 1e-5
+    assert ((out.double() - y).abs() / (scale if not half_out else y.abs() + 1e-2)).max().item() < tol
+    assert torch.equal(out, wide)
+
+
+@pytest.mark.parametrize("tile", [160, 224])
+def test_intermediate_tile_widths_pair_operands(kernels, tile):
+    """The three-product mode at a width that leaves the last N tile partial:
+    its W rows past N come from the lo plane (the map covers both planes) into
+    columns that are never stored."""
+    g = torch.Generator(device="cuda").manual_seed(62)
+    M, N, K = 300, 456, 192
+    a = torch.randn(M, K, device="cuda", generator=g)
+    w = torch.randn(N, K, device="cuda", generator=g) * K ** -0.5
+    b = torch.randn(N, device="cuda", generator=g) * 0.1
+
+    def pair(t):
+        hi = t.half()
+        return torch.stack([hi, (t - hi.float()).half()]).contiguous()
+
+    out = kernels.linear_fp16(pair(a), pair(w), b, pair_operands=True, tile_n=tile)
+    wide = kernels.linear_fp16(pair(a), pair(w), b, pair_operands=True, tile_n=256)
+    assert torch.equal(out, wide)
+    y = a.double() @ w.double().t() + b.double()
+    assert ((out.double() - y).abs() / (a.double().abs() @ w.double().abs().t())).max().item() < 4e-6
