@@ -101,7 +101,15 @@ def _check(rc: int) -> None:
 
 
 def _stream(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    # The raw handle of torch's current stream on that device (the one a
+    # torch.cuda.stream() context or a graph capture has made current),
+    # without building a torch.cuda.Stream object on every kernel call.
+    if device.type != "cuda":
+        raise ValueError(f"libdotl kernels take CUDA tensors, got a tensor on {device}")
+    index = device.index
+    if index is None:
+        index = torch.cuda.current_device()
+    return torch._C._cuda_getCurrentRawStream(index)
 
 
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
