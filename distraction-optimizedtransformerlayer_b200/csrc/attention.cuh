@@ -76,6 +76,8 @@ struct AttnParams {
     int head_inner;      // bit t (q=0,k=1,v=2): tensor map dims are {hd, H, rows, B}
     int64_t out_lo;      // 0, or the element offset from `out` of a plane receiving
                          // fp16(o - fp16(o)) (the fp16 pair of the three-product GEMM mode)
+    int single;          // every item has at most one key tile (sequences of at
+                         // most 128 keys, or packed ones that divide 128)
     int splits;          // key runs per query tile (1: no split-KV)
     int kt_per_split;    // key tiles per run
     float* ws_o;         // split-KV: [slot][128][HD] unnormalised fp32 O
@@ -383,7 +385,72 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             constexpr int kStepsPerBlk = L::kBlkCols / 16;
             uint32_t tcount = 0, qcount = 0, icount = 0, singles = 0;
             uint32_t pcount[2] = {0, 0};
-            for (int item = blockIdx.x; item < num_items; item += gridDim.x, ++icount) {
+            if (p.single) {
+                // Items of one key tile each, which the softmax groups take in
+                // turn: S of item i+1 is issued before PV of item i, so both
+                // groups run their softmax at once. S(t+1) refills the buffer
+                // of item t+1-NS, whose PV this thread issued before S(t).
+                bool ok = true, pend = false;
+                int pend_g = 0;
+                uint32_t pend_t = 0;
+                auto issue_pv = [&](int g, uint32_t t) -> bool {
+                    const int st = static_cast<int>(t % STAGES);
+                    const int sb = static_cast<int>(t % L::kNS);
+                    // the group's previous item has read its O accumulator
+                    if (!mbar_wait(o_free(g), (pcount[g] & 1u) ^ 1u, abort_flag)) return false;
+                    if (!mbar_wait(p_full(sb), (t / L::kNS) & 1u, abort_flag)) return false;
+                    if (!mbar_wait(v_full(st), (t / STAGES) & 1u, abort_flag)) return false;
+                    tc_fence_after();
+                    const uint32_t d = tmem_base + L::kColO + static_cast<uint32_t>(g * HD);
+                    const uint32_t pa = tmem_base + L::kColS + static_cast<uint32_t>(sb * kAttnTile);
+                    const uint32_t va = sbase + L::kOffV + st * L::kTileBytes;
+#pragma unroll
+                    for (int kk = 0; kk < kAttnTile / 16; ++kk)
+                        mma_f16_ts(d, pa + kk * 8,
+                                   smem_desc(va + kk * 16 * L::kRowBytes, L::kBlkBytes, 8 * L::kRowBytes, L::kSwz),
+                                   idesc_o, kk != 0 ? 1u : 0u);
+                    tc_commit(o_done(g));
+                    tc_commit(v_empty(st));
+                    tc_commit(o_final(g));
+                    ++pcount[g];
+                    return true;
+                };
+                for (int item = blockIdx.x; item < num_items; item += gridDim.x, ++icount) {
+                    const int slot = static_cast<int>(icount & 1u);
+                    if (!mbar_wait(info_full(slot), (icount >> 1) & 1u, abort_flag)) { ok = false; break; }
+                    const int n_kt = info[2 * slot];
+                    mbar_arrive(info_empty(slot));
+                    if (n_kt == 0) continue;
+                    const int g0 = first_group(n_kt, singles);
+                    const int qs = static_cast<int>(qcount & 1u);
+                    if (!mbar_wait(q_full(qs), (qcount >> 1) & 1u, abort_flag)) { ok = false; break; }
+                    const uint32_t t = tcount;
+                    const int st = static_cast<int>(t % STAGES);
+                    const int sb = static_cast<int>(t % L::kNS);
+                    if (!mbar_wait(k_full(st), (t / STAGES) & 1u, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t d = tmem_base + L::kColS + static_cast<uint32_t>(sb * kAttnTile);
+                    const uint32_t qa = sbase + L::kOffQ + qs * L::kTileBytes;
+                    const uint32_t ka = sbase + L::kOffK + st * L::kTileBytes;
+#pragma unroll
+                    for (int kk = 0; kk < HD / 16; ++kk) {
+                        const uint32_t off = (kk / kStepsPerBlk) * L::kBlkBytes + (kk % kStepsPerBlk) * 32;
+                        mma_f16_ss(d, smem_desc(qa + off, 16, 8 * L::kRowBytes, L::kSwz),
+                                   smem_desc(ka + off, 16, 8 * L::kRowBytes, L::kSwz), idesc_s, kk != 0 ? 1u : 0u);
+                    }
+                    tc_commit(s_full(g0, sb));
+                    tc_commit(k_empty(st));
+                    tc_commit(q_empty(qs));
+                    if (pend && !issue_pv(pend_g, pend_t)) { ok = false; break; }
+                    pend = true;
+                    pend_g = g0;
+                    pend_t = t;
+                    ++tcount;
+                    ++qcount;
+                }
+                if (ok && pend) issue_pv(pend_g, pend_t);
+            }
+            for (int item = blockIdx.x; !p.single && item < num_items; item += gridDim.x, ++icount) {
                 const int slot = static_cast<int>(icount & 1u);
                 if (!mbar_wait(info_full(slot), (icount >> 1) & 1u, abort_flag)) break;
                 const int n_kt = info[2 * slot];

@@ -958,6 +958,9 @@ int attention_run(const void* q, const void* k, const void* v, int B, int H, int
                                                     dotl::kAttnTile * head_dim * 4);
         }
     }
+    // One key tile per item: a query tile's keys are its own sequence's (at
+    // most 128 of them), or, packed, those of the sequences that fill it.
+    p.single = p.splits == 1 && (packed ? dotl::kAttnTile % S == 0 : S <= dotl::kAttnTile) ? 1 : 0;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     switch (head_dim) {
         case 32: return launch_attn<32, 4>(maps[0], maps[1], maps[2], p, dev, s);
