@@ -17,8 +17,9 @@
 //   warp 1      tcgen05.mma, for F/128 hidden chunks j, buffer b = j & 1:
 //                 G1(j): acc1[b] = a W1[j]^T             (TMEM, 128 fp32 columns)
 //                 G2(j): acc2   += H[b] W2[:, j]^T       (A operand read from TMEM)
-//               issued G1(0), G1(1), G2(0), G1(2), G2(1), ...; G1(j+2) waits
-//               for G2(j) to complete, since H(j) lives in acc1[b];
+//               issued G1(0), G1(1), G2(0), G1(2), G2(1), ...; G1(j+2)
+//               overwrites acc1[b], where H(j) lives, with no wait: G2(j) was
+//               issued before it, and tcgen05 MMAs run in issue order;
 //   warps 2-9   per chunk: acc1 -> + b1 -> GELU -> fp16, written back into the
 //               columns of acc1[b] it was read from (two fp16 per column), so
 //               H never touches shared memory; per block: acc2 -> + b2 +
@@ -72,9 +73,9 @@ struct FfnSmem {
     static constexpr uint32_t kStageWarpBytes = 4096 + 2048;
     static constexpr uint32_t kOffStage = kOffStats + 2 * 2 * kGemmBM * 8;
     static constexpr uint32_t kOffBar = kOffStage + 8 * kStageWarpBytes;
-    // a_full, a_empty, w_full[S], w_empty[S], acc1_full[2], h_full[2], g2_done[2],
+    // a_full, a_empty, w_full[S], w_empty[S], acc1_full[2], h_full[2],
     // acc2_full, acc2_empty, stats[2 parity][4 quarters], drain, resid_full[8 warps]
-    static constexpr int kNumBars = 2 + 2 * kStages + 6 + 2 + 8 + 1 + 8;
+    static constexpr int kNumBars = 2 + 2 * kStages + 4 + 2 + 8 + 1 + 8;
     static constexpr uint32_t kOffSlot = kOffBar + kNumBars * 8;
     static constexpr uint32_t kOffAbort = kOffSlot + 4;
     static constexpr uint32_t kBytes = kOffAbort + 4;
@@ -93,14 +94,13 @@ struct FfnBars {
     __device__ __forceinline__ uint32_t w_empty(int s) const { return bar0 + 8u * (2 + L::kStages + s); }
     __device__ __forceinline__ uint32_t acc1_full(int b) const { return bar0 + 8u * (2 + 2 * L::kStages + b); }
     __device__ __forceinline__ uint32_t h_full(int b) const { return bar0 + 8u * (4 + 2 * L::kStages + b); }
-    __device__ __forceinline__ uint32_t g2_done(int b) const { return bar0 + 8u * (6 + 2 * L::kStages + b); }
-    __device__ __forceinline__ uint32_t acc2_full() const { return bar0 + 8u * (8 + 2 * L::kStages); }
-    __device__ __forceinline__ uint32_t acc2_empty() const { return bar0 + 8u * (9 + 2 * L::kStages); }
+    __device__ __forceinline__ uint32_t acc2_full() const { return bar0 + 8u * (6 + 2 * L::kStages); }
+    __device__ __forceinline__ uint32_t acc2_empty() const { return bar0 + 8u * (7 + 2 * L::kStages); }
     __device__ __forceinline__ uint32_t stats(int par, int q) const {
-        return bar0 + 8u * (10 + 2 * L::kStages + par * 4 + q);
+        return bar0 + 8u * (8 + 2 * L::kStages + par * 4 + q);
     }
-    __device__ __forceinline__ uint32_t drain() const { return bar0 + 8u * (18 + 2 * L::kStages); }
-    __device__ __forceinline__ uint32_t resid_full(int w) const { return bar0 + 8u * (19 + 2 * L::kStages + w); }
+    __device__ __forceinline__ uint32_t drain() const { return bar0 + 8u * (16 + 2 * L::kStages); }
+    __device__ __forceinline__ uint32_t resid_full(int w) const { return bar0 + 8u * (17 + 2 * L::kStages + w); }
 };
 
 // The W ring in consumption order: per 128-row block, G1(0), G1(1) [W1 chunk
@@ -148,7 +148,6 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
         for (int b = 0; b < 2; ++b) {
             mbar_init(bars.acc1_full(b), 1);
             mbar_init(bars.h_full(b), 256);
-            mbar_init(bars.g2_done(b), 1);
         }
         mbar_init(bars.acc2_full(), 1);
         mbar_init(bars.acc2_empty(), 256);
@@ -249,9 +248,10 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
                 n_chunks,
                 [&](int j) {
                     const int b = static_cast<int>(c1 & 1u);
-                    // H of the chunk that last used acc1[b] has been consumed by its G2
-                    if (!mbar_wait(bars.g2_done(b), ((c1 >> 1) & 1u) ^ 1u, abort_flag)) return false;
-                    tc_fence_after();
+                    // acc1[b] last held H of chunk j-2, which its G2 reads from
+                    // TMEM. That G2 was issued before this G1 from this thread,
+                    // and tcgen05 MMAs run in issue order, so no wait: the
+                    // tensor pipe stays fed while G2(j-2) executes.
                     const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * kFfnChunk);
                     for (int kb = 0; kb < L::kKb; ++kb) {
                         if (!take()) return false;
@@ -310,7 +310,6 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
                             }
                         }
                     }
-                    tc_commit(bars.g2_done(b));
                     ++c2;
                     if (j == n_chunks - 1) tc_commit(bars.acc2_full());
                     return true;
