@@ -76,8 +76,6 @@ struct AttnParams {
     int head_inner;      // bit t (q=0,k=1,v=2): tensor map dims are {hd, H, rows, B}
     int64_t out_lo;      // 0, or the element offset from `out` of a plane receiving
                          // fp16(o - fp16(o)) (the fp16 pair of the three-product GEMM mode)
-    int single;          // every item has at most one key tile (sequences of at
-                         // most 128 keys, or packed ones that divide 128)
     int splits;          // key runs per query tile (1: no split-KV)
     int kt_per_split;    // key tiles per run
     float* ws_o;         // split-KV: [slot][128][HD] unnormalised fp32 O
@@ -200,7 +198,9 @@ __device__ __forceinline__ void attn_scan_keys(const AttnParams& p, int b, int l
     hole = __reduce_min_sync(0xffffffffu, first_zero);
 }
 
-template <int HD, int STAGES>
+// SINGLE: every item has one key tile and CTAs take several items (the host
+// decides); the MMA thread then overlaps consecutive items (see below).
+template <int HD, int STAGES, bool SINGLE>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                    const __grid_constant__ CUtensorMap tmap_v, const AttnParams p) {
@@ -385,7 +385,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             constexpr int kStepsPerBlk = L::kBlkCols / 16;
             uint32_t tcount = 0, qcount = 0, icount = 0, singles = 0;
             uint32_t pcount[2] = {0, 0};
-            if (p.single) {
+            if constexpr (SINGLE) {
                 // Items of one key tile each, which the softmax groups take in
                 // turn: S of item i+1 is issued before PV of item i, so both
                 // groups run their softmax at once. S(t+1) refills the buffer
@@ -450,7 +450,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 }
                 if (ok && pend) issue_pv(pend_g, pend_t);
             }
-            for (int item = blockIdx.x; !p.single && item < num_items; item += gridDim.x, ++icount) {
+            for (int item = blockIdx.x; !SINGLE && item < num_items; item += gridDim.x, ++icount) {
                 const int slot = static_cast<int>(icount & 1u);
                 if (!mbar_wait(info_full(slot), (icount >> 1) & 1u, abort_flag)) break;
                 const int n_kt = info[2 * slot];

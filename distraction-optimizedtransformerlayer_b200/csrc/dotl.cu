@@ -306,17 +306,22 @@ int pick_tile_n_ln(int64_t M, int64_t N, int sms) {
 
 // ------------------------------------------------------------- attention --
 
+// single: every item has one key tile (the host's test in dotl_attention).
 template <int HD, int STAGES>
 int launch_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const dotl::AttnParams& p,
-                int dev, cudaStream_t stream) {
+                bool single, int dev, cudaStream_t stream) {
     using L = dotl::AttnSmem<HD, STAGES>;
-    auto kernel = dotl::attn_tc_kernel<HD, STAGES>;
-    static DeviceFlags done;
-    static DeviceFlags regs_ok;
-    if (int rc = ensure_smem(kernel, L::kAlloc, dev, done)) return rc;
-    if (int rc = check_regs(kernel, dotl::kAttnThreads, dotl::kAttnRegSplit, regs_ok, dev, "dotl_attention")) return rc;
     const int items = p.num_streams * p.num_q_tiles * p.splits;
     const int grid = items < sm_count(dev) ? items : sm_count(dev);
+    // The overlapped order only pays when a CTA has a next item; with one
+    // item per CTA the plain kernel (smaller code) runs.
+    const bool overlap = single && items > grid;
+    auto kernel = overlap ? dotl::attn_tc_kernel<HD, STAGES, true> : dotl::attn_tc_kernel<HD, STAGES, false>;
+    static DeviceFlags done[2];
+    static DeviceFlags regs_ok[2];
+    if (int rc = ensure_smem(kernel, L::kAlloc, dev, done[overlap])) return rc;
+    if (int rc = check_regs(kernel, dotl::kAttnThreads, dotl::kAttnRegSplit, regs_ok[overlap], dev, "dotl_attention"))
+        return rc;
     cudaError_t e = launch_pdl(kernel, dim3(grid), dim3(dotl::kAttnThreads), L::kAlloc, stream, tq, tk, tv, p);
     if (e != cudaSuccess) return fail(DOTL_ECUDA, "dotl_attention: launch failed: %s", cudaGetErrorString(e));
     if (p.splits > 1) {
@@ -960,12 +965,12 @@ int attention_run(const void* q, const void* k, const void* v, int B, int H, int
     }
     // One key tile per item: a query tile's keys are its own sequence's (at
     // most 128 of them), or, packed, those of the sequences that fill it.
-    p.single = p.splits == 1 && (packed ? dotl::kAttnTile % S == 0 : S <= dotl::kAttnTile) ? 1 : 0;
+    const bool single = p.splits == 1 && (packed ? dotl::kAttnTile % S == 0 : S <= dotl::kAttnTile);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     switch (head_dim) {
-        case 32: return launch_attn<32, 4>(maps[0], maps[1], maps[2], p, dev, s);
-        case 64: return launch_attn<64, 3>(maps[0], maps[1], maps[2], p, dev, s);
-        default: return launch_attn<128, 2>(maps[0], maps[1], maps[2], p, dev, s);
+        case 32: return launch_attn<32, 4>(maps[0], maps[1], maps[2], p, single, dev, s);
+        case 64: return launch_attn<64, 3>(maps[0], maps[1], maps[2], p, single, dev, s);
+        default: return launch_attn<128, 2>(maps[0], maps[1], maps[2], p, single, dev, s);
     }
 }
 
