@@ -858,22 +858,28 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 if (two) tmem_ld_32x32b_x16(t_o0 + HD + cc, o1);
                 tmem_ld_wait16(o0);
                 if (two) tmem_ld_wait16(o1);
-                uint32_t w[8], wl[8];
+                float v[16];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const float v0 = two ? fmaf(__uint_as_float(o0[2 * i]), a0, __uint_as_float(o1[2 * i]) * a1)
-                                         : __uint_as_float(o0[2 * i]) * a0;
-                    const float v1 = two ? fmaf(__uint_as_float(o0[2 * i + 1]), a0, __uint_as_float(o1[2 * i + 1]) * a1)
-                                         : __uint_as_float(o0[2 * i + 1]) * a0;
-                    split_half2(v0, v1, w[i], wl[i]);
+                for (int i = 0; i < 16; ++i)
+                    v[i] = two ? fmaf(__uint_as_float(o0[i]), a0, __uint_as_float(o1[i]) * a1)
+                               : __uint_as_float(o0[i]) * a0;
+                uint32_t w[8];
+                if (p.out_lo != 0) {
+                    // the fp16 pair's lo plane too (three-product mode)
+                    uint32_t wl[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) split_half2(v[2 * i], v[2 * i + 1], w[i], wl[i]);
+                    if (q_ok) {
+                        *reinterpret_cast<uint4*>(op + p.out_lo + cc) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
+                        *reinterpret_cast<uint4*>(op + p.out_lo + cc + 8) = make_uint4(wl[4], wl[5], wl[6], wl[7]);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) w[i] = pack_half2(v[2 * i], v[2 * i + 1]);
                 }
                 if (q_ok) {
                     *reinterpret_cast<uint4*>(op + cc) = make_uint4(w[0], w[1], w[2], w[3]);
                     *reinterpret_cast<uint4*>(op + cc + 8) = make_uint4(w[4], w[5], w[6], w[7]);
-                    if (p.out_lo != 0) {
-                        *reinterpret_cast<uint4*>(op + p.out_lo + cc) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
-                        *reinterpret_cast<uint4*>(op + p.out_lo + cc + 8) = make_uint4(wl[4], wl[5], wl[6], wl[7]);
-                    }
                 }
             }
             tc_fence_before();

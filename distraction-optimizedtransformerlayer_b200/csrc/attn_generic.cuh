@@ -255,10 +255,15 @@ __global__ void __launch_bounds__(kRowsBlock) attn_rows_kernel(const AttnGeneric
         uint4 hi, lo;
         uint32_t* hw = reinterpret_cast<uint32_t*>(&hi);
         uint32_t* lw = reinterpret_cast<uint32_t*>(&lo);
+        if (p.out_lo != 0) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) split_half2(o[d + 2 * i] * inv, o[d + 2 * i + 1] * inv, hw[i], lw[i]);
+            for (int i = 0; i < 4; ++i) split_half2(o[d + 2 * i] * inv, o[d + 2 * i + 1] * inv, hw[i], lw[i]);
+            *reinterpret_cast<uint4*>(p.out + p.out_lo + base + d) = lo;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) hw[i] = pack_half2(o[d + 2 * i] * inv, o[d + 2 * i + 1] * inv);
+        }
         *reinterpret_cast<uint4*>(p.out + base + d) = hi;
-        if (p.out_lo != 0) *reinterpret_cast<uint4*>(p.out + p.out_lo + base + d) = lo;
     }
 }
 

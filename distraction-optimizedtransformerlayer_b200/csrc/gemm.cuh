@@ -636,16 +636,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     __syncwarp();
                     uint8_t* srow = stage_ptr + sb + lane * kRowB;
                     if constexpr (OUT_F16) {
-                        // 64 B rows, 64B swizzle: granule q of row r at q ^ ((r >> 1) & 3)
+                        // 64 B rows, 64B swizzle: granule q of row r at q ^ ((r >> 1) & 3).
+                        // The lo half is computed only when its plane is stored
+                        // (a warp-uniform branch outside the loop).
+                        if (lo_out) {
 #pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            uint4 w, l;
-                            split_half2(v[8 * q], v[8 * q + 1], w.x, l.x);
-                            split_half2(v[8 * q + 2], v[8 * q + 3], w.y, l.y);
-                            split_half2(v[8 * q + 4], v[8 * q + 5], w.z, l.z);
-                            split_half2(v[8 * q + 6], v[8 * q + 7], w.w, l.w);
-                            *reinterpret_cast<uint4*>(srow + ((q ^ ((lane >> 1) & 3)) << 4)) = w;
-                            if (lo_out) *reinterpret_cast<uint4*>(srow + 2048 + ((q ^ ((lane >> 1) & 3)) << 4)) = l;
+                            for (int q = 0; q < 4; ++q) {
+                                uint4 w, l;
+                                split_half2(v[8 * q], v[8 * q + 1], w.x, l.x);
+                                split_half2(v[8 * q + 2], v[8 * q + 3], w.y, l.y);
+                                split_half2(v[8 * q + 4], v[8 * q + 5], w.z, l.z);
+                                split_half2(v[8 * q + 6], v[8 * q + 7], w.w, l.w);
+                                *reinterpret_cast<uint4*>(srow + ((q ^ ((lane >> 1) & 3)) << 4)) = w;
+                                *reinterpret_cast<uint4*>(srow + 2048 + ((q ^ ((lane >> 1) & 3)) << 4)) = l;
+                            }
+                        } else {
+#pragma unroll
+                            for (int q = 0; q < 4; ++q)
+                                *reinterpret_cast<uint4*>(srow + ((q ^ ((lane >> 1) & 3)) << 4)) =
+                                    make_uint4(pack_half2(v[8 * q], v[8 * q + 1]), pack_half2(v[8 * q + 2], v[8 * q + 3]),
+                                               pack_half2(v[8 * q + 4], v[8 * q + 5]),
+                                               pack_half2(v[8 * q + 6], v[8 * q + 7]));
                         }
                     } else {
                         // 128 B rows, 128B swizzle: granule q of row r at q ^ (r & 7)

@@ -353,15 +353,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 if constexpr (NORM_F16) {
                     // the lo half of the fp16 pair (three-product mode) goes
                     // to the second half of the 4 KB buffer
+                    if (p.norm_lo) {
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        uint4 w, l;
-                        split_half2(v[8 * q], v[8 * q + 1], w.x, l.x);
-                        split_half2(v[8 * q + 2], v[8 * q + 3], w.y, l.y);
-                        split_half2(v[8 * q + 4], v[8 * q + 5], w.z, l.z);
-                        split_half2(v[8 * q + 6], v[8 * q + 7], w.w, l.w);
-                        *reinterpret_cast<uint4*>(srow + ((q ^ ((lane >> 1) & 3)) << 4)) = w;
-                        if (p.norm_lo) *reinterpret_cast<uint4*>(srow + 2048 + ((q ^ ((lane >> 1) & 3)) << 4)) = l;
+                        for (int q = 0; q < 4; ++q) {
+                            uint4 w, l;
+                            split_half2(v[8 * q], v[8 * q + 1], w.x, l.x);
+                            split_half2(v[8 * q + 2], v[8 * q + 3], w.y, l.y);
+                            split_half2(v[8 * q + 4], v[8 * q + 5], w.z, l.z);
+                            split_half2(v[8 * q + 6], v[8 * q + 7], w.w, l.w);
+                            *reinterpret_cast<uint4*>(srow + ((q ^ ((lane >> 1) & 3)) << 4)) = w;
+                            *reinterpret_cast<uint4*>(srow + 2048 + ((q ^ ((lane >> 1) & 3)) << 4)) = l;
+                        }
+                    } else {
+#pragma unroll
+                        for (int q = 0; q < 4; ++q)
+                            *reinterpret_cast<uint4*>(srow + ((q ^ ((lane >> 1) & 3)) << 4)) =
+                                make_uint4(pack_half2(v[8 * q], v[8 * q + 1]), pack_half2(v[8 * q + 2], v[8 * q + 3]),
+                                           pack_half2(v[8 * q + 4], v[8 * q + 5]), pack_half2(v[8 * q + 6], v[8 * q + 7]));
                     }
                 } else {
 #pragma unroll

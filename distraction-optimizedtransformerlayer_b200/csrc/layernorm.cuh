@@ -134,13 +134,15 @@ __global__ void __launch_bounds__(kLnWarpsPerBlock * 32)
                 if constexpr (sizeof(NormT) == 4) {
                     *reinterpret_cast<float4*>(reinterpret_cast<float*>(normed) + base + c) =
                         make_float4(o0, o1, o2, o3);
-                } else {
+                } else if (lo_plane != 0) {
                     uint2 h, l;
                     split_half2(o0, o1, h.x, l.x);
                     split_half2(o2, o3, h.y, l.y);
                     *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(normed) + base + c) = h;
-                    if (lo_plane != 0)
-                        *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(normed) + lo_plane + base + c) = l;
+                    *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(normed) + lo_plane + base + c) = l;
+                } else {
+                    *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(normed) + base + c) =
+                        make_uint2(pack_half2(o0, o1), pack_half2(o2, o3));
                 }
             }
         }
