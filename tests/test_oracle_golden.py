@@ -95,7 +95,7 @@ def test_generate_random_case_lengths():
     assert torch.all(x[~mask] == 0)
 
 
-def test_baseline_configs_match_survey():
+def test_baseline_config_shapes():
     shapes = {k: (c.batch_size, c.seq_len, c.d_model, c.num_heads, c.ffn_dim, c.causal, p)
               for k, (c, p) in O.BASELINE_CONFIGS.items()}
     assert shapes == {
