@@ -389,7 +389,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 // Items of one key tile each, which the softmax groups take in
                 // turn: S of item i+1 is issued before PV of item i, so both
                 // groups run their softmax at once. S(t+1) refills the buffer
-                // of item t+1-NS, whose PV this thread issued before S(t).
+                // of item t+1-NS, whose PV this thread issued earlier (in the
+                // previous iteration at the latest), and MMAs run in issue order.
                 bool ok = true, pend = false;
                 int pend_g = 0;
                 uint32_t pend_t = 0;
