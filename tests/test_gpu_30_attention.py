@@ -221,3 +221,37 @@ def test_split_kv_matches_one_pass(kernels, case):
     assert torch.equal(pair[0], split)
     if lengths is not None and 0 in lengths:
         assert torch.all(split[lengths.index(0)] == 0)
+
+
+@pytest.mark.parametrize("S,d,causal,padded", [(32, 64, False, False), (32, 64, True, True), (64, 32, False, True),
+                                                (16, 128, True, False), (128, 64, False, True)])
+def test_single_tile_items_overlapped(kernels, S, d, causal, padded):
+    """Every work item one key tile (packed sequences that divide 128, or
+    sequences of 128) and more items than SMs, so CTAs take several: the MMA
+    thread then issues the next item's S before this item's P.V and both
+    softmax groups work at once. Checked against float64, and bit for bit
+    against the same sequences run 128 items at a time (one item per CTA,
+    the kernel without the overlap)."""
+    H = 4
+    B = 1024 * 32 // S if S < 128 else 64          # 1024 or 256 items
+    g = torch.Generator(device="cuda").manual_seed(S + d)
+    qkv = torch.randn(B, S, 3, H, d, device="cuda", generator=g).half()
+    q, k, v = (qkv[:, :, i].permute(0, 2, 1, 3) for i in range(3))
+    mask = None
+    if padded:
+        lengths = torch.randint(1, S + 1, (B,), device="cuda", generator=g)
+        mask = torch.arange(S, device="cuda")[None, :] < lengths[:, None]
+    scale = d ** -0.5
+    out = kernels.attention_packed(q, k, v, causal, scale, key_mask=mask)
+    # each chunk: 128 items (128 // H batch rows of one tile row block each)
+    per = 128 * 128 // (S * H) if S < 128 else 128 // H
+    for lo in range(0, B, per):
+        hi = min(lo + per, B)
+        part = kernels.attention_packed(q[lo:hi], k[lo:hi], v[lo:hi], causal, scale,
+                                        key_mask=mask[lo:hi] if mask is not None else None)
+        assert torch.equal(part, out[lo:hi]), f"batch rows {lo}:{hi} differ from the whole batch"
+    n = min(B, 64)
+    am = mask[:n, None, None, :] if mask is not None else None
+    ref = reference_attention_f64(q[:n].float(), k[:n].float(), v[:n].float(), am, causal, scale)
+    ref = ref.transpose(1, 2).reshape(n, S, H * d)
+    assert (out[:n].double() - ref).abs().max().item() <= TOL
