@@ -238,7 +238,7 @@ def run_reference(args, rank, world):
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": med * 1e3,
-        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "weak" if args.weak else "strong", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic", "impl": "reference",
         "config": _config_dict(args.config, world, cfg.num_layers),
         "reference_run": {"device": "cpu", "step": "one fp32 CPU forward of the sample below, timed on the host",
@@ -759,7 +759,9 @@ def run_ours(args, rank, world, local_rank):
         line = {
             "metric": METRIC, "value": head["value"], "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
-            "higher_is_better": True, "scaling": "strong" if head["strong"] else "weak",
+            # the run's mode (the config's batch split over the ranks unless
+            # --weak), the same label at every N of a scaling sweep
+            "higher_is_better": True, "scaling": "weak" if args.weak else "strong",
             "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
             "config": _config_dict(args.config, world, args.layers),
             "impl_notes": {"cuda_graph": head["cuda_graph"], "l2": head["l2"],
